@@ -1,0 +1,100 @@
+/* b2_linear.h -- extended entry points of the B200 Linear path.
+ *
+ * The reference caps M, N, K at 4096 (research/custom-ops/include/custom_ops.h:20,145-146) and
+ * only offers host-array and device-cube entries. The B200 build keeps those limits on the
+ * co_* API (custom_ops.h) and adds, here:
+ *   - explicit device selection and caller-supplied CUDA streams (one handle per GPU);
+ *   - operators up to B2_MAX_DIM in M, N and K (the SmolLM LM head N=49152, K=16384 cases);
+ *   - full-K FP32 accumulation as an alternative to the reference's per-256-K FP16 narrowing;
+ *   - asynchronous row-major device-pointer entries (inputs already resident in HBM);
+ *   - raw FP32 partial accumulators and a separate bias/activation epilogue, used for K-split
+ *     across GPUs (partials reduced with NCCL between the two calls);
+ *   - a host-side fault-injection seam for failure-path tests.
+ * An operator created here is the same object type as a co_linear and accepts every co_* run
+ * entry whose shape limits it meets.
+ */
+#ifndef B2_LINEAR_H
+#define B2_LINEAR_H
+#include "custom_ops.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2_MAX_DIM (1u << 20)
+
+typedef struct co_linear_hsig b2_linear;
+
+/* Accumulation of the K reduction. */
+enum b2_accumulate {
+    B2_ACC_TILE16 = 0,  /* reference: FP32 per 256-wide K tile, running sum narrowed to FP16 */
+    B2_ACC_FP32 = 1,    /* FP32 over the whole K, FP32 bias/activation, one FP16 rounding */
+};
+
+/* Device status bits (accumulated per handle by asynchronous entries). */
+#define B2_STATUS_TIMEOUT           0x1u   /* a bounded device wait expired; kernel bailed out */
+#define B2_STATUS_NONFINITE_OUTPUT  0x2u
+#define B2_STATUS_NONFINITE_INPUT   0x4u
+#define B2_STATUS_GUARD             0x8u   /* a buffer's slack or guard bytes were overwritten */
+
+/* ----------------------------------------------------------------------- devices and streams */
+int b2_device_count(void);
+/* Opens CUDA device `ordinal` with a new non-blocking stream; returns a handle (fd) >= 0. */
+int b2_open_device(int ordinal);
+/* Streams work submitted through `fd` onto `stream` (a cudaStream_t); NULL restores the
+ * handle's own stream. The caller keeps ownership of the stream. */
+int b2_set_stream(int fd, void *stream);
+void *b2_get_stream(int fd);
+int b2_sync(int fd);
+/* Returns the accumulated B2_STATUS_* bits of asynchronous calls on `fd`; clears them if asked. */
+unsigned b2_status(int fd, int clear);
+/* Number of streaming multiprocessors of the handle's device (0 on error). */
+int b2_sm_count(int fd);
+/* Pinned host memory (for end-to-end transfers at full PCIe rate). */
+void *b2_host_alloc(size_t bytes);
+void b2_host_free(void *p);
+
+/* ----------------------------------------------------------------------- extended operator */
+/* Like co_linear_create without the 4096 caps: 1 <= m,k,n <= B2_MAX_DIM. `m` sizes the host
+ * staging used by co_linear_run; device entries take their own row count. */
+int b2_linear_create(int fd, unsigned m, unsigned k, unsigned n,
+                     const _Float16 *weights, const _Float16 *optional_bias,
+                     enum co_linear_post post, enum co_mode mode,
+                     enum b2_accumulate acc, b2_linear **out);
+int b2_linear_set_accumulate(b2_linear *, enum b2_accumulate);
+/* X: device row-major [m, ldx] FP16, Y: device row-major [m, ldy] FP16, both 16-byte aligned,
+ * ldx and ldy multiples of 8 elements. Asynchronous on the handle's stream: returns after the
+ * launches; errors raised by the device appear in b2_status(). */
+int b2_linear_run_device(b2_linear *, unsigned m, const void *x, size_t ldx, void *y, size_t ldy);
+/* Raw accumulator only: P[m, ldp] FP32 = X * W^T (no bias, no activation, FP32 accumulation). */
+int b2_linear_partial_device(b2_linear *, unsigned m, const void *x, size_t ldx,
+                             float *partial, size_t ldp);
+/* Y[m, ldy] FP16 = act(P + b) using this operator's bias and post-op (FP32 arithmetic). */
+int b2_linear_epilogue_device(b2_linear *, unsigned m, const float *partial, size_t ldp,
+                              void *y, size_t ldy);
+
+typedef struct {
+    unsigned m, k, n;
+    unsigned kernel;             /* 0 = tcgen05 GEMM, 1 = GEMV (small M) */
+    unsigned tile_m, tile_n, tile_k, stages;
+    unsigned grid;               /* CTAs of the main kernel for the create-time m */
+    unsigned launches_per_run;   /* CUDA launches of one co_linear_run */
+    enum b2_accumulate acc;
+    size_t device_bytes;         /* HBM held by the operator */
+} b2_linear_info;
+int b2_linear_get_info(const b2_linear *, b2_linear_info *);
+
+/* ----------------------------------------------------------------------- fault injection */
+enum b2_fault {
+    B2_FAULT_NONE = 0,
+    B2_FAULT_ALLOC = 1,      /* the nth device allocation from now fails (ROCKET_E_NOMEM) */
+    B2_FAULT_LAUNCH = 2,     /* the nth kernel launch from now is refused (ROCKET_E_DEVICE) */
+    B2_FAULT_NAN_OUTPUT = 3, /* the nth op run from now reports a non-finite output */
+};
+/* Host-side seam only: nothing is done to the GPU. nth >= 1; kind NONE disarms. */
+void b2_fault_inject(enum b2_fault kind, unsigned nth);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

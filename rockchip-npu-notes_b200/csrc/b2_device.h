@@ -1,0 +1,111 @@
+/* b2_device.h -- internal seam between the host C layer and the CUDA layer.
+ *
+ * Host code (the C files under csrc/host) reaches the GPU only through these functions; the
+ * CUDA files under csrc/cuda implement them with the CUDA runtime and hand-written sm_100a kernels. The host C tests link
+ * a CPU stand-in of this seam instead (tests/c/mock_device.c), the way the reference's host tests
+ * wrap its BO and submit calls (research/custom-ops/tests/c/multitile_host_test.c:14-58): that
+ * stand-in exists only in test binaries; the shipped library has no CPU compute path.
+ *
+ * Only plain C types cross this boundary. FP16 data is opaque (uint16_t bits).
+ */
+#ifndef B2_DEVICE_H
+#define B2_DEVICE_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct b2_dev b2_dev;
+
+/* Status bits returned by b2d_status (the same values as B2_STATUS_* in b2_linear.h). */
+enum {
+    B2D_ST_TIMEOUT = 1u,
+    B2D_ST_NONFINITE_OUTPUT = 2u,
+    B2D_ST_NONFINITE_INPUT = 4u,
+    B2D_ST_GUARD = 8u,
+};
+
+/* Largest M served by the weight-streaming small-M kernel; larger M uses the tcgen05 GEMM. */
+#define B2D_GEMV_MAX_M 8u
+
+int b2d_device_count(void);
+int b2d_open(int ordinal, b2_dev **out);
+void b2d_close(b2_dev *);
+int b2d_set_stream(b2_dev *, void *stream);
+void *b2d_stream(b2_dev *);
+int b2d_sm_count(b2_dev *);
+
+/* Zero-filled device allocation; returns ROCKET_E_NOMEM on failure. */
+int b2d_malloc(b2_dev *, size_t bytes, void **out);
+void b2d_free(b2_dev *, void *ptr);
+void *b2d_host_alloc(size_t bytes);
+void b2d_host_free(void *ptr);
+
+enum { B2D_H2D = 0, B2D_D2H = 1, B2D_D2D = 2 };
+/* Pitched copy of `rows` rows of `width` bytes, asynchronous on the handle's stream. */
+int b2d_copy_2d(b2_dev *, void *dst, size_t dpitch, const void *src, size_t spitch,
+                size_t width, size_t rows, int kind);
+int b2d_memset(b2_dev *, void *ptr, int value, size_t bytes);
+/* Waits for the handle's stream; ROCKET_E_DEVICE if CUDA reported an error. */
+int b2d_sync(b2_dev *);
+/* Device status word (B2_STATUS_* bits) written by kernels; read after b2d_sync. */
+uint32_t b2d_status(b2_dev *, int clear);
+/* ORs `bits` into the status word (restores bits a synchronous entry read out early). */
+void b2d_status_merge(b2_dev *, uint32_t bits);
+
+/* ---------------------------------------------------------------------- Linear launches */
+typedef struct {
+    unsigned m, n, k;
+    const void *x; size_t ldx;      /* FP16 [m, ldx], 16-byte aligned, ldx % 8 == 0 */
+    const void *w; size_t ldw;      /* FP16 [n, ldw], 16-byte aligned, ldw % 8 == 0 */
+    const void *bias;               /* FP16 [n] or NULL */
+    void *y; size_t ldy;            /* FP16 [m, ldy] */
+    float *partial; size_t ldp;     /* FP32 [m, ldp]: raw-accumulator destination / workspace */
+    int post;                       /* 0 none, 1 HardSigmoid */
+    int acc;                        /* 0 per-256-K FP16 fold (reference), 1 FP32 */
+    int fused;                      /* 1: epilogue in the GEMM; 0: raw to `partial`, then epilogue */
+    int raw_only;                   /* 1: stop after writing the raw accumulator to `partial` */
+} b2k_linear;
+
+typedef struct {
+    unsigned kernel;                /* 0 tcgen05 GEMM, 1 GEMV */
+    unsigned tile_m, tile_n, tile_k, stages, grid;
+} b2k_config;
+
+/* Picks the kernel for the shape and launches it (plus the separate epilogue when !fused).
+ * *launches receives the number of kernels launched. */
+int b2d_linear(b2_dev *, const b2k_linear *, unsigned *launches);
+int b2d_linear_config(b2_dev *, const b2k_linear *, b2k_config *);
+/* y = act(partial + bias) with the same arithmetic as the fused epilogue of mode `acc`. */
+int b2d_epilogue(b2_dev *, unsigned m, unsigned n, const float *partial, size_t ldp,
+                 const void *bias, int post, int acc, void *y, size_t ldy);
+
+/* Sets status `bit` if any of rows x cols FP16 elements (row pitch ld elements) is not finite. */
+int b2d_scan_nonfinite(b2_dev *, const void *p, size_t rows, size_t cols, size_t ld, uint32_t bit);
+
+/* One C2=8 FP16 cube tile placed at (row0, col0) of a row-major matrix. */
+typedef struct {
+    void *ptr;                      /* device address of the cube view */
+    unsigned rows, cols;            /* logical extent */
+    unsigned physical_rows, physical_cols;
+    unsigned row0, col0;            /* position in the row-major matrix */
+} b2k_cube_tile;
+#define B2K_MAX_CUBE_TILES 64
+/* Gather cube tiles into row-major dst [*, ld] (logical elements and their atoms). */
+int b2d_cube_to_rowmajor(b2_dev *, const b2k_cube_tile *tiles, unsigned count, void *dst, size_t ld);
+/* Scatter row-major src into cube tiles: logical elements, padding zeroed (within each view). */
+int b2d_rowmajor_to_cube(b2_dev *, const void *src, size_t ld, const b2k_cube_tile *tiles,
+                         unsigned count);
+
+/* Guard regions: [payload, payload+slack) must be zero, [payload+slack, +guard) 0xA5. */
+int b2d_guard_init(b2_dev *, void *base, size_t payload, size_t slack, size_t guard);
+/* Checks up to B2K_MAX_CUBE_TILES buffers; sets B2_STATUS_GUARD on any mismatch. */
+int b2d_guard_check(b2_dev *, void *const *bases, const size_t *payloads, unsigned count,
+                    size_t slack, size_t guard);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,56 @@
+// common.cuh -- device helpers shared by the sm_100a kernels of the Linear path.
+//
+// Epilogue arithmetic (one definition, used by the fused GEMM/GEMV epilogues and by the separate
+// epilogue kernel, so CO_CHAIN and CO_SEPARATE runs give identical bytes):
+//   per-256-K fold   run = fp16(chunk) for the first K tile, run = fp16(run + chunk) afterwards
+//                    (research/custom-ops/src/linear_hardsigmoid.c:51-62, co_emit_mm/_acc)
+//   tile-16 finish   affine = bias ? fp16(run + b) : run;  y = post ? fp16(hsig(affine)) : affine
+//                    (linear_hardsigmoid.c:63-79, co_emit_ew bias then co_emit_lut HardSigmoid)
+//   FP32 finish      y = fp16(post ? hsig(acc + b) : acc + b), single rounding
+//   hsig(v)          clamp(v / 6 + 0.5, 0, 1): the function the reference's 513-entry LUT
+//                    samples (research/custom-ops/src/custom_ops.c:357-369), evaluated exactly
+//                    in FP32 with an IEEE division instead of an interpolated Q0.15 table.
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace b2 {
+
+// Status flag slots (host-mapped pinned memory; one word per kind, written with plain stores so
+// no system-scope atomics are needed). Host side maps them to the B2_STATUS_* bits.
+enum : int { FLAG_TIMEOUT = 0, FLAG_NONFINITE_OUTPUT = 1, FLAG_NONFINITE_INPUT = 2, FLAG_GUARD = 3,
+             FLAG_COUNT = 4 };
+
+__device__ __forceinline__ void raise_flag(unsigned *flags, int idx) {
+    volatile unsigned *p = flags + idx;
+    *p = 1u;
+    __threadfence_system();
+}
+
+__device__ __forceinline__ float hsig(float v) {
+    float r = __fdiv_rn(v, 6.0f) + 0.5f;
+    return fminf(fmaxf(r, 0.0f), 1.0f);
+}
+
+__device__ __forceinline__ float round16(float v) { return __half2float(__float2half_rn(v)); }
+
+// One fold step of the reference's per-K-tile FP16 running sum.
+__device__ __forceinline__ float fold16(float run, float chunk, bool first) {
+    return first ? round16(chunk) : round16(run + chunk);
+}
+
+__device__ __forceinline__ float finish_tile16(float run, float b, bool has_bias, bool post) {
+    float a = has_bias ? round16(run + b) : run;
+    return post ? hsig(a) : a;
+}
+
+__device__ __forceinline__ float finish_fp32(float acc, float b, bool post) {
+    float a = acc + b;
+    return post ? hsig(a) : a;
+}
+
+__device__ __forceinline__ bool half_nonfinite(__half h) {
+    return (__half_as_ushort(h) & 0x7c00u) == 0x7c00u;
+}
+
+}  // namespace b2

@@ -1,0 +1,337 @@
+// device.cu -- CUDA implementation of the host/device seam (b2_device.h).
+//
+// One b2_dev per opened handle: a device ordinal, a non-blocking stream (or a caller's stream),
+// and a few status words in host-mapped pinned memory that kernels set with plain stores (so
+// no system-scope atomics are needed and the host reads them after a stream sync without a copy).
+// b2d_linear picks the kernel for the shape: the weight-streaming GEMV for M <= 8, the persistent
+// tcgen05 GEMM otherwise, plus the separate epilogue kernel for the unfused (CO_SEPARATE) arm.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <new>
+
+#include "../b2_device.h"
+#include "aux_kernels.h"
+#include "common.cuh"
+#include "gemm_sm100.h"
+#include "gemv.h"
+#include "rocket_b200.h"
+
+struct b2_dev {
+    int ordinal;
+    int sm_count;
+    cudaStream_t own;
+    cudaStream_t stream;
+    unsigned *flags;        // host pointer of the mapped status words
+    unsigned *flags_dev;    // the same words as seen by kernels
+};
+
+namespace {
+
+inline bool set_device(const b2_dev *d) { return d && cudaSetDevice(d->ordinal) == cudaSuccess; }
+
+inline int rc_of(cudaError_t e) {
+    if (e == cudaSuccess) return 0;
+    if (e == cudaErrorMemoryAllocation) return ROCKET_E_NOMEM;
+    return ROCKET_E_DEVICE;
+}
+
+inline int flag_of_bit(uint32_t bit) {
+    switch (bit) {
+        case B2D_ST_TIMEOUT: return b2::FLAG_TIMEOUT;
+        case B2D_ST_NONFINITE_OUTPUT: return b2::FLAG_NONFINITE_OUTPUT;
+        case B2D_ST_NONFINITE_INPUT: return b2::FLAG_NONFINITE_INPUT;
+        case B2D_ST_GUARD: return b2::FLAG_GUARD;
+        default: return -1;
+    }
+}
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int b2d_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+int b2d_open(int ordinal, b2_dev **out) {
+    *out = nullptr;
+    if (ordinal < 0 || ordinal >= b2d_device_count()) return ROCKET_E_DEVICE;
+    if (cudaSetDevice(ordinal) != cudaSuccess) return ROCKET_E_DEVICE;
+    b2_dev *d = new (std::nothrow) b2_dev();
+    if (!d) return ROCKET_E_NOMEM;
+    d->ordinal = ordinal;
+    if (cudaDeviceGetAttribute(&d->sm_count, cudaDevAttrMultiProcessorCount, ordinal) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&d->own, cudaStreamNonBlocking) != cudaSuccess) {
+        delete d;
+        return ROCKET_E_DEVICE;
+    }
+    d->stream = d->own;
+    if (cudaHostAlloc(reinterpret_cast<void **>(&d->flags), b2::FLAG_COUNT * sizeof(unsigned),
+                      cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer(reinterpret_cast<void **>(&d->flags_dev), d->flags, 0) != cudaSuccess) {
+        if (d->flags) cudaFreeHost(d->flags);
+        cudaStreamDestroy(d->own);
+        delete d;
+        return ROCKET_E_DEVICE;
+    }
+    memset(d->flags, 0, b2::FLAG_COUNT * sizeof(unsigned));
+    *out = d;
+    return 0;
+}
+
+void b2d_close(b2_dev *d) {
+    if (!d) return;
+    set_device(d);
+    cudaStreamSynchronize(d->stream);
+    cudaStreamDestroy(d->own);
+    cudaFreeHost(d->flags);
+    delete d;
+}
+
+int b2d_set_stream(b2_dev *d, void *stream) {
+    if (!d) return ROCKET_E_SHAPE;
+    d->stream = stream ? static_cast<cudaStream_t>(stream) : d->own;
+    return 0;
+}
+
+void *b2d_stream(b2_dev *d) { return d ? static_cast<void *>(d->stream) : nullptr; }
+int b2d_sm_count(b2_dev *d) { return d ? d->sm_count : 0; }
+
+int b2d_malloc(b2_dev *d, size_t bytes, void **out) {
+    *out = nullptr;
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    void *p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return ROCKET_E_NOMEM;
+    }
+    if (cudaMemsetAsync(p, 0, bytes, d->stream) != cudaSuccess || cudaStreamSynchronize(d->stream) != cudaSuccess) {
+        cudaFree(p);
+        return ROCKET_E_DEVICE;
+    }
+    *out = p;
+    return 0;
+}
+
+void b2d_free(b2_dev *d, void *ptr) {
+    if (!ptr || !set_device(d)) return;
+    cudaStreamSynchronize(d->stream);
+    cudaFree(ptr);
+}
+
+void *b2d_host_alloc(size_t bytes) {
+    void *p = nullptr;
+    if (cudaHostAlloc(&p, bytes, cudaHostAllocPortable) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return p;
+}
+
+void b2d_host_free(void *ptr) {
+    if (ptr) cudaFreeHost(ptr);
+}
+
+int b2d_copy_2d(b2_dev *d, void *dst, size_t dpitch, const void *src, size_t spitch, size_t width, size_t rows,
+                int kind) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (!rows || !width) return 0;
+    const cudaMemcpyKind k = kind == B2D_H2D ? cudaMemcpyHostToDevice
+                             : kind == B2D_D2H ? cudaMemcpyDeviceToHost
+                                               : cudaMemcpyDeviceToDevice;
+    cudaError_t e;
+    if (dpitch == width && spitch == width) e = cudaMemcpyAsync(dst, src, width * rows, k, d->stream);
+    else e = cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, k, d->stream);
+    return rc_of(e);
+}
+
+int b2d_memset(b2_dev *d, void *ptr, int value, size_t bytes) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    return rc_of(cudaMemsetAsync(ptr, value, bytes, d->stream));
+}
+
+int b2d_sync(b2_dev *d) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    return cudaStreamSynchronize(d->stream) == cudaSuccess ? 0 : ROCKET_E_DEVICE;
+}
+
+uint32_t b2d_status(b2_dev *d, int clear) {
+    if (!d) return 0;
+    volatile unsigned *f = d->flags;
+    uint32_t bits = 0;
+    if (f[b2::FLAG_TIMEOUT]) bits |= B2D_ST_TIMEOUT;
+    if (f[b2::FLAG_NONFINITE_OUTPUT]) bits |= B2D_ST_NONFINITE_OUTPUT;
+    if (f[b2::FLAG_NONFINITE_INPUT]) bits |= B2D_ST_NONFINITE_INPUT;
+    if (f[b2::FLAG_GUARD]) bits |= B2D_ST_GUARD;
+    if (clear)
+        for (int i = 0; i < b2::FLAG_COUNT; ++i) f[i] = 0;
+    return bits;
+}
+
+void b2d_status_merge(b2_dev *d, uint32_t bits) {
+    if (!d) return;
+    volatile unsigned *f = d->flags;
+    for (uint32_t b = 1; b <= B2D_ST_GUARD; b <<= 1)
+        if (bits & b) f[flag_of_bit(b)] = 1;
+}
+
+// ----------------------------------------------------------------------------- Linear dispatch
+static bool use_gemv(const b2k_linear *a) { return a->m <= B2D_GEMV_MAX_M; }
+
+int b2d_linear_config(b2_dev *d, const b2k_linear *a, b2k_config *cfg) {
+    if (!d || !a || !cfg) return ROCKET_E_SHAPE;
+    memset(cfg, 0, sizeof(*cfg));
+    if (use_gemv(a)) {
+        cfg->kernel = 1;
+        cfg->tile_m = a->m;
+        cfg->tile_n = 8;
+        cfg->tile_k = 256;
+        cfg->grid = b2::gemv::grid_for((int)a->n, d->sm_count);
+    } else {
+        cfg->kernel = 0;
+        cfg->tile_m = b2::gemm::TILE_M;
+        cfg->tile_n = b2::gemm::TILE_N;
+        cfg->tile_k = b2::gemm::TILE_K;
+        cfg->stages = b2::gemm::NUM_STAGES;
+        cfg->grid = b2::gemm::grid_for((int)a->m, (int)a->n, d->sm_count);
+    }
+    return 0;
+}
+
+int b2d_linear(b2_dev *d, const b2k_linear *a, unsigned *launches) {
+    *launches = 0;
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (!a->m || !a->n || !a->k || !a->x || !a->w || a->ldx % 8 || a->ldw % 8 || a->ldx < a->k ||
+        a->ldw < a->k || !aligned16(a->x) || !aligned16(a->w) || a->m > (1u << 24) || a->n > (1u << 24) ||
+        a->k > (1u << 24))
+        return ROCKET_E_SHAPE;
+    const bool fold = a->acc == 0 && !a->raw_only;
+    int out_mode;
+    if (a->raw_only) out_mode = b2::gemm::OUT_RAW32;
+    else if (a->fused) out_mode = b2::gemm::OUT_FINAL;
+    else out_mode = fold ? b2::gemm::OUT_RAW16 : b2::gemm::OUT_RAW32;
+    if (out_mode == b2::gemm::OUT_RAW32 && (!a->partial || a->ldp < a->n)) return ROCKET_E_SHAPE;
+    if (out_mode != b2::gemm::OUT_RAW32 && (!a->y || a->ldy < a->n)) return ROCKET_E_SHAPE;
+
+    const __half *bias = static_cast<const __half *>(a->bias);
+    cudaError_t e;
+    if (use_gemv(a)) {
+        b2::gemv::Params p = {};
+        p.M = (int)a->m; p.N = (int)a->n; p.K = (int)a->k;
+        p.x = static_cast<const __half *>(a->x); p.ldx = (long long)a->ldx;
+        p.w = static_cast<const __half *>(a->w); p.ldw = (long long)a->ldw;
+        p.bias = out_mode == b2::gemv::OUT_FINAL ? bias : nullptr;
+        p.y = static_cast<__half *>(a->y); p.ldy = (long long)a->ldy;
+        p.partial = a->partial; p.ldp = (long long)a->ldp;
+        p.out_mode = out_mode; p.post = a->post; p.fold = fold ? 1 : 0;
+        p.flags = d->flags_dev;
+        e = b2::gemv::launch(p, d->stream, d->sm_count, nullptr);
+    } else {
+        b2::gemm::Params p = {};
+        p.M = (int)a->m; p.N = (int)a->n; p.K = (int)a->k;
+        p.bias = out_mode == b2::gemm::OUT_FINAL ? bias : nullptr;
+        p.y = static_cast<__half *>(a->y); p.ldy = (long long)a->ldy;
+        p.partial = a->partial; p.ldp = (long long)a->ldp;
+        p.out_mode = out_mode; p.post = a->post; p.fold = fold ? 1 : 0;
+        p.vec_y = a->y && aligned16(a->y) && a->ldy % 8 == 0;
+        p.vec_p = a->partial && aligned16(a->partial) && a->ldp % 4 == 0;
+        p.flags = d->flags_dev;
+        b2::gemm::Shape s = {a->x, a->ldx, a->w, a->ldw};
+        e = b2::gemm::launch(s, p, d->stream, d->ordinal, d->sm_count, nullptr);
+    }
+    if (e != cudaSuccess) return rc_of(e);
+    *launches = 1;
+    if (a->fused || a->raw_only) return 0;
+    // Separate epilogue: FP32 partial -> y, or the folded FP16 sum in y -> y in place.
+    b2::aux::EpilogueParams ep = {};
+    ep.M = (int)a->m; ep.N = (int)a->n;
+    ep.partial = fold ? nullptr : a->partial; ep.ldp = (long long)a->ldp;
+    ep.bias = bias;
+    ep.y = static_cast<__half *>(a->y); ep.ldy = (long long)a->ldy;
+    ep.post = a->post;
+    ep.flags = d->flags_dev;
+    e = b2::aux::epilogue(ep, d->stream, d->sm_count);
+    if (e != cudaSuccess) return rc_of(e);
+    *launches = 2;
+    return 0;
+}
+
+int b2d_epilogue(b2_dev *d, unsigned m, unsigned n, const float *partial, size_t ldp, const void *bias, int post,
+                 int acc, void *y, size_t ldy) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (!m || !n || !partial || !y || ldp < n || ldy < n || acc != 1) return ROCKET_E_SHAPE;
+    b2::aux::EpilogueParams ep = {};
+    ep.M = (int)m; ep.N = (int)n;
+    ep.partial = partial; ep.ldp = (long long)ldp;
+    ep.bias = static_cast<const __half *>(bias);
+    ep.y = static_cast<__half *>(y); ep.ldy = (long long)ldy;
+    ep.post = post;
+    ep.flags = d->flags_dev;
+    return rc_of(b2::aux::epilogue(ep, d->stream, d->sm_count));
+}
+
+int b2d_scan_nonfinite(b2_dev *d, const void *p, size_t rows, size_t cols, size_t ld, uint32_t bit) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    const int flag = flag_of_bit(bit);
+    if (flag < 0 || !p || ld % 8 || !aligned16(p)) return ROCKET_E_SHAPE;
+    if (!rows || !cols) return 0;
+    return rc_of(b2::aux::scan_nonfinite(p, rows, cols, ld, d->flags_dev, flag, d->stream, d->sm_count));
+}
+
+static bool to_tiles(const b2k_cube_tile *in, unsigned count, b2::aux::CubeTiles *t) {
+    if (count > b2::aux::MAX_TILES) return false;
+    memset(t, 0, sizeof(*t));
+    for (unsigned i = 0; i < count; ++i) {
+        if (!in[i].ptr || !aligned16(in[i].ptr) || in[i].physical_cols % 8 || in[i].rows > in[i].physical_rows ||
+            in[i].cols > in[i].physical_cols)
+            return false;
+        t->tile[i] = {in[i].ptr, in[i].rows, in[i].cols, in[i].physical_rows, in[i].physical_cols, in[i].row0,
+                      in[i].col0};
+    }
+    t->count = count;
+    return true;
+}
+
+int b2d_cube_to_rowmajor(b2_dev *d, const b2k_cube_tile *tiles, unsigned count, void *dst, size_t ld) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    b2::aux::CubeTiles t;
+    if (!to_tiles(tiles, count, &t) || !dst || !aligned16(dst) || ld % 8) return ROCKET_E_SHAPE;
+    return rc_of(b2::aux::cube_gather(t, dst, ld, d->stream, d->sm_count));
+}
+
+int b2d_rowmajor_to_cube(b2_dev *d, const void *src, size_t ld, const b2k_cube_tile *tiles, unsigned count) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    b2::aux::CubeTiles t;
+    if (!to_tiles(tiles, count, &t) || !src || !aligned16(src) || ld % 8) return ROCKET_E_SHAPE;
+    return rc_of(b2::aux::cube_scatter(src, ld, t, d->stream, d->sm_count));
+}
+
+int b2d_guard_init(b2_dev *d, void *base, size_t payload, size_t slack, size_t guard) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    return rc_of(cudaMemsetAsync(static_cast<char *>(base) + payload + slack, 0xa5, guard, d->stream));
+}
+
+int b2d_guard_check(b2_dev *d, void *const *bases, const size_t *payloads, unsigned count, size_t slack,
+                    size_t guard) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (count > b2::aux::MAX_TILES) return ROCKET_E_SHAPE;
+    b2::aux::GuardList g;
+    memset(&g, 0, sizeof(g));
+    for (unsigned i = 0; i < count; ++i) {
+        g.base[i] = bases[i];
+        g.payload[i] = payloads[i];
+    }
+    g.count = count;
+    return rc_of(b2::aux::guard_check(g, slack, guard, d->flags_dev, d->stream));
+}
+
+}  // extern "C"

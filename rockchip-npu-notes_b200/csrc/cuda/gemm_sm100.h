@@ -1,0 +1,43 @@
+// gemm_sm100.h -- parameters and host launcher of the tcgen05 GEMM (gemm_sm100.cu).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace b2 {
+namespace gemm {
+
+enum OutMode : int {
+    OUT_FINAL = 0,   // y = FP16 result with bias and activation
+    OUT_RAW16 = 1,   // y = the per-256-K folded FP16 running sum (no bias, no activation)
+    OUT_RAW32 = 2,   // partial = the FP32 accumulator over the whole K
+};
+
+struct Params {
+    int M, N, K;
+    int num_m_blocks, num_n_blocks, num_tiles, num_kb, kb_per_chunk;
+    const __half *bias;          // [N] or nullptr
+    __half *y;                   // [M, ldy]
+    long long ldy;
+    float *partial;              // [M, ldp]
+    long long ldp;
+    int out_mode, post, fold, vec_y, vec_p;
+    unsigned *flags;             // status flag words (common.cuh)
+};
+
+struct Shape {
+    const void *x; size_t ldx;   // FP16 [M, ldx]
+    const void *w; size_t ldw;   // FP16 [N, ldw]
+};
+
+constexpr int TILE_M = 128, TILE_N = 256, TILE_K = 64, NUM_STAGES = 4;
+
+// Launches one persistent GEMM on `stream`. `p` carries M/N/K, epilogue and output fields; the
+// block counts are filled in here. Returns the CUDA error of the launch.
+cudaError_t launch(const Shape &s, Params p, cudaStream_t stream, int device, int sm_count,
+                   unsigned *grid_out);
+// Grid the launch would use (for reporting).
+unsigned grid_for(int M, int N, int sm_count);
+
+}  // namespace gemm
+}  // namespace b2
