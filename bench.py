@@ -1,0 +1,374 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 FP16 Linear path (one JSON line on rank 0).
+
+Workload (per GPU): FP16 Linear Y = X W^T + b at M = N = K = 4096, X ~ N(0,1), W ~ N(0,1/K),
+b = 0, FP32 accumulation, FP16 output -- the reference's headline square case. With N GPUs the
+Linear is column-parallel: rank r owns W[r*4096:(r+1)*4096, :] and Y[:, r*4096:(r+1)*4096] of a
+4096 x (4096*N) x 4096 problem, X is replicated and no collective touches the data path (weak
+scaling, one process per GPU).
+
+  value     whole-job TFLOP/s, inputs resident in HBM: K back-to-back launches of the tcgen05
+            GEMM through b2_linear_run_device, timed with CUDA events on the launching stream,
+            max over ranks. Four rotating X/W/Y sets (384 MiB) > 126 MiB L2, so every launch
+            starts with cold L2.
+  e2e       the same metric through co_linear_run with pinned HOST buffers: H2D of X, device
+            finiteness scan, GEMM, status check, D2H of Y per step.
+  roofline  GEMM kernel: 2*M*N*K FLOPs per launch / event-timed launch duration vs the measured
+            dense 16-bit tensor peak; DRAM traffic per launch from the committed ncu summary.
+  gemv      M=1 decode projections of a SmolLM-135M-shaped layer (HBM GB/s per launch, weights
+            rotated over > 4x L2).
+  cpu_baseline  the oracle's restatement of the reference arithmetic (per-256-K FP16 running
+            sum, tile16_fast) on a bounded row sample, all host threads.
+
+--impl reference  times only that CPU restatement on the same workload (rank 0; other ranks exit).
+"""
+import argparse
+import ctypes
+import importlib
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M = N_PER_GPU = K = 4096
+FLOPS_PER_GPU = 2 * M * N_PER_GPU * K
+METRIC = "FP16 Linear TFLOP/s at 4096^3 + M=1 GEMV HBM GB/s, % of B200 peak, 1-8 GPUs"
+WORKLOAD = ("FP16 Linear Y=XW^T+b, M=N=K=4096 per GPU, column-parallel over N (global N=4096*GPUs), "
+            "X~N(0,1), W~N(0,1/K), b=0, FP32 accumulate, FP16 out")
+GEMV_LAYER = [("q", 576, 576), ("k", 192, 576), ("v", 192, 576), ("o", 576, 576), ("gate", 1536, 576),
+              ("up", 1536, 576), ("down", 576, 1536), ("lm_head", 49152, 576)]
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+def traffic_per_launch():
+    """DRAM bytes (read + write) of one 4096^3 GEMM launch from the committed ncu summary."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get("gemm_4096_fp32acc_bytes")
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while the timed region runs."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            pass
+        self._stop = threading.Event()
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples),
+                "source": "nvml" if self.ok else "unavailable"}
+
+
+def cpu_sample(flops_target_s=10.0, max_rows=M):
+    """Time the oracle's tile16 restatement on a row sample of the workload (all host threads)."""
+    import numpy as np
+    import oracle
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(1)
+    w = oracle.Widened((rng.standard_normal((N_PER_GPU, K)) / np.sqrt(K)).astype(np.float16))
+    b = np.zeros(N_PER_GPU, np.float16)
+    rows = 16
+    while True:
+        x = rng.standard_normal((rows, K)).astype(np.float16)
+        t0 = time.perf_counter()
+        oracle.linear("tile16_fast", x, w, b, post=0, threads=threads)
+        dt = time.perf_counter() - t0
+        if dt >= flops_target_s or rows >= max_rows:
+            break
+        rows = min(max_rows, max(rows * 2, int(rows * flops_target_s / max(dt, 1e-3))))
+    tflops = 2 * rows * N_PER_GPU * K / dt / 1e12
+    return {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} of {M} rows of X against the full W (N=K=4096), tile16_fast oracle, "
+                      f"{dt:.2f} s"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    import numpy as np
+    import oracle
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(1)
+    w = oracle.Widened((rng.standard_normal((N_PER_GPU, K)) / np.sqrt(K)).astype(np.float16))
+    b = np.zeros(N_PER_GPU, np.float16)
+    # size one step so the whole --steps/--warmup run stays near two minutes (<= 0.5 s a step)
+    step_s = min(0.5, 120.0 / max(1, args.steps + args.warmup))
+    rows = 16
+    x = rng.standard_normal((rows, K)).astype(np.float16)
+    t0 = time.perf_counter()
+    oracle.linear("tile16_fast", x, w, b, post=0, threads=threads)
+    dt = time.perf_counter() - t0
+    rows = max(1, min(M, int(rows * step_s / max(dt, 1e-4))))
+    x = rng.standard_normal((rows, K)).astype(np.float16)
+    for _ in range(args.warmup):
+        oracle.linear("tile16_fast", x, w, b, post=0, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.linear("tile16_fast", x, w, b, post=0, threads=threads)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = 2 * rows * N_PER_GPU * K / dt / 1e12
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "m": M, "n_per_gpu": N_PER_GPU, "k": K,
+                       "step": f"{rows} rows of X x full W per step (bounded sample)",
+                       "parallelism": "none (host CPU)"},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                             "sample": f"{rows} of {M} rows of X per step, tile16_fast oracle "
+                                       f"(per-256-K FP16 running sum), {threads} threads"},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-gemv", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    b2 = importlib.import_module("rockchip-npu-notes_b200")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    warmup = max(3, args.warmup)
+    steps = max(1, args.steps)
+    peak_tflops, peak_gbs, peak_src = peaks()
+
+    fd = b2.open_device(local)
+    stream = torch.cuda.ExternalStream(b2.lib().b2_get_stream(fd))
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+
+    # ---------------------------------------------------------------- device-resident timing
+    sets = []
+    for s in range(4):
+        x = torch.randn(M, K, device="cuda", dtype=torch.float32, generator=gen).half()
+        w = (torch.randn(N_PER_GPU, K, device="cuda", dtype=torch.float32, generator=gen) / K ** 0.5).half()
+        y = torch.empty(M, N_PER_GPU, device="cuda", dtype=torch.float16)
+        op = b2.Linear(fd, 1, K, N_PER_GPU, w.cpu().numpy(), np.zeros(N_PER_GPU, np.float16),
+                       post=b2.CO_LINEAR_NONE, mode=b2.CO_CHAIN, acc=b2.ACC_FP32, compat=False)
+        sets.append((x, w, y, op))
+    torch.cuda.synchronize()
+
+    def step(i):
+        x, _, y, op = sets[i % 4]
+        op.run_device(M, x.data_ptr(), K, y.data_ptr(), N_PER_GPU)
+
+    for i in range(warmup):
+        step(i)
+    b2.sync(fd)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = b2.counters()["launches"]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for i in range(steps):
+            step(i)
+        end.record(stream)
+        end.synchronize()
+    gpu_launches = b2.counters()["launches"] - launches0
+    if b2.status(fd):
+        raise RuntimeError("device status raised during the timed region")
+    ms = start.elapsed_time(end) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    torch.cuda.synchronize()
+    value = world * FLOPS_PER_GPU / (ms * 1e-3) / 1e12
+    kernel_tflops = FLOPS_PER_GPU / (ms * 1e-3) / 1e12
+
+    # correctness spot check of the timed configuration (sampled rows vs the FP64 oracle)
+    import oracle
+    x0, w0, y0, _ = sets[0]
+    rows = torch.arange(0, M, 257, device="cuda")
+    ref = oracle.linear("fp64", x0[rows].cpu().numpy(), w0.cpu().numpy(), np.zeros(N_PER_GPU, np.float16),
+                        post=0, want=("act",))["act"]
+    ok, worst = oracle.tolerance_ok(y0[rows].cpu().numpy(), ref)
+    if not ok:
+        raise RuntimeError(f"bench output outside tolerance (worst err/tol {worst:.3f})")
+    for _, _, _, op in sets:
+        op.destroy()
+    del sets
+
+    # ---------------------------------------------------------------- end to end (host buffers)
+    op = b2.Linear(fd, M, K, N_PER_GPU, w0.cpu().numpy(), np.zeros(N_PER_GPU, np.float16),
+                   post=b2.CO_LINEAR_NONE, mode=b2.CO_CHAIN, acc=b2.ACC_FP32, compat=True)
+    hx = b2.lib().b2_host_alloc(M * K * 2)
+    hy = b2.lib().b2_host_alloc(M * N_PER_GPU * 2)
+    xh = np.ctypeslib.as_array(ctypes.cast(hx, ctypes.POINTER(ctypes.c_uint16)), shape=(M, K))
+    xh[:] = x0.cpu().numpy().view(np.uint16)
+    e2e_steps = max(3, min(steps, 200))
+    for _ in range(3):
+        b2.check("co_linear_run", b2.lib().co_linear_run(op.h, hx, hy))
+    if world > 1:
+        dist.barrier()
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record(stream)
+    for _ in range(e2e_steps):
+        b2.check("co_linear_run", b2.lib().co_linear_run(op.h, hx, hy))
+    ee.record(stream)
+    ee.synchronize()
+    e2e_ms = es.elapsed_time(ee) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    op.destroy()
+    b2.lib().b2_host_free(hx)
+    b2.lib().b2_host_free(hy)
+
+    # ---------------------------------------------------------------- GEMV (rank 0, N=1 only)
+    gemv = None
+    if rank == 0 and world == 1 and not args.no_gemv:
+        gemv = bench_gemv(b2, fd, torch, stream, peak_gbs)
+
+    line = None
+    if rank == 0:
+        traffic = traffic_per_launch()
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "m": M, "n_per_gpu": N_PER_GPU, "k": K,
+                       "accumulate": "fp32", "kernel": "tcgen05 persistent GEMM 128x256x64, 4 stages",
+                       "l2": "inputs larger than L2: 4 rotating X/W/Y sets of 96 MiB",
+                       "parallelism": f"column-parallel x{world}, no collective"},
+            "e2e": {"value": world * FLOPS_PER_GPU / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "ms_per_step": e2e_ms, "api": "co_linear_run (pinned host X/Y)",
+                    "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N_PER_GPU * 2},
+            "roofline": {"bound": "tensor", "achieved": kernel_tflops, "peak": peak_tflops, "unit": "TFLOP/s",
+                         "frac": kernel_tflops / peak_tflops, "traffic": traffic,
+                         "peak_source": f"{peak_src} dense 16-bit (cuBLAS bf16 burst)",
+                         "algorithmic_flops_per_launch": FLOPS_PER_GPU},
+            "gpu_launches": gpu_launches,
+            "clocks": clocks.summary(),
+            "spot_check": {"rows": int(rows.numel()), "worst_err_over_tol_vs_fp64": worst},
+        }
+        if gemv:
+            line["gemv"] = gemv
+        if world == 1 and not args.no_cpu:
+            line["cpu_baseline"] = cpu_sample()
+    b2.close(fd)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line:
+        print(json.dumps(line), flush=True)
+
+
+def bench_gemv(b2, fd, torch, stream, peak_gbs):
+    """M=1 projections of a SmolLM-135M-shaped layer, weights rotated over >= 4x L2."""
+    import numpy as np
+    l2 = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
+    out = {"l2_bytes": l2, "projections": {}}
+    layer_bytes, layer_ms = 0, 0.0
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    for name, n, k in GEMV_LAYER:
+        wbytes = 2 * n * k
+        copies = max(2, -(-4 * l2 // wbytes))
+        copies = min(copies, 2048)
+        ops = []
+        w_host = (np.random.default_rng(n * k).standard_normal((n, k)) * 0.02).astype(np.float16)
+        # one operator per weight copy (same values, distinct HBM buffers): copies*bytes >= 4x L2
+        for _ in range(copies):
+            ops.append(b2.Linear(fd, 1, k, n, w_host, None, post=b2.CO_LINEAR_NONE, acc=b2.ACC_FP32, compat=False))
+        x = torch.randn(1, k, device="cuda", generator=gen).half()
+        y = torch.empty(1, n, device="cuda", dtype=torch.float16)
+        reps = max(64, len(ops) * 4)
+        for i in range(len(ops)):
+            ops[i].run_device(1, x.data_ptr(), k, y.data_ptr(), n)
+        b2.sync(fd)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for i in range(reps):
+            ops[i % len(ops)].run_device(1, x.data_ptr(), k, y.data_ptr(), n)
+        e.record(stream)
+        e.synchronize()
+        ms = s.elapsed_time(e) / reps
+        nbytes = 2 * n * k + 2 * k + 2 * n
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out["projections"][name] = {"n": n, "k": k, "bytes": nbytes, "us": ms * 1e3, "gb_s": gbs,
+                                    "frac": gbs / peak_gbs, "weight_copies": len(ops)}
+        if name != "lm_head":
+            layer_bytes += nbytes
+            layer_ms += ms
+        for op in ops:
+            op.destroy()
+    out["layer_7_projections"] = {"bytes": layer_bytes, "us": layer_ms * 1e3,
+                                  "gb_s": layer_bytes / (layer_ms * 1e-3) / 1e9,
+                                  "frac": layer_bytes / (layer_ms * 1e-3) / 1e9 / peak_gbs}
+    out["peak_gbs"] = peak_gbs
+    return out
+
+
+if __name__ == "__main__":
+    main()

@@ -65,6 +65,9 @@ def lib():
         L.oracle_linear.argtypes = [ctypes.c_int, ctypes.c_uint, ctypes.c_uint, ctypes.c_uint,
                                     u16p, u16p, u16p, ctypes.c_int, u16p, dp, dp, ctypes.c_int]
         L.oracle_linear.restype = ctypes.c_int
+        L.oracle_linear_pre.argtypes = [ctypes.c_int, ctypes.c_uint, ctypes.c_uint, ctypes.c_uint,
+                                        u16p, u16p, dp, u16p, ctypes.c_int, u16p, dp, dp, ctypes.c_int]
+        L.oracle_linear_pre.restype = ctypes.c_int
         L.oracle_f16_encode.argtypes = [dp, u16p, ctypes.c_size_t]
         L.oracle_f16_decode.argtypes = [u16p, dp, ctypes.c_size_t]
         _lib = L
@@ -83,16 +86,28 @@ def _ptr(a, ct):
     return a.ctypes.data_as(ctypes.POINTER(ct)) if a is not None else None
 
 
+class Widened:
+    """W converted to float64 once, for repeated oracle calls against the same weights."""
+
+    def __init__(self, w):
+        self.w = _u16(w)
+        self.wd = self.w.view(np.float16).astype(np.float64)
+
+
 def linear(mode, x, w, bias=None, post=1, threads=None, want=("y16",)):
     """Run the C oracle.
 
-    ``x`` [m,k], ``w`` [n,k], ``bias`` [n] or None: float16 arrays (or their uint16 bits).
-    ``post`` 1 = HardSigmoid, 0 = none.  ``want`` selects the outputs among ``y16`` (float16
-    [m,n]), ``act`` (float64 value before the final FP16 rounding) and ``raw`` (float64 pre-bias
-    accumulator).  Returns a dict.
+    ``x`` [m,k], ``w`` [n,k] (or a ``Widened``), ``bias`` [n] or None: float16 arrays (or their
+    uint16 bits).  ``post`` 1 = HardSigmoid, 0 = none.  ``want`` selects the outputs among
+    ``y16`` (float16 [m,n]), ``act`` (float64 value before the final FP16 rounding) and ``raw``
+    (float64 pre-bias accumulator).  Returns a dict.
     """
     if isinstance(mode, str):
         mode = MODES[mode]
+    wd = None
+    if isinstance(w, Widened):
+        wd = w.wd
+        w = w.w
     x = _u16(x)
     w = _u16(w)
     m, k = x.shape
@@ -106,9 +121,10 @@ def linear(mode, x, w, bias=None, post=1, threads=None, want=("y16",)):
     raw = np.empty((m, n), np.float64) if "raw" in want else None
     if threads is None:
         threads = os.cpu_count() or 1
-    rc = lib().oracle_linear(mode, m, k, n, _ptr(x, ctypes.c_uint16), _ptr(w, ctypes.c_uint16),
-                             _ptr(b, ctypes.c_uint16), int(post), _ptr(y16, ctypes.c_uint16),
-                             _ptr(act, ctypes.c_double), _ptr(raw, ctypes.c_double), int(threads))
+    rc = lib().oracle_linear_pre(mode, m, k, n, _ptr(x, ctypes.c_uint16), _ptr(w, ctypes.c_uint16),
+                                 _ptr(wd, ctypes.c_double), _ptr(b, ctypes.c_uint16), int(post),
+                                 _ptr(y16, ctypes.c_uint16), _ptr(act, ctypes.c_double),
+                                 _ptr(raw, ctypes.c_double), int(threads))
     if rc:
         raise RuntimeError(f"oracle_linear failed: {rc}")
     out = {}

@@ -181,7 +181,7 @@ static void element(const oracle_job *j, unsigned r, unsigned col) {
             } else if (j->mode == ORACLE_TILE16_FAST) {
                 const double *xr = j->xd + (size_t)r * k + k0, *wr = j->wd + (size_t)col * k + k0;
                 double s = 0.0;
-#pragma GCC ivdep
+#pragma omp simd reduction(+ : s)
                 for (unsigned c = 0; c < len; c++) s += xr[c] * wr[c];
                 ts = s;
             } else {
@@ -208,24 +208,36 @@ static void *worker(void *arg) {
     return NULL;
 }
 
+static double f16_table[65536];
+static pthread_once_t f16_table_once = PTHREAD_ONCE_INIT;
+static void f16_table_init(void) {
+    for (unsigned i = 0; i < 65536; i++) f16_table[i] = oracle_f16_to_double((uint16_t)i);
+}
+
 static double *widen(const uint16_t *v, size_t n) {
+    pthread_once(&f16_table_once, f16_table_init);
     double *d = malloc(n * sizeof(*d));
     if (!d) return NULL;
-    for (size_t i = 0; i < n; i++) d[i] = oracle_f16_to_double(v[i]);
+    for (size_t i = 0; i < n; i++) d[i] = f16_table[v[i]];
     return d;
 }
 
 /* Returns 0 on success, -1 on bad arguments, -3 on allocation failure. */
-int oracle_linear(int mode, unsigned m, unsigned k, unsigned n,
-                  const uint16_t *x, const uint16_t *w, const uint16_t *bias, int post,
-                  uint16_t *y16, double *act, double *raw, int threads) {
+/* `w_wide`, when not NULL, is W already widened to double ([n,k]); it is used as is (and not
+ * freed) by the modes that work on widened operands, so repeated calls skip the conversion. */
+int oracle_linear_pre(int mode, unsigned m, unsigned k, unsigned n,
+                      const uint16_t *x, const uint16_t *w, const double *w_wide,
+                      const uint16_t *bias, int post,
+                      uint16_t *y16, double *act, double *raw, int threads) {
     if (!m || !k || !n || !x || !w || mode < 0 || mode > ORACLE_FP32ACC || (post != 0 && post != 1))
         return -1;
     double *xd = NULL, *wd = NULL;
+    const double *wuse = NULL;
     if (mode != ORACLE_TILE16_EXACT) {
         xd = widen(x, (size_t)m * k);
-        wd = widen(w, (size_t)n * k);
-        if (!xd || !wd) { free(xd); free(wd); return -3; }
+        if (!w_wide) wd = widen(w, (size_t)n * k);
+        wuse = w_wide ? w_wide : wd;
+        if (!xd || !wuse) { free(xd); free(wd); return -3; }
     }
     if (threads < 1) threads = 1;
     if ((unsigned)threads > m) threads = (int)m;
@@ -233,7 +245,7 @@ int oracle_linear(int mode, unsigned m, unsigned k, unsigned n,
     pthread_t *tid = calloc((size_t)threads, sizeof(*tid));
     if (!jobs || !tid) { free(jobs); free(tid); free(xd); free(wd); return -3; }
     for (int t = 0; t < threads; t++) {
-        jobs[t] = (oracle_job){mode, post, m, k, n, x, w, bias, xd, wd, y16, act, raw,
+        jobs[t] = (oracle_job){mode, post, m, k, n, x, w, bias, xd, wuse, y16, act, raw,
                                (unsigned)((size_t)m * t / threads),
                                (unsigned)((size_t)m * (t + 1) / threads)};
     }
@@ -248,6 +260,12 @@ int oracle_linear(int mode, unsigned m, unsigned k, unsigned n,
     }
     free(created); free(jobs); free(tid); free(xd); free(wd);
     return 0;
+}
+
+int oracle_linear(int mode, unsigned m, unsigned k, unsigned n,
+                  const uint16_t *x, const uint16_t *w, const uint16_t *bias, int post,
+                  uint16_t *y16, double *act, double *raw, int threads) {
+    return oracle_linear_pre(mode, m, k, n, x, w, NULL, bias, post, y16, act, raw, threads);
 }
 
 /* Batch FP16 conversion helpers for the Python side. */
