@@ -8,8 +8,11 @@
 //                    (linear_hardsigmoid.c:63-79, co_emit_ew bias then co_emit_lut HardSigmoid)
 //   FP32 finish      y = fp16(post ? hsig(acc + b) : acc + b), single rounding
 //   hsig(v)          clamp(v / 6 + 0.5, 0, 1): the function the reference's 513-entry LUT
-//                    samples (research/custom-ops/src/custom_ops.c:357-369), evaluated exactly
-//                    in FP32 with an IEEE division instead of an interpolated Q0.15 table.
+//                    samples (research/custom-ops/src/custom_ops.c:357-369), evaluated in FP32
+//                    instead of an interpolated Q0.15 table. v / 6 is the correctly rounded
+//                    quotient, obtained with Markstein's division-by-constant step: q = v * RN(1/6),
+//                    r = v - 6q exactly (one FMA), q' = q + r * RN(1/6) (one FMA) -- three flops
+//                    instead of a full division, checked against IEEE division on all FP32 inputs.
 #pragma once
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -27,25 +30,40 @@ __device__ __forceinline__ void raise_flag(unsigned *flags, int idx) {
     __threadfence_system();
 }
 
+// Correctly rounded v / 6 (Markstein: one exact remainder, one corrective FMA).
+__device__ __forceinline__ float div6(float v) {
+    const float y = 0.16666667f;          // RN(1/6) = 0x3E2AAAAB
+    const float q = __fmul_rn(v, y);
+    const float r = __fmaf_rn(-q, 6.0f, v);
+    return __fmaf_rn(r, y, q);
+}
+
+// clamp(v/6 + 0.5, 0, 1). Exactly 1 for v >= 3 and 0 for v <= -3 (this also covers infinities,
+// for which the remainder step of div6 is undefined); NaN gives 0 like fmax(0, NaN).
 __device__ __forceinline__ float hsig(float v) {
-    float r = __fdiv_rn(v, 6.0f) + 0.5f;
+    if (v >= 3.0f) return 1.0f;
+    if (v <= -3.0f) return 0.0f;
+    const float r = __fadd_rn(div6(v), 0.5f);
     return fminf(fmaxf(r, 0.0f), 1.0f);
 }
+
+// True if v does not round to a finite FP16 (NaN or |v| >= 65520).
+__device__ __forceinline__ bool f16_overflows(float v) { return !(fabsf(v) < 65520.0f); }
 
 __device__ __forceinline__ float round16(float v) { return __half2float(__float2half_rn(v)); }
 
 // One fold step of the reference's per-K-tile FP16 running sum.
 __device__ __forceinline__ float fold16(float run, float chunk, bool first) {
-    return first ? round16(chunk) : round16(run + chunk);
+    return first ? round16(chunk) : round16(__fadd_rn(run, chunk));
 }
 
 __device__ __forceinline__ float finish_tile16(float run, float b, bool has_bias, bool post) {
-    float a = has_bias ? round16(run + b) : run;
+    float a = has_bias ? round16(__fadd_rn(run, b)) : run;
     return post ? hsig(a) : a;
 }
 
 __device__ __forceinline__ float finish_fp32(float acc, float b, bool post) {
-    float a = acc + b;
+    float a = __fadd_rn(acc, b);
     return post ? hsig(a) : a;
 }
 

@@ -4,21 +4,27 @@
 // It replaces the reference's per-output-tile NPU task chain
 //   MM (first K tile) -> MM_ACC (each further K tile, FP16 ping-pong accumulators)
 //   -> EW (bias) -> LUT (HardSigmoid)        research/custom-ops/src/linear_hardsigmoid.c:51-82
-// with one launch:
-//   warp 0      TMA producer: 128x64 X and 256x64 W tiles (128-byte swizzle) into a 4-stage
-//               shared-memory ring, mbarrier transaction counts
-//   warp 1      MMA issuer (one thread): tcgen05.mma kind::f16, M=128 N=256 K=16 per instruction,
-//               accumulating into one of two 256-column TMEM buffers; tcgen05.commit frees ring
-//               stages and publishes finished accumulators
+// with one launch. Two variants share the code (template CG = CTA group):
+//   CG=2  a cluster of two CTAs on a TPC computes a 256x256 output tile with the 2-SM UMMA
+//         (tcgen05.mma.cta_group::2, M=256 N=256 K=16): each CTA stages its own 128 rows of X and
+//         128 rows of W per 64-wide K block (32 KB, 6-stage ring), so per SM the shared-memory
+//         and L2 traffic per FLOP is two thirds of the single-SM tile. Used for M > 128.
+//   CG=1  one CTA computes a 128x256 tile with tcgen05.mma.cta_group::1 (48 KB, 4-stage ring).
+// Roles per CTA (384 threads):
+//   warp 0      TMA producer (one thread): X and W boxes, 128-byte swizzle, into the ring; both
+//               CTAs of a pair signal the leader's full barrier (.cta_group::2, no multicast)
+//   warp 1      MMA issuer (one thread, leader CTA only): tcgen05.mma kind::f16 into one of two
+//               256-column TMEM accumulators; tcgen05.commit (multicast to both CTAs of a pair)
+//               frees ring stages and publishes finished accumulators
 //   warp 2      TMEM allocator (512 columns)
-//   warps 4-11  epilogue: tcgen05.ld of their 32-lane quarter and 128-column half, then either
+//   warps 4-11  epilogue: tcgen05.ld of their 32-lane quarter and 128-column half, then
 //                 - FP32 mode: y = fp16(act(acc + b)), or
 //                 - tile-16 mode (the reference's FP16-K-TILING numerics): the MMA warp closes an
 //                   accumulator every 256 K, the epilogue folds run = fp16(run + chunk) in
 //                   registers and finishes with affine = fp16(run + b), y = fp16(hsig(affine));
-//               results are written with 16-byte stores.
-// Tiles are scheduled persistently: CTA i takes output tiles i, i+grid, ... so the TMA/MMA of the
-// next tile overlaps the epilogue of the previous one (two TMEM accumulators).
+//               16-byte stores to global.
+// Tiles are scheduled persistently (cluster c takes tiles c, c + clusters, ...) so the TMA/MMA of
+// the next tile overlaps the epilogue of the previous one through the two TMEM accumulators.
 //
 // Every mbarrier wait is bounded (globaltimer): on expiry the CTA raises the timeout flag, stops
 // issuing work, waits (bounded) for its own TMA loads and MMAs in flight, frees TMEM and returns.
@@ -33,24 +39,45 @@
 namespace b2 {
 namespace gemm {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int BK = 64;
+constexpr int BN = 256;                 // output columns per tile (both variants)
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 128 + EPI_WARPS * 32;
-constexpr uint32_t A_BYTES = BM * BK * 2;
-constexpr uint32_t B_BYTES = BN * BK * 2;
-constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t TMEM_COLS = 2 * BN;
-constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1;
-constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + NUM_BARS * 8 + 16;
 constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;   // 1 s per wait; a healthy wait is microseconds
 
-// Instruction descriptor, kind::f16: D=F32 (bits 4-5 = 1), A=B=F16 (0), both K-major,
-// N>>3 at bits 17-22, M>>4 at bits 24-28.
-constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+template <int CG>
+struct Cfg {
+    static constexpr int BM = 128 * CG;                 // output rows per tile (per CTA: 128)
+    static constexpr int B_ROWS = BN / CG;              // W rows staged by each CTA
+    static constexpr int STAGES = CG == 2 ? 6 : 4;
+    static constexpr uint32_t A_BYTES = 128 * BK * 2;
+    static constexpr uint32_t B_BYTES = B_ROWS * BK * 2;
+    static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1;
+    static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + NUM_BARS * 8 + 16;
+    // Instruction descriptor, kind::f16: D=F32 (bits 4-5 = 1), A=B=F16 (0), both K-major,
+    // N>>3 at bits 17-22, M>>4 at bits 24-28.
+    static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+};
 
 // ----------------------------------------------------------------------------- PTX wrappers
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -61,6 +88,9 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 }
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
@@ -84,14 +114,19 @@ __device__ __forceinline__ uint64_t global_ns() {
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int *abort_flag,
                                            unsigned *flags) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
-    while (true) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
-        if (global_ns() - t0 > WAIT_LIMIT_NS) {
-            *abort_flag = 1;
-            raise_flag(flags, FLAG_TIMEOUT);
-            return false;
+        if ((i & 255u) == 0) {   // the abort flag and the clock are checked every 256 polls
+            if (*abort_flag) return false;
+            const uint64_t t = global_ns();
+            if (!t0) {
+                t0 = t;
+            } else if (t - t0 > WAIT_LIMIT_NS) {
+                *abort_flag = 1;
+                raise_flag(flags, FLAG_TIMEOUT);
+                return false;
+            }
         }
     }
 }
@@ -102,29 +137,49 @@ __device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity) {
         if (global_ns() - t0 > WAIT_LIMIT_NS) return;
 }
 
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
-                                            int c0, int c1) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
-        : "memory");
+template <int CG>
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1) {
+    if constexpr (CG == 2) {
+        // `bar` is the leader CTA's barrier (shared::cluster address); no multicast.
+        asm volatile(
+            "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+            " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+            "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+            : "memory");
+    } else {
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+            " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+            "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+            : "memory");
+    }
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+template <int CG>
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
-                 "r"(ncols)
-                 : "memory");
+    if constexpr (CG == 2)
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                     : "memory");
+    else
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                     : "memory");
 }
+template <int CG>
 __device__ __forceinline__ void tmem_relinquish() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if constexpr (CG == 2)
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    else
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
 }
+template <int CG>
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-                 : "memory");
+    if constexpr (CG == 2)
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+    else
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -132,19 +187,45 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                         uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate)
-        : "memory");
+template <int CG>
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    if constexpr (CG == 2)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+            "l"(adesc), "l"(bdesc), "r"(Cfg<2>::IDESC), "r"(accumulate)
+            : "memory");
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+            "l"(adesc), "l"(bdesc), "r"(Cfg<1>::IDESC), "r"(accumulate)
+            : "memory");
 }
+// Completion of this thread's earlier MMAs arrives on `bar` (in both CTAs of a pair for CG=2).
+template <int CG>
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     bar)
-                 : "memory");
+    if constexpr (CG == 2) {
+        const uint16_t both = 0x3;
+        asm volatile(
+            "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+            "h"(both)
+            : "memory");
+    } else {
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                     : "memory");
+    }
+}
+template <int CG>
+__device__ __forceinline__ void umma_commit_local(uint32_t bar) {
+    if constexpr (CG == 2)
+        asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                     : "memory");
+    else
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                     : "memory");
 }
 
 // 32 consecutive FP32 columns of this thread's TMEM lane; the wait is in the same asm statement so
@@ -178,31 +259,200 @@ __device__ __forceinline__ float load_bias(const __half *bias, int col, int n) {
     return (bias && col < n) ? __half2float(bias[col]) : 0.0f;
 }
 
+
+// 32 bias values of columns [cb, cb+32) as floats (zero past n or without bias).
+__device__ __forceinline__ void load_bias32(const __half *bias, int cb, int n, float (&b)[32]) {
+    if (bias && cb + 32 <= n) {
+        const uint4 *bp = reinterpret_cast<const uint4 *>(bias + cb);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint4 u = __ldg(bp + q);
+            const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(h[e]);
+                b[8 * q + 2 * e] = f.x;
+                b[8 * q + 2 * e + 1] = f.y;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) b[i] = load_bias(bias, cb + i, n);
+    }
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// 32 FP16 results (16 packed pairs) to row `dst` at columns [cb, cb+32), clipped at n.
+__device__ __forceinline__ void store32(__half *dst, int cb, int n, bool vec, const uint32_t (&pk)[16]) {
+    if (vec && cb + 32 <= n) {
+        uint4 *d = reinterpret_cast<uint4 *>(dst + cb);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) d[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const __half2 h = *reinterpret_cast<const __half2 *>(&pk[i]);
+            if (cb + 2 * i < n) dst[cb + 2 * i] = __low2half(h);
+            if (cb + 2 * i + 1 < n) dst[cb + 2 * i + 1] = __high2half(h);
+        }
+    }
+}
+
+// 32 FP32 raw accumulators to row `dst` at columns [cb, cb+32), clipped at n.
+__device__ __forceinline__ void store32f(float *dst, int cb, int n, bool vec, const float (&v)[32]) {
+    if (vec && cb + 32 <= n) {
+        float4 *d = reinterpret_cast<float4 *>(dst + cb);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (cb + i < n) dst[cb + i] = v[i];
+    }
+}
+
+// Output tile -> (m block, n block). With group_m > 0, tiles are walked in bands of group_m
+// m-blocks so that the clusters running at the same time share X and W blocks in L2.
+__device__ __forceinline__ void tile_coords(int tile, const Params &p, int &mb, int &nb) {
+    if (p.group_m > 0) {
+        const int per_group = p.group_m * p.num_n_blocks;
+        const int g = tile / per_group, r = tile % per_group;
+        const int gm0 = g * p.group_m;
+        const int gsz = min(p.group_m, p.num_m_blocks - gm0);
+        mb = gm0 + r % gsz;
+        nb = r / gsz;
+    } else {
+        mb = tile % p.num_m_blocks;
+        nb = tile / p.num_m_blocks;
+    }
+}
+
+// Epilogue modes (one kernel instantiation each, so no mode branches in the hot code).
+enum : int { EPI_FP32 = 0, EPI_TILE16 = 1, EPI_RAW16 = 2, EPI_RAW32 = 3 };
+
+// Epilogue warps: drain the TMEM accumulator of each finished tile (or 256-K chunk) in four
+// 32-column pieces, hand the accumulator back after the last piece is in registers, finish and
+// store. The loops stay rolled so the code of the persistent kernel fits the instruction cache.
+template <int CG, int MODE>
+__device__ __forceinline__ void epilogue_role(const Params &p, int warp, int lane, uint32_t rank, int cluster_id,
+                                              int num_clusters, int nchunks, uint32_t tmem_base, uint32_t tfull0,
+                                              uint32_t tempty0, volatile int *abort_flag) {
+    using C = Cfg<CG>;
+    const int quarter = warp & 3;          // TMEM lanes [32*quarter, 32*quarter + 32)
+    const int half = (warp - 4) >> 2;      // columns [128*half, 128*half + 128) of the tile
+    const bool has_bias = p.bias != nullptr;
+    const uint32_t tempty_leader = CG == 2 ? map_to_rank(tempty0, 0) : tempty0;
+    uint32_t acc_used = 0;
+    bool ok = true, bad = false;
+    __half2 run[64];                       // per-256-K FP16 running sum (tile-16 modes)
+    for (int tile = cluster_id; ok && tile < p.num_tiles; tile += num_clusters) {
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
+        const int row = mb * C::BM + (int)rank * 128 + quarter * 32 + lane;
+        const bool row_ok = row < p.M;
+        const int col0 = nb * BN + half * 128;
+        for (int c = 0; c < nchunks; ++c) {
+            const uint32_t acc = acc_used & 1u, acc_ph = (acc_used >> 1) & 1u;
+            int got = 1;
+            if (lane == 0) got = wait_phase(tfull0 + 8 * acc, acc_ph, abort_flag, p.flags);
+            got = __shfl_sync(0xffffffffu, got, 0);       // the warp stays converged
+            if (!got) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + half * 128;
+            const bool first = c == 0, last = c == nchunks - 1;
+#pragma unroll 1
+            for (int j = 0; j < 4; ++j) {
+                float v[32];
+                tmem_ld32(taddr + j * 32, v);
+                if (j == 3) {   // accumulator drained into registers: hand it back
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if constexpr (CG == 2) mbar_arrive_cluster(tempty_leader + 8 * acc);
+                        else mbar_arrive(tempty0 + 8 * acc);
+                    }
+                }
+                const int cb = col0 + 32 * j;
+                if constexpr (MODE == EPI_RAW32) {
+                    if (row_ok) store32f(p.partial + (size_t)row * p.ldp, cb, p.N, p.vec_p, v);
+                } else if constexpr (MODE == EPI_FP32) {
+                    float b[32];
+                    load_bias32(p.bias, cb, p.N, b);
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float y0 = finish_fp32(v[2 * i], b[2 * i], p.post);
+                        const float y1 = finish_fp32(v[2 * i + 1], b[2 * i + 1], p.post);
+                        bad |= f16_overflows(y0) | f16_overflows(y1);
+                        pk[i] = pack_half2(y0, y1);
+                    }
+                    if (row_ok) store32(p.y + (size_t)row * p.ldy, cb, p.N, p.vec_y, pk);
+                } else {
+                    __half2 *r = run + 16 * j;
+                    if (!last) {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const float2 o = first ? make_float2(0.0f, 0.0f) : __half22float2(r[i]);
+                            r[i] = __floats2half2_rn(fold16(o.x, v[2 * i], first), fold16(o.y, v[2 * i + 1], first));
+                        }
+                    } else {
+                        float b[32];
+                        if constexpr (MODE == EPI_TILE16) load_bias32(p.bias, cb, p.N, b);
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const float2 o = first ? make_float2(0.0f, 0.0f) : __half22float2(r[i]);
+                            float s0 = fold16(o.x, v[2 * i], first), s1 = fold16(o.y, v[2 * i + 1], first);
+                            if constexpr (MODE == EPI_TILE16) {
+                                s0 = finish_tile16(s0, b[2 * i], has_bias, p.post);
+                                s1 = finish_tile16(s1, b[2 * i + 1], has_bias, p.post);
+                                bad |= f16_overflows(s0) | f16_overflows(s1);
+                            }
+                            pk[i] = pack_half2(s0, s1);
+                        }
+                        if (row_ok) store32(p.y + (size_t)row * p.ldy, cb, p.N, p.vec_y, pk);
+                    }
+                }
+            }
+            ++acc_used;
+        }
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) raise_flag(p.flags, FLAG_NONFINITE_OUTPUT);
+}
+
 // ----------------------------------------------------------------------------- the kernel
+template <int CG, int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const Params p) {
+    using C = Cfg<CG>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~static_cast<uintptr_t>(1023));
     uint8_t *sA = smem;
-    uint8_t *sB = smem + STAGES * A_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NUM_BARS);
+    uint8_t *sB = smem + C::STAGES * C::A_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + C::NUM_BARS);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * STAGES;
-    const uint32_t tfull0 = empty0 + 8 * STAGES, tempty0 = tfull0 + 16, drain_bar = tempty0 + 16;
+    const uint32_t rank = CG == 2 ? cluster_rank() : 0;   // 0 = leader (issues the MMAs)
+    const int cluster_id = (int)blockIdx.x / CG, num_clusters = (int)gridDim.x / CG;
+    const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * C::STAGES;
+    const uint32_t tfull0 = empty0 + 8 * C::STAGES, tempty0 = tfull0 + 16, drain_bar = tempty0 + 16;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < C::STAGES; ++s) {
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull0 + 8 * a, 1);
-            mbar_init(tempty0 + 8 * a, EPI_WARPS);
+            mbar_init(tempty0 + 8 * a, EPI_WARPS * CG);
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -211,11 +461,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         prefetch_tmap(&tmap_b);
     }
     if (warp == 2) {
-        tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
-        tmem_relinquish();
+        tmem_alloc<CG>(smem_u32(tmem_slot), TMEM_COLS);
+        tmem_relinquish<CG>();
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync();   // peer barriers initialised before any remote use
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int nchunks = (p.num_kb + p.kb_per_chunk - 1) / p.kb_per_chunk;
@@ -225,30 +476,34 @@ __global__ void __launch_bounds__(THREADS, 1)
             // ------------------------------------------------------------------ TMA producer
             uint32_t issued = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-                const int mb = tile % p.num_m_blocks, nb = tile / p.num_m_blocks;
+            for (int tile = cluster_id; ok && tile < p.num_tiles; tile += num_clusters) {
+                int mb, nb;
+                tile_coords(tile, p, mb, nb);
+                const int row_a = mb * C::BM + (int)rank * 128, row_b = nb * BN + (int)rank * C::B_ROWS;
                 for (int kb = 0; kb < p.num_kb; ++kb) {
-                    const uint32_t s = issued % STAGES, ph = (issued / STAGES) & 1u;
+                    const uint32_t s = issued % C::STAGES, ph = (issued / C::STAGES) & 1u;
                     if (!wait_phase(empty0 + 8 * s, ph ^ 1u, abort_flag, p.flags)) { ok = false; break; }
-                    mbar_arrive_expect_tx(full0 + 8 * s, STAGE_BYTES);
-                    tma_load_2d(smem_u32(sA + s * A_BYTES), &tmap_a, full0 + 8 * s, kb * BK, mb * BM);
-                    tma_load_2d(smem_u32(sB + s * B_BYTES), &tmap_b, full0 + 8 * s, kb * BK, nb * BN);
+                    uint32_t full_bar = full0 + 8 * s;
+                    if constexpr (CG == 2) full_bar = map_to_rank(full_bar, 0);
+                    if (rank == 0) mbar_arrive_expect_tx(full0 + 8 * s, C::STAGE_BYTES * CG);
+                    tma_load_2d<CG>(smem_u32(sA + s * C::A_BYTES), &tmap_a, full_bar, kb * BK, row_a);
+                    tma_load_2d<CG>(smem_u32(sB + s * C::B_BYTES), &tmap_b, full_bar, kb * BK, row_b);
                     ++issued;
                 }
             }
-            if (!ok) {
+            if (!ok && rank == 0) {
                 // Loads in flight land in the last STAGES slots; wait for each before exiting.
-                const uint32_t first = issued > STAGES ? issued - STAGES : 0;
+                const uint32_t first = issued > (uint32_t)C::STAGES ? issued - C::STAGES : 0;
                 for (uint32_t i = first; i < issued; ++i)
-                    drain_phase(full0 + 8 * (i % STAGES), (i / STAGES) & 1u);
+                    drain_phase(full0 + 8 * (i % C::STAGES), (i / C::STAGES) & 1u);
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        if (lane == 0 && rank == 0) {
             // ------------------------------------------------------------------ MMA issuer
             uint32_t consumed = 0, acc_used = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+            for (int tile = cluster_id; ok && tile < p.num_tiles; tile += num_clusters) {
                 for (int c = 0; ok && c < nchunks; ++c) {
                     const uint32_t acc = acc_used & 1u, acc_ph = (acc_used >> 1) & 1u;
                     if (!wait_phase(tempty0 + 8 * acc, acc_ph ^ 1u, abort_flag, p.flags)) { ok = false; break; }
@@ -257,155 +512,44 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const int kb0 = c * p.kb_per_chunk;
                     const int kb1 = min(kb0 + p.kb_per_chunk, p.num_kb);
                     for (int kb = kb0; kb < kb1; ++kb) {
-                        const uint32_t s = consumed % STAGES, ph = (consumed / STAGES) & 1u;
+                        const uint32_t s = consumed % C::STAGES, ph = (consumed / C::STAGES) & 1u;
                         if (!wait_phase(full0 + 8 * s, ph, abort_flag, p.flags)) { ok = false; break; }
                         tc_fence_after();
-                        const uint64_t adesc = sw128_desc(smem_u32(sA + s * A_BYTES));
-                        const uint64_t bdesc = sw128_desc(smem_u32(sB + s * B_BYTES));
+                        const uint64_t adesc = sw128_desc(smem_u32(sA + s * C::A_BYTES));
+                        const uint64_t bdesc = sw128_desc(smem_u32(sB + s * C::B_BYTES));
 #pragma unroll
                         for (int k = 0; k < BK / 16; ++k)   // +32 bytes along K = +2 in the desc
-                            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, (kb > kb0 || k > 0) ? 1u : 0u);
-                        umma_commit(empty0 + 8 * s);
+                            umma_f16<CG>(d_tmem, adesc + 2 * k, bdesc + 2 * k, (kb > kb0 || k > 0) ? 1u : 0u);
+                        umma_commit<CG>(empty0 + 8 * s);
                         ++consumed;
                     }
                     if (!ok) break;
-                    umma_commit(tfull0 + 8 * acc);
+                    umma_commit<CG>(tfull0 + 8 * acc);
                     ++acc_used;
                 }
             }
-            // All MMAs issued by this thread complete before TMEM can be released.
-            umma_commit(drain_bar);
-            drain_phase(drain_bar, 0);
-        }
-    } else if (warp >= 4) {
-        // ---------------------------------------------------------------------- epilogue
-        const int quarter = warp & 3;          // TMEM lanes [32*quarter, 32*quarter + 32)
-        const int half = (warp - 4) >> 2;      // columns [128*half, 128*half + 128) of the tile
-        const bool has_bias = p.bias != nullptr;
-        uint32_t acc_used = 0;
-        bool ok = true;
-        for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-            const int mb = tile % p.num_m_blocks, nb = tile / p.num_m_blocks;
-            const int row = mb * BM + quarter * 32 + lane;
-            const int col0 = nb * BN + half * 128;
-            __half2 out[64];      // 128 columns as FP16 pairs: the running sum, then the result
-#pragma unroll
-            for (int i = 0; i < 64; ++i) out[i] = __floats2half2_rn(0.0f, 0.0f);
-            for (int c = 0; c < nchunks; ++c) {
-                const uint32_t acc = acc_used & 1u, acc_ph = (acc_used >> 1) & 1u;
-                if (!wait_phase(tfull0 + 8 * acc, acc_ph, abort_flag, p.flags)) { ok = false; break; }
-                __syncwarp();
-                tc_fence_after();
-                const uint32_t taddr =
-                    tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + half * 128;
-                const bool first = c == 0, last = c == nchunks - 1;
-                if (p.out_mode == OUT_RAW32) {
-                    // Raw FP32 accumulator straight from TMEM (K-split partials).
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        float v[32];
-                        tmem_ld32(taddr + j * 32, v);
-                        if (row < p.M) {
-                            float *dst = p.partial + (size_t)row * p.ldp;
-#pragma unroll
-                            for (int g = 0; g < 8; ++g) {
-                                const int col = col0 + j * 32 + g * 4;
-                                if (p.vec_p && col + 4 <= p.N) {
-                                    *reinterpret_cast<float4 *>(dst + col) =
-                                        make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
-                                } else {
-#pragma unroll
-                                    for (int e = 0; e < 4; ++e)
-                                        if (col + e < p.N) dst[col + e] = v[4 * g + e];
-                                }
-                            }
-                        }
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        float v[32];
-                        tmem_ld32(taddr + j * 32, v);
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            float a0 = v[2 * i], a1 = v[2 * i + 1];
-                            if (p.fold) {
-                                const float2 r = __half22float2(out[j * 16 + i]);
-                                a0 = fold16(r.x, a0, first);
-                                a1 = fold16(r.y, a1, first);
-                            } else if (p.out_mode == OUT_FINAL) {
-                                // FP32 mode (a single chunk): finish from the exact accumulator.
-                                const int col = col0 + j * 32 + 2 * i;
-                                a0 = finish_fp32(a0, load_bias(p.bias, col, p.N), p.post);
-                                a1 = finish_fp32(a1, load_bias(p.bias, col + 1, p.N), p.post);
-                            }
-                            out[j * 16 + i] = __floats2half2_rn(a0, a1);
-                        }
-                    }
-                }
-                // Accumulator drained into registers: hand it back to the MMA warp.
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(tempty0 + 8 * acc);
-                ++acc_used;
-                if (!last || p.out_mode == OUT_RAW32) continue;
-
-                // ------------------------------------------------ finish and store 128 columns
-                if (p.out_mode == OUT_FINAL) {
-                    bool bad = false;
-#pragma unroll
-                    for (int i = 0; i < 64; ++i) {
-                        if (p.fold) {   // tile-16 mode: bias and activation after the last fold
-                            const int col = col0 + 2 * i;
-                            const float2 a = __half22float2(out[i]);
-                            out[i] = __floats2half2_rn(
-                                finish_tile16(a.x, load_bias(p.bias, col, p.N), has_bias, p.post),
-                                finish_tile16(a.y, load_bias(p.bias, col + 1, p.N), has_bias, p.post));
-                        }
-                        bad |= half_nonfinite(__low2half(out[i])) | half_nonfinite(__high2half(out[i]));
-                    }
-                    if (__any_sync(0xffffffffu, bad) && lane == 0) raise_flag(p.flags, FLAG_NONFINITE_OUTPUT);
-                }
-                if (row < p.M) {
-                    __half *dst = p.y + (size_t)row * p.ldy;
-#pragma unroll
-                    for (int g = 0; g < 16; ++g) {
-                        const int col = col0 + 8 * g;
-                        if (p.vec_y && col + 8 <= p.N) {
-                            uint4 v;
-                            v.x = *reinterpret_cast<const uint32_t *>(&out[4 * g]);
-                            v.y = *reinterpret_cast<const uint32_t *>(&out[4 * g + 1]);
-                            v.z = *reinterpret_cast<const uint32_t *>(&out[4 * g + 2]);
-                            v.w = *reinterpret_cast<const uint32_t *>(&out[4 * g + 3]);
-                            *reinterpret_cast<uint4 *>(dst + col) = v;
-                        } else {
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                if (col + 2 * e < p.N) dst[col + 2 * e] = __low2half(out[4 * g + e]);
-                                if (col + 2 * e + 1 < p.N) dst[col + 2 * e + 1] = __high2half(out[4 * g + e]);
-                            }
-                        }
-                    }
-                }
+            // All MMAs issued by this thread complete before TMEM can be released (a commit is only
+            // issued when this thread issued MMAs before it).
+            if (consumed) {
+                umma_commit_local<CG>(drain_bar);
+                drain_phase(drain_bar, 0);
             }
         }
+    } else if (warp >= 4) {
+        epilogue_role<CG, MODE>(p, warp, lane, rank, cluster_id, num_clusters, nchunks, tmem_base, tfull0,
+                                tempty0, abort_flag);
     }
 
     tc_fence_before();
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync();   // the leader's MMAs into this CTA's TMEM are done
     if (warp == 2) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, TMEM_COLS);
+        tmem_dealloc<CG>(tmem_base, TMEM_COLS);
     }
 }
 
-}  // namespace gemm
-}  // namespace b2
-
 // ----------------------------------------------------------------------------- host launcher
-namespace b2 {
-namespace gemm {
-
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -431,41 +575,132 @@ static bool make_map(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t
     if (!enc) return false;
     cuuint64_t dims[2] = {inner, rows};
     cuuint64_t strides[1] = {ld * 2};
-    cuuint32_t box[2] = {(cuuint32_t)TILE_K, box_rows};
+    cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
     cuuint32_t estr[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims, strides, box,
                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-unsigned grid_for(int M, int N, int sm_count) {
-    long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    return (unsigned)(tiles < sm_count ? tiles : sm_count);
+// The 2-SM variant pays off once there are enough 256-row tiles to fill the machine.
+static int pick_cg(int M) { return M > 128 ? 2 : 1; }
+
+template <int CG, int MODE>
+static void set_smem_attr() {
+    cudaFuncSetAttribute(gemm_kernel<CG, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)Cfg<CG>::SMEM_BYTES);
 }
 
-cudaError_t launch(const Shape &s, Params p, cudaStream_t stream, int device, int sm_count,
-                   unsigned *grid_out) {
+// Co-resident clusters of the kernel on this device (2-SM clusters must fit inside a GPC, so this
+// can be below sm_count / 2); queried once per device.
+static int resident_clusters(int cg, int sm_count) {
+    static int cached[64][3];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return sm_count / cg;
+    if (cached[dev][cg]) return cached[dev][cg];
+    int n = 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(sm_count / cg * cg));
+    cfg.blockDim = dim3(THREADS);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cg;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
+    if (cg == 2) {
+        cfg.dynamicSmemBytes = Cfg<2>::SMEM_BYTES;
+        set_smem_attr<2, EPI_FP32>();
+        e = cudaOccupancyMaxActiveClusters(&n, gemm_kernel<2, EPI_FP32>, &cfg);
+    } else {
+        cfg.dynamicSmemBytes = Cfg<1>::SMEM_BYTES;
+        set_smem_attr<1, EPI_FP32>();
+        e = cudaOccupancyMaxActiveClusters(&n, gemm_kernel<1, EPI_FP32>, &cfg);
+    }
+    if (e != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = sm_count / cg;
+    }
+    if (n > sm_count / cg) n = sm_count / cg;
+    cached[dev][cg] = n;
+    return n;
+}
+
+unsigned grid_for(int M, int N, int sm_count) {
+    const int cg = pick_cg(M), bm = 128 * cg;
+    const long long tiles = (long long)((M + bm - 1) / bm) * ((N + BN - 1) / BN);
+    const long long clusters = resident_clusters(cg, sm_count);
+    return (unsigned)((tiles < clusters ? tiles : clusters) * cg);
+}
+
+void config_for(int M, unsigned *tile_m, unsigned *tile_n, unsigned *stages) {
+    const int cg = pick_cg(M);
+    *tile_m = 128u * cg;
+    *tile_n = BN;
+    *stages = cg == 2 ? Cfg<2>::STAGES : Cfg<1>::STAGES;
+}
+
+template <int CG, int MODE>
+static cudaError_t launch_mode(const CUtensorMap &ta, const CUtensorMap &tb, const Params &p, unsigned grid,
+                               cudaStream_t stream, int device) {
     static bool attr_done[64];
-    if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
     if (!attr_done[device]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<CG, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)Cfg<CG>::SMEM_BYTES);
         if (e != cudaSuccess) return e;
         attr_done[device] = true;
     }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = Cfg<CG>::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CG;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_kernel<CG, MODE>, ta, tb, p);
+}
+
+template <int CG>
+static cudaError_t launch_cg(const Shape &s, Params p, cudaStream_t stream, int device, int sm_count,
+                             unsigned *grid_out) {
+    using C = Cfg<CG>;
+    if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
     CUtensorMap ta, tb;
-    if (!make_map(&ta, s.x, (uint64_t)p.K, (uint64_t)p.M, s.ldx, BM) ||
-        !make_map(&tb, s.w, (uint64_t)p.K, (uint64_t)p.N, s.ldw, BN))
+    if (!make_map(&ta, s.x, (uint64_t)p.K, (uint64_t)p.M, s.ldx, 128) ||
+        !make_map(&tb, s.w, (uint64_t)p.K, (uint64_t)p.N, s.ldw, C::B_ROWS))
         return cudaErrorInvalidValue;
-    p.num_m_blocks = (p.M + BM - 1) / BM;
+    p.num_m_blocks = (p.M + C::BM - 1) / C::BM;
     p.num_n_blocks = (p.N + BN - 1) / BN;
     p.num_tiles = p.num_m_blocks * p.num_n_blocks;
     p.num_kb = (p.K + BK - 1) / BK;
     p.kb_per_chunk = p.fold ? 256 / BK : p.num_kb;
-    unsigned grid = grid_for(p.M, p.N, sm_count);
+    // Bands of 8 m-blocks keep a wave's X and W blocks L2-resident once the problem outgrows L2.
+    p.group_m = (p.num_m_blocks >= 16 && p.num_n_blocks >= 16 && (long long)p.M * p.K >= (64ll << 20)) ? 8 : 0;
+    const unsigned grid = grid_for(p.M, p.N, sm_count);
     if (grid_out) *grid_out = grid;
-    gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, p);
-    return cudaGetLastError();
+    int mode;
+    if (p.out_mode == OUT_RAW32) mode = EPI_RAW32;
+    else if (p.out_mode == OUT_RAW16) mode = EPI_RAW16;
+    else mode = p.fold ? EPI_TILE16 : EPI_FP32;
+    switch (mode) {
+        case EPI_FP32: return launch_mode<CG, EPI_FP32>(ta, tb, p, grid, stream, device);
+        case EPI_TILE16: return launch_mode<CG, EPI_TILE16>(ta, tb, p, grid, stream, device);
+        case EPI_RAW16: return launch_mode<CG, EPI_RAW16>(ta, tb, p, grid, stream, device);
+        default: return launch_mode<CG, EPI_RAW32>(ta, tb, p, grid, stream, device);
+    }
+}
+
+cudaError_t launch(const Shape &s, Params p, cudaStream_t stream, int device, int sm_count,
+                   unsigned *grid_out) {
+    if (pick_cg(p.M) == 2) return launch_cg<2>(s, p, stream, device, sm_count, grid_out);
+    return launch_cg<1>(s, p, stream, device, sm_count, grid_out);
 }
 
 }  // namespace gemm

@@ -22,6 +22,7 @@ struct Params {
     float *partial;              // [M, ldp]
     long long ldp;
     int out_mode, post, fold, vec_y, vec_p;
+    int group_m;                 // tile raster: bands of group_m m-blocks (0 = column-major)
     unsigned *flags;             // status flag words (common.cuh)
 };
 
@@ -30,14 +31,16 @@ struct Shape {
     const void *w; size_t ldw;   // FP16 [N, ldw]
 };
 
-constexpr int TILE_M = 128, TILE_N = 256, TILE_K = 64, NUM_STAGES = 4;
+constexpr int TILE_K = 64;
 
-// Launches one persistent GEMM on `stream`. `p` carries M/N/K, epilogue and output fields; the
-// block counts are filled in here. Returns the CUDA error of the launch.
+// Launches one persistent GEMM on `stream` (2-SM 256x256 tiles for M > 128, else 1-SM 128x256).
+// `p` carries M/N/K, epilogue and output fields; the block counts are filled in here. Returns
+// the CUDA error of the launch.
 cudaError_t launch(const Shape &s, Params p, cudaStream_t stream, int device, int sm_count,
                    unsigned *grid_out);
-// Grid the launch would use (for reporting).
+// Grid (CTAs) the launch would use, and its tile shape and ring depth (for reporting).
 unsigned grid_for(int M, int N, int sm_count);
+void config_for(int M, unsigned *tile_m, unsigned *tile_n, unsigned *stages);
 
 }  // namespace gemm
 }  // namespace b2
