@@ -198,7 +198,7 @@ int b2d_linear_config(b2_dev *d, const b2k_linear *a, b2k_config *cfg) {
         cfg->grid = b2::gemv::grid_for((int)a->n, d->sm_count);
     } else {
         cfg->kernel = 0;
-        b2::gemm::config_for((int)a->m, &cfg->tile_m, &cfg->tile_n, &cfg->stages);
+        b2::gemm::config_for((int)a->m, (int)a->n, d->sm_count, &cfg->tile_m, &cfg->tile_n, &cfg->stages);
         cfg->tile_k = b2::gemm::TILE_K;
         cfg->grid = b2::gemm::grid_for((int)a->m, (int)a->n, d->sm_count);
     }

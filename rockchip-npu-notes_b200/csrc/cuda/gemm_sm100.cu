@@ -40,25 +40,28 @@ namespace b2 {
 namespace gemm {
 
 constexpr int BK = 64;
-constexpr int BN = 256;                 // output columns per tile (both variants)
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 128 + EPI_WARPS * 32;
-constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;   // 1 s per wait; a healthy wait is microseconds
+constexpr uint32_t SMEM_LIMIT = 232448;              // dynamic shared memory per CTA on sm_100
+constexpr int TILE_N = 256;                          // output columns per tile
 
-template <int CG>
+// Tile configuration: CG CTAs per cluster (1 or 2) and TN output columns per tile (128 or 256).
+template <int CG, int TN>
 struct Cfg {
     static constexpr int BM = 128 * CG;                 // output rows per tile (per CTA: 128)
-    static constexpr int B_ROWS = BN / CG;              // W rows staged by each CTA
-    static constexpr int STAGES = CG == 2 ? 6 : 4;
+    static constexpr int B_ROWS = TN / CG;              // W rows staged by each CTA
     static constexpr uint32_t A_BYTES = 128 * BK * 2;
     static constexpr uint32_t B_BYTES = B_ROWS * BK * 2;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (int)((SMEM_LIMIT - 1024 - 512) / STAGE_BYTES);
     static constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1;
     static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + NUM_BARS * 8 + 16;
+    static constexpr uint32_t TMEM_COLS = 2 * TN;       // two accumulators (power of two >= 32)
     // Instruction descriptor, kind::f16: D=F32 (bits 4-5 = 1), A=B=F16 (0), both K-major,
     // N>>3 at bits 17-22, M>>4 at bits 24-28.
-    static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+    static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(TN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+    static_assert(SMEM_BYTES <= SMEM_LIMIT, "shared memory");
 };
 
 // ----------------------------------------------------------------------------- PTX wrappers
@@ -188,20 +191,21 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 template <int CG>
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
     if constexpr (CG == 2)
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
             "setp.ne.b32 p, %4, 0;\n\t"
             "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-            "l"(adesc), "l"(bdesc), "r"(Cfg<2>::IDESC), "r"(accumulate)
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
             : "memory");
     else
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
             "setp.ne.b32 p, %4, 0;\n\t"
             "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-            "l"(adesc), "l"(bdesc), "r"(Cfg<1>::IDESC), "r"(accumulate)
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
             : "memory");
 }
 // Completion of this thread's earlier MMAs arrives on `bar` (in both CTAs of a pair for CG=2).
@@ -337,24 +341,25 @@ enum : int { EPI_FP32 = 0, EPI_TILE16 = 1, EPI_RAW16 = 2, EPI_RAW32 = 3 };
 // Epilogue warps: drain the TMEM accumulator of each finished tile (or 256-K chunk) in four
 // 32-column pieces, hand the accumulator back after the last piece is in registers, finish and
 // store. The loops stay rolled so the code of the persistent kernel fits the instruction cache.
-template <int CG, int MODE>
+template <int CG, int TN, int MODE>
 __device__ __forceinline__ void epilogue_role(const Params &p, int warp, int lane, uint32_t rank, int cluster_id,
                                               int num_clusters, int nchunks, uint32_t tmem_base, uint32_t tfull0,
                                               uint32_t tempty0, volatile int *abort_flag) {
-    using C = Cfg<CG>;
+    using C = Cfg<CG, TN>;
+    constexpr int HALF = TN / 2, PIECES = HALF / 32;
     const int quarter = warp & 3;          // TMEM lanes [32*quarter, 32*quarter + 32)
-    const int half = (warp - 4) >> 2;      // columns [128*half, 128*half + 128) of the tile
+    const int half = (warp - 4) >> 2;      // columns [HALF*half, HALF*half + HALF) of the tile
     const bool has_bias = p.bias != nullptr;
     const uint32_t tempty_leader = CG == 2 ? map_to_rank(tempty0, 0) : tempty0;
     uint32_t acc_used = 0;
     bool ok = true, bad = false;
-    __half2 run[64];                       // per-256-K FP16 running sum (tile-16 modes)
+    __half2 run[HALF / 2];                 // per-256-K FP16 running sum (tile-16 modes)
     for (int tile = cluster_id; ok && tile < p.num_tiles; tile += num_clusters) {
         int mb, nb;
         tile_coords(tile, p, mb, nb);
         const int row = mb * C::BM + (int)rank * 128 + quarter * 32 + lane;
         const bool row_ok = row < p.M;
-        const int col0 = nb * BN + half * 128;
+        const int col0 = nb * TN + half * HALF;
         for (int c = 0; c < nchunks; ++c) {
             const uint32_t acc = acc_used & 1u, acc_ph = (acc_used >> 1) & 1u;
             int got = 1;
@@ -362,13 +367,13 @@ __device__ __forceinline__ void epilogue_role(const Params &p, int warp, int lan
             got = __shfl_sync(0xffffffffu, got, 0);       // the warp stays converged
             if (!got) { ok = false; break; }
             tc_fence_after();
-            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + half * 128;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * TN + half * HALF;
             const bool first = c == 0, last = c == nchunks - 1;
 #pragma unroll 1
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < PIECES; ++j) {
                 float v[32];
                 tmem_ld32(taddr + j * 32, v);
-                if (j == 3) {   // accumulator drained into registers: hand it back
+                if (j == PIECES - 1) {   // accumulator drained into registers: hand it back
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) {
@@ -425,11 +430,11 @@ __device__ __forceinline__ void epilogue_role(const Params &p, int warp, int lan
 }
 
 // ----------------------------------------------------------------------------- the kernel
-template <int CG, int MODE>
+template <int CG, int TN, int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                 const Params p) {
-    using C = Cfg<CG>;
+    using C = Cfg<CG, TN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~static_cast<uintptr_t>(1023));
@@ -461,7 +466,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         prefetch_tmap(&tmap_b);
     }
     if (warp == 2) {
-        tmem_alloc<CG>(smem_u32(tmem_slot), TMEM_COLS);
+        tmem_alloc<CG>(smem_u32(tmem_slot), C::TMEM_COLS);
         tmem_relinquish<CG>();
     }
     tc_fence_before();
@@ -479,7 +484,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int tile = cluster_id; ok && tile < p.num_tiles; tile += num_clusters) {
                 int mb, nb;
                 tile_coords(tile, p, mb, nb);
-                const int row_a = mb * C::BM + (int)rank * 128, row_b = nb * BN + (int)rank * C::B_ROWS;
+                const int row_a = mb * C::BM + (int)rank * 128, row_b = nb * TN + (int)rank * C::B_ROWS;
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     const uint32_t s = issued % C::STAGES, ph = (issued / C::STAGES) & 1u;
                     if (!wait_phase(empty0 + 8 * s, ph ^ 1u, abort_flag, p.flags)) { ok = false; break; }
@@ -508,7 +513,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const uint32_t acc = acc_used & 1u, acc_ph = (acc_used >> 1) & 1u;
                     if (!wait_phase(tempty0 + 8 * acc, acc_ph ^ 1u, abort_flag, p.flags)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t d_tmem = tmem_base + acc * BN;
+                    const uint32_t d_tmem = tmem_base + acc * TN;
                     const int kb0 = c * p.kb_per_chunk;
                     const int kb1 = min(kb0 + p.kb_per_chunk, p.num_kb);
                     for (int kb = kb0; kb < kb1; ++kb) {
@@ -519,7 +524,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const uint64_t bdesc = sw128_desc(smem_u32(sB + s * C::B_BYTES));
 #pragma unroll
                         for (int k = 0; k < BK / 16; ++k)   // +32 bytes along K = +2 in the desc
-                            umma_f16<CG>(d_tmem, adesc + 2 * k, bdesc + 2 * k, (kb > kb0 || k > 0) ? 1u : 0u);
+                            umma_f16<CG>(d_tmem, adesc + 2 * k, bdesc + 2 * k, C::IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
                         umma_commit<CG>(empty0 + 8 * s);
                         ++consumed;
                     }
@@ -536,7 +541,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     } else if (warp >= 4) {
-        epilogue_role<CG, MODE>(p, warp, lane, rank, cluster_id, num_clusters, nchunks, tmem_base, tfull0,
+        epilogue_role<CG, TN, MODE>(p, warp, lane, rank, cluster_id, num_clusters, nchunks, tmem_base, tfull0,
                                 tempty0, abort_flag);
     }
 
@@ -545,7 +550,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if constexpr (CG == 2) cluster_sync();   // the leader's MMAs into this CTA's TMEM are done
     if (warp == 2) {
         tc_fence_after();
-        tmem_dealloc<CG>(tmem_base, TMEM_COLS);
+        tmem_dealloc<CG>(tmem_base, C::TMEM_COLS);
     }
 }
 
@@ -582,125 +587,133 @@ static bool make_map(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// The 2-SM variant pays off once there are enough 256-row tiles to fill the machine.
-static int pick_cg(int M) { return M > 128 ? 2 : 1; }
 
-template <int CG, int MODE>
-static void set_smem_attr() {
-    cudaFuncSetAttribute(gemm_kernel<CG, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)Cfg<CG>::SMEM_BYTES);
+template <int CG, int TN, int MODE>
+static cudaError_t set_smem_attr() {
+    return cudaFuncSetAttribute(gemm_kernel<CG, TN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)Cfg<CG, TN>::SMEM_BYTES);
 }
 
-// Co-resident clusters of the kernel on this device (2-SM clusters must fit inside a GPC, so this
-// can be below sm_count / 2); queried once per device.
-static int resident_clusters(int cg, int sm_count) {
-    static int cached[64][3];
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return sm_count / cg;
-    if (cached[dev][cg]) return cached[dev][cg];
-    int n = 0;
+static cudaLaunchConfig_t cluster_config(int cg, unsigned grid, uint32_t smem, cudaStream_t stream,
+                                         cudaLaunchAttribute *attr) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(sm_count / cg * cg));
+    cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(THREADS);
-    cudaLaunchAttribute attr[1];
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = cg;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e;
-    if (cg == 2) {
-        cfg.dynamicSmemBytes = Cfg<2>::SMEM_BYTES;
-        set_smem_attr<2, EPI_FP32>();
-        e = cudaOccupancyMaxActiveClusters(&n, gemm_kernel<2, EPI_FP32>, &cfg);
-    } else {
-        cfg.dynamicSmemBytes = Cfg<1>::SMEM_BYTES;
-        set_smem_attr<1, EPI_FP32>();
-        e = cudaOccupancyMaxActiveClusters(&n, gemm_kernel<1, EPI_FP32>, &cfg);
-    }
-    if (e != cudaSuccess || n <= 0) {
+    return cfg;
+}
+
+// Co-resident clusters of a variant on the current device (2-SM clusters must fit inside a GPC,
+// so this can be below sm_count / 2); queried once per device and variant.
+template <int CG, int TN>
+static int resident_clusters(int sm_count) {
+    static int cached[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return sm_count / CG;
+    if (cached[dev]) return cached[dev];
+    int n = 0;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = cluster_config(CG, (unsigned)(sm_count / CG * CG), Cfg<CG, TN>::SMEM_BYTES, 0, attr);
+    if (set_smem_attr<CG, TN, EPI_FP32>() != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, gemm_kernel<CG, TN, EPI_FP32>, &cfg) != cudaSuccess || n <= 0) {
         cudaGetLastError();
-        n = sm_count / cg;
+        n = sm_count / CG;
     }
-    if (n > sm_count / cg) n = sm_count / cg;
-    cached[dev][cg] = n;
+    if (n > sm_count / CG) n = sm_count / CG;
+    cached[dev] = n;
     return n;
 }
 
-unsigned grid_for(int M, int N, int sm_count) {
-    const int cg = pick_cg(M), bm = 128 * cg;
-    const long long tiles = (long long)((M + bm - 1) / bm) * ((N + BN - 1) / BN);
-    const long long clusters = resident_clusters(cg, sm_count);
+static int clusters_for(int cg, int sm_count) {
+    return cg == 2 ? resident_clusters<2, TILE_N>(sm_count) : resident_clusters<1, TILE_N>(sm_count);
+}
+
+// Tiles are TILE_N = 256 columns wide: narrower tiles need more operand traffic per FLOP and
+// measured 0.55-0.65x the throughput on B200. Picks the CTA group with fewer persistent waves,
+// preferring the 2-SM pair (less shared-memory traffic per FLOP); 2-SM tiles need M > 128.
+static int choose_cg(int M, int N, int sm_count) {
+    if (M <= 128) return 1;
+    long long waves[3];
+    for (int cg = 1; cg <= 2; ++cg) {
+        const long long tiles = (long long)((M + 128 * cg - 1) / (128 * cg)) * ((N + TILE_N - 1) / TILE_N);
+        const long long clusters = clusters_for(cg, sm_count);
+        waves[cg] = (tiles + clusters - 1) / clusters;
+    }
+    return waves[1] < waves[2] ? 1 : 2;
+}
+
+unsigned grid_for_variant(int cg, int M, int N, int sm_count) {
+    const long long tiles = (long long)((M + 128 * cg - 1) / (128 * cg)) * ((N + TILE_N - 1) / TILE_N);
+    const long long clusters = clusters_for(cg, sm_count);
     return (unsigned)((tiles < clusters ? tiles : clusters) * cg);
 }
 
-void config_for(int M, unsigned *tile_m, unsigned *tile_n, unsigned *stages) {
-    const int cg = pick_cg(M);
-    *tile_m = 128u * cg;
-    *tile_n = BN;
-    *stages = cg == 2 ? Cfg<2>::STAGES : Cfg<1>::STAGES;
+unsigned grid_for(int M, int N, int sm_count) {
+    return grid_for_variant(choose_cg(M, N, sm_count), M, N, sm_count);
 }
 
-template <int CG, int MODE>
+void config_for(int M, int N, int sm_count, unsigned *tile_m, unsigned *tile_n, unsigned *stages) {
+    const int cg = choose_cg(M, N, sm_count);
+    *tile_m = 128u * cg;
+    *tile_n = (unsigned)TILE_N;
+    *stages = cg == 2 ? Cfg<2, TILE_N>::STAGES : Cfg<1, TILE_N>::STAGES;
+}
+
+template <int CG, int TN, int MODE>
 static cudaError_t launch_mode(const CUtensorMap &ta, const CUtensorMap &tb, const Params &p, unsigned grid,
                                cudaStream_t stream, int device) {
     static bool attr_done[64];
     if (!attr_done[device]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel<CG, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)Cfg<CG>::SMEM_BYTES);
+        const cudaError_t e = set_smem_attr<CG, TN, MODE>();
         if (e != cudaSuccess) return e;
         attr_done[device] = true;
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = Cfg<CG>::SMEM_BYTES;
-    cfg.stream = stream;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = CG;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_kernel<CG, MODE>, ta, tb, p);
+    cudaLaunchConfig_t cfg = cluster_config(CG, grid, Cfg<CG, TN>::SMEM_BYTES, stream, attr);
+    return cudaLaunchKernelEx(&cfg, gemm_kernel<CG, TN, MODE>, ta, tb, p);
 }
 
-template <int CG>
-static cudaError_t launch_cg(const Shape &s, Params p, cudaStream_t stream, int device, int sm_count,
-                             unsigned *grid_out) {
-    using C = Cfg<CG>;
+template <int CG, int TN>
+static cudaError_t launch_tile(const Shape &s, Params p, cudaStream_t stream, int device, int sm_count,
+                               unsigned *grid_out) {
+    using C = Cfg<CG, TN>;
     if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
     CUtensorMap ta, tb;
     if (!make_map(&ta, s.x, (uint64_t)p.K, (uint64_t)p.M, s.ldx, 128) ||
         !make_map(&tb, s.w, (uint64_t)p.K, (uint64_t)p.N, s.ldw, C::B_ROWS))
         return cudaErrorInvalidValue;
     p.num_m_blocks = (p.M + C::BM - 1) / C::BM;
-    p.num_n_blocks = (p.N + BN - 1) / BN;
+    p.num_n_blocks = (p.N + TN - 1) / TN;
     p.num_tiles = p.num_m_blocks * p.num_n_blocks;
     p.num_kb = (p.K + BK - 1) / BK;
     p.kb_per_chunk = p.fold ? 256 / BK : p.num_kb;
-    // Bands of 8 m-blocks keep a wave's X and W blocks L2-resident once the problem outgrows L2.
+    // Bands of 8 m-blocks keep a wave's X and W blocks L2-resident once X outgrows the L2.
     p.group_m = (p.num_m_blocks >= 16 && p.num_n_blocks >= 16 && (long long)p.M * p.K >= (64ll << 20)) ? 8 : 0;
-    const unsigned grid = grid_for(p.M, p.N, sm_count);
+    const unsigned grid = grid_for_variant(CG, p.M, p.N, sm_count);
     if (grid_out) *grid_out = grid;
-    int mode;
-    if (p.out_mode == OUT_RAW32) mode = EPI_RAW32;
-    else if (p.out_mode == OUT_RAW16) mode = EPI_RAW16;
-    else mode = p.fold ? EPI_TILE16 : EPI_FP32;
-    switch (mode) {
-        case EPI_FP32: return launch_mode<CG, EPI_FP32>(ta, tb, p, grid, stream, device);
-        case EPI_TILE16: return launch_mode<CG, EPI_TILE16>(ta, tb, p, grid, stream, device);
-        case EPI_RAW16: return launch_mode<CG, EPI_RAW16>(ta, tb, p, grid, stream, device);
-        default: return launch_mode<CG, EPI_RAW32>(ta, tb, p, grid, stream, device);
-    }
+    if (p.out_mode == OUT_RAW32) return launch_mode<CG, TN, EPI_RAW32>(ta, tb, p, grid, stream, device);
+    if (p.out_mode == OUT_RAW16) return launch_mode<CG, TN, EPI_RAW16>(ta, tb, p, grid, stream, device);
+    if (p.fold) return launch_mode<CG, TN, EPI_TILE16>(ta, tb, p, grid, stream, device);
+    return launch_mode<CG, TN, EPI_FP32>(ta, tb, p, grid, stream, device);
+}
+
+cudaError_t launch_variant(int cg, const Shape &s, const Params &p, cudaStream_t stream, int device,
+                           int sm_count, unsigned *grid_out) {
+    if (cg == 2) return launch_tile<2, TILE_N>(s, p, stream, device, sm_count, grid_out);
+    if (cg == 1) return launch_tile<1, TILE_N>(s, p, stream, device, sm_count, grid_out);
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch(const Shape &s, Params p, cudaStream_t stream, int device, int sm_count,
                    unsigned *grid_out) {
-    if (pick_cg(p.M) == 2) return launch_cg<2>(s, p, stream, device, sm_count, grid_out);
-    return launch_cg<1>(s, p, stream, device, sm_count, grid_out);
+    return launch_variant(choose_cg(p.M, p.N, sm_count), s, p, stream, device, sm_count, grid_out);
 }
 
 }  // namespace gemm

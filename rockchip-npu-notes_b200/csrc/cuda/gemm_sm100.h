@@ -33,14 +33,17 @@ struct Shape {
 
 constexpr int TILE_K = 64;
 
-// Launches one persistent GEMM on `stream` (2-SM 256x256 tiles for M > 128, else 1-SM 128x256).
+// Launches one persistent GEMM on `stream` with the tile shape chosen for (M, N).
 // `p` carries M/N/K, epilogue and output fields; the block counts are filled in here. Returns
 // the CUDA error of the launch.
 cudaError_t launch(const Shape &s, Params p, cudaStream_t stream, int device, int sm_count,
                    unsigned *grid_out);
+// A specific variant: cg CTAs per cluster (1 = 128x256 tiles, 2 = 256x256 tiles per CTA pair).
+cudaError_t launch_variant(int cg, const Shape &s, const Params &p, cudaStream_t stream, int device,
+                           int sm_count, unsigned *grid_out);
 // Grid (CTAs) the launch would use, and its tile shape and ring depth (for reporting).
 unsigned grid_for(int M, int N, int sm_count);
-void config_for(int M, unsigned *tile_m, unsigned *tile_n, unsigned *stages);
+void config_for(int M, int N, int sm_count, unsigned *tile_m, unsigned *tile_n, unsigned *stages);
 
 }  // namespace gemm
 }  // namespace b2
