@@ -73,6 +73,34 @@ int b2_linear_partial_device(b2_linear *, unsigned m, const void *x, size_t ldx,
 int b2_linear_epilogue_device(b2_linear *, unsigned m, const float *partial, size_t ldp,
                               void *y, size_t ldy);
 
+/* No counterpart in the reference: an allocation-free way to run the unfused FP32 arm.
+ *
+ * Some callers must not allocate GPU memory once they are running -- for instance a serving loop
+ * whose device memory is planned up front, where a cudaMalloc/cudaFree in the middle of a request
+ * would synchronise the device, add latency, or fail under memory pressure. The other entries
+ * that run the unfused FP32 arm (CO_SEPARATE mode with B2_ACC_FP32) allocate their M x N FP32
+ * workspace with cudaMalloc on first use. This entry instead uses a fixed scratch array that the
+ * library keeps in static device memory: B2_NOALLOC_SCRATCH_BYTES (8 MiB) on every GPU that
+ * loads the library, held until the process exits.
+ *
+ * Computes Y[m, ldy] = act(X W^T + b) like b2_linear_run_device, with FP32 accumulation over the
+ * whole K (the operator must use B2_ACC_FP32, else ROCKET_E_UNSUPPORTED), as two launches: the
+ * GEMM writes the raw FP32 accumulator into the scratch, then the epilogue kernel writes Y.
+ * The caller passes device X and Y (same rules as b2_linear_run_device). Nothing is allocated:
+ * no cudaMalloc/cudaFree and no allocating library call.
+ *
+ * Limits and rules:
+ *   - m * roundup(n, 4) * 4 bytes must fit in B2_NOALLOC_SCRATCH_BYTES, else ROCKET_E_TILING
+ *     (for example n = 4096 allows m <= 512).
+ *   - The first call on a device looks up the scratch address (cudaGetSymbolAddress) and caches
+ *     it; make that first call before any stream capture.
+ *   - All calls on a device share the one scratch array and it keeps the last call's contents.
+ *     No clearing is needed (each call writes every scratch element it later reads), but calls
+ *     whose work overlaps on the GPU -- two streams, or two operators at once -- race on it.
+ *   - Asynchronous on the handle's stream, like b2_linear_run_device. */
+#define B2_NOALLOC_SCRATCH_BYTES (8u << 20)
+int b2_linear_run_device_noalloc(b2_linear *, unsigned m, const void *x, size_t ldx, void *y, size_t ldy);
+
 typedef struct {
     unsigned m, k, n;
     unsigned kernel;             /* 0 = tcgen05 GEMM, 1 = GEMV (small M) */

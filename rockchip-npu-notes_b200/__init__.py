@@ -156,6 +156,7 @@ SIGNATURES = {
     "b2_linear_create": (_I, [_I, _U, _U, _U, _P, _P, _I, _I, _I, ctypes.POINTER(_P)]),
     "b2_linear_set_accumulate": (_I, [_P, _I]),
     "b2_linear_run_device": (_I, [_P, _U, _P, _Z, _P, _Z]),
+    "b2_linear_run_device_noalloc": (_I, [_P, _U, _P, _Z, _P, _Z]),
     "b2_linear_partial_device": (_I, [_P, _U, _P, _Z, _P, _Z]),
     "b2_linear_epilogue_device": (_I, [_P, _U, _P, _Z, _P, _Z]),
     "b2_linear_get_info": (_I, [_P, ctypes.POINTER(B2LinearInfo)]),

@@ -99,6 +99,14 @@ int b2d_cube_to_rowmajor(b2_dev *, const b2k_cube_tile *tiles, unsigned count, v
 int b2d_rowmajor_to_cube(b2_dev *, const void *src, size_t ld, const b2k_cube_tile *tiles,
                          unsigned count);
 
+/* Ordinal of the CUDA device behind a handle (-1 for NULL). */
+int b2d_ordinal(b2_dev *);
+
+/* Fixed FP32 scratch of B2D_NOALLOC_SCRATCH_BYTES in every device's static memory (noalloc.cu).
+ * The first call on a device looks its address up (cudaGetSymbolAddress); nothing is allocated. */
+#define B2D_NOALLOC_SCRATCH_BYTES (8u << 20)
+int b2d_noalloc_scratch(b2_dev *, float **ptr, size_t *bytes);
+
 /* Guard regions: [payload, payload+slack) must be zero, [payload+slack, +guard) 0xA5. */
 int b2d_guard_init(b2_dev *, void *base, size_t payload, size_t slack, size_t guard);
 /* Checks up to B2K_MAX_CUBE_TILES buffers; sets B2_STATUS_GUARD on any mismatch. */

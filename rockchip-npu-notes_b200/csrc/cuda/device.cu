@@ -104,6 +104,7 @@ int b2d_set_stream(b2_dev *d, void *stream) {
 }
 
 void *b2d_stream(b2_dev *d) { return d ? static_cast<void *>(d->stream) : nullptr; }
+int b2d_ordinal(b2_dev *d) { return d ? d->ordinal : -1; }
 int b2d_sm_count(b2_dev *d) { return d ? d->sm_count : 0; }
 
 int b2d_malloc(b2_dev *d, size_t bytes, void **out) {

@@ -400,6 +400,30 @@ int b2_linear_run_device(b2_linear *c, unsigned m, const void *x, size_t ldx, vo
     return rc;
 }
 
+/* Allocation-free unfused FP32 arm: the FP32 accumulator goes to the library's static device
+ * scratch (b2d_noalloc_scratch) instead of a cudaMalloc'ed workspace. */
+int b2_linear_run_device_noalloc(b2_linear *c, unsigned m, const void *x, size_t ldx, void *y,
+                                 size_t ldy) {
+    if (!device_args_ok(c, m, x, ldx, y, ldy, 0)) return ROCKET_E_SHAPE;
+    if (c->acc != B2_ACC_FP32) return ROCKET_E_UNSUPPORTED;
+    const size_t ldp = b2h_round_up(c->plan.n, 4);
+    if ((size_t)m * ldp * 4 > B2_NOALLOC_SCRATCH_BYTES) return ROCKET_E_TILING;
+    float *scratch = NULL;
+    size_t scratch_bytes = 0;
+    int rc = b2d_noalloc_scratch(b2h_dev(c->fd), &scratch, &scratch_bytes);
+    if (rc) return rc;
+    if ((size_t)m * ldp * 4 > scratch_bytes) return ROCKET_E_TILING;
+    if (b2h_fault(B2_FAULT_LAUNCH)) return ROCKET_E_DEVICE;
+    b2k_linear a = {.m = m, .n = c->plan.n, .k = c->plan.k, .x = x, .ldx = ldx, .w = c->w,
+                    .ldw = c->ldw, .bias = c->bias, .y = y, .ldy = ldy, .partial = scratch,
+                    .ldp = ldp, .post = c->post == CO_LINEAR_HSIG, .acc = B2_ACC_FP32, .fused = 0,
+                    .raw_only = 0};
+    unsigned launches = 0;
+    rc = b2d_linear(b2h_dev(c->fd), &a, &launches);
+    if (launches) count_run(c, launches);
+    return rc;
+}
+
 int b2_linear_partial_device(b2_linear *c, unsigned m, const void *x, size_t ldx, float *partial,
                              size_t ldp) {
     if (!device_args_ok(c, m, x, ldx, partial, ldp, 1)) return ROCKET_E_SHAPE;
