@@ -1,0 +1,97 @@
+"""The linear_hardsigmoid file CLI against the reference's file-gate contract.
+
+research/custom-ops/tools/python/cli_gate.py drives research/custom-ops/tools/c/operator_cli.c:
+  * SHAPES with LCG inputs, both modes, repeat 3: output within 0.002 of the oracle, chain and
+    separate outputs byte-identical, and "repeat=3 submits=S tasks=T PASS" with S = output_tiles*3
+    (chain) or tasks*3 (separate) and T = tasks*3 (cli_gate.py:55-96);
+  * invalid sizes / non-finite input / bad dims exit 1 and leave an existing output file
+    untouched (cli_gate.py:98-114);
+  * no device exits 77 (operator_cli.c:75-76).
+The negative cases fail before any device is opened, so they run on a CPU-only host as well.
+"""
+import json
+import math
+import os
+import re
+import struct
+import subprocess
+
+import numpy as np
+import pytest
+
+import oracle
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def run(cli, args, timeout=120):
+    return subprocess.run([cli] + [str(a) for a in args], capture_output=True, text=True, timeout=timeout)
+
+
+def write_half(path, values):
+    path.write_bytes(np.asarray(values, np.float16).tobytes())
+
+
+def test_help_and_usage(b2):
+    r = run(b2.CLI_PATH, ["--help"])
+    assert r.returncode == 0 and "usage:" in r.stdout
+    assert run(b2.CLI_PATH, []).returncode == 1
+    assert run(b2.CLI_PATH, [1, 1, 1, "a", "b", "c", "d", "sideways"]).returncode == 1
+
+
+def test_invalid_inputs_preserve_existing_output(b2, tmp_path):
+    xfile, wfile, bfile, out = (tmp_path / n for n in ("x.bin", "w.bin", "b.bin", "y.bin"))
+    write_half(wfile, [1])
+    write_half(bfile, [0])
+    marker = b"existing-output-preserved"
+    cases = [(b"", "1"), (struct.pack("<ee", 1, 2), "1"), (struct.pack("<e", math.nan), "1"),
+             (struct.pack("<e", 1), "0"), (struct.pack("<e", 1), "4097")]
+    for data, m in cases:
+        xfile.write_bytes(data)
+        out.write_bytes(marker)
+        r = run(b2.CLI_PATH, [m, 1, 1, xfile, wfile, bfile, out])
+        assert r.returncode == 1, (m, data, r.stderr)
+        assert out.read_bytes() == marker
+    # output path equal to an input path is refused
+    xfile.write_bytes(struct.pack("<e", 1))
+    assert run(b2.CLI_PATH, [1, 1, 1, xfile, wfile, bfile, wfile]).returncode == 1
+
+
+def test_no_device_exits_77(b2, tmp_path):
+    if b2.device_count() > 0:
+        pytest.skip("a CUDA device is present")
+    xfile, wfile, bfile, out = (tmp_path / n for n in ("x.bin", "w.bin", "b.bin", "y.bin"))
+    for f in (xfile, wfile):
+        write_half(f, [1])
+    write_half(bfile, [0])
+    out.write_bytes(b"keep")
+    r = run(b2.CLI_PATH, [1, 1, 1, xfile, wfile, bfile, out])
+    assert r.returncode == 77 and out.read_bytes() == b"keep"
+
+
+@pytest.mark.gpu
+def test_file_gate_on_gpu(b2, tmp_path):
+    z = np.load(os.path.join(GOLDEN, "cli_gate_shapes.npz"))
+    meta = json.loads(bytes(z["meta"]).decode())
+    for case in meta:
+        m, k, n = case["m"], case["k"], case["n"]
+        x, w, b = oracle.lcg_fill(m * k, 303, 1.7), oracle.lcg_fill(n * k, 911, 0.21), oracle.lcg_fill(n, 409, 4.7)
+        files = [tmp_path / f"{m}-{k}-{n}-{s}.bin" for s in ("x", "w", "b")]
+        for f, v in zip(files, (x, w, b)):
+            write_half(f, v)
+        want = z[f"y_{m}_{k}_{n}"].view(np.float16)
+        tiles, tasks = oracle.plan_tasks(m, k, n)
+        outputs = {}
+        for mode in ("separate", "chain"):
+            out = tmp_path / f"{m}-{k}-{n}-{mode}-y.bin"
+            r = run(b2.CLI_PATH, [m, k, n, *files, out, mode, 3])
+            assert r.returncode == 0, r.stderr
+            got = np.frombuffer(out.read_bytes(), np.float16)
+            assert got.size == m * n
+            assert np.all(np.isfinite(got)) and np.max(np.abs(got.astype(np.float64) - want)) <= 0.002
+            subs = tiles * 3 if mode == "chain" else tasks * 3
+            mt = re.search(r"repeat=3 submits=(\d+) tasks=(\d+) PASS", r.stdout)
+            assert mt and (int(mt[1]), int(mt[2])) == (subs, tasks * 3), r.stdout
+            assert re.search(r"PASS launches=\d+", r.stdout)
+            outputs[mode] = out.read_bytes()
+        assert outputs["chain"] == outputs["separate"]

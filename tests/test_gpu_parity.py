@@ -187,3 +187,21 @@ def test_overflow_output_is_device_error(b2, gpu_fd):
     op = b2.Linear(gpu_fd, m, k, n, w, np.zeros(n, np.float16), post=b2.CO_LINEAR_HSIG)
     assert np.all(op.run(x) == 1.0)
     op.destroy()
+
+
+def test_hardsigmoid_every_fp16_preactivation_is_bitexact(b2, gpu_fd):
+    """One-hot X makes acc[m, n] = W[n, m] exactly, so the 65536 entries of W sweep every FP16
+    pre-activation (non-finite patterns replaced by 0) through bias + HardSigmoid + FP16 rounding.
+    Both accumulation modes must equal the oracle bit for bit."""
+    m = n = k = 256
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    bits[(bits & 0x7C00) == 0x7C00] = 0
+    w = bits.view(np.float16).reshape(n, k)
+    x = np.eye(m, k, dtype=np.float16)
+    b = np.zeros(n, np.float16)
+    want = oracle.linear("tile16", x, w, b, post=1)["y16"].view(np.uint16)
+    for acc in (b2.ACC_TILE16, b2.ACC_FP32):
+        op = b2.Linear(gpu_fd, m, k, n, w, b, post=b2.CO_LINEAR_HSIG, acc=acc)
+        y = op.run(x)
+        op.destroy()
+        assert np.array_equal(y.view(np.uint16), want), f"acc={acc}: {np.count_nonzero(y.view(np.uint16) != want)} differ"
