@@ -15,6 +15,9 @@ scaling, one process per GPU).
             finiteness scan, GEMM, status check, D2H of Y per step.
   roofline  GEMM kernel: 2*M*N*K FLOPs per launch / event-timed launch duration vs the measured
             dense 16-bit tensor peak; DRAM traffic per launch from the committed ncu summary.
+  sharded   M=8192, N=16384, K=16384 over all ranks with the total fixed (strong scaling):
+            column-parallel (no collective) and the K-split N=1024 variant (FP32 partials reduced
+            by NCCL all-reduce / reduce-scatter, then the epilogue).
   gemv      M=1 decode projections of a SmolLM-135M-shaped layer (HBM GB/s per launch, weights
             rotated over > 4x L2).
   cpu_baseline  the oracle's restatement of the reference arithmetic (per-256-K FP16 running
@@ -181,6 +184,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-gemv", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
@@ -286,6 +290,11 @@ def main():
     b2.lib().b2_host_free(hx)
     b2.lib().b2_host_free(hy)
 
+    # ---------------------------------------------------------------- M=8192,N=16384,K=16384 (all ranks)
+    shard = None
+    if not args.no_sharded:
+        shard = bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup, steps)
+
     # ---------------------------------------------------------------- GEMV (rank 0, N=1 only)
     gemv = None
     if rank == 0 and world == 1 and not args.no_gemv:
@@ -313,6 +322,8 @@ def main():
             "clocks": clocks.summary(),
             "spot_check": {"rows": int(rows.numel()), "worst_err_over_tol_vs_fp64": worst},
         }
+        if shard:
+            line["sharded"] = shard
         if gemv:
             line["gemv"] = gemv
         if world == 1 and not args.no_cpu:
@@ -323,6 +334,128 @@ def main():
         dist.destroy_process_group()
     if line:
         print(json.dumps(line), flush=True)
+
+
+def _timed_steps(torch, dist, world, stream, fn, warmup, steps, flush=None):
+    """Mean device ms of `fn` over `steps` (per-step CUDA events on `stream`; an optional L2 flush
+    between steps, outside the events), max over ranks."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    pairs = []
+    for _ in range(steps):
+        if flush is not None:
+            flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        fn()
+        e.record(stream)
+        pairs.append((s, e))
+    torch.cuda.synchronize()
+    ms = sum(s.elapsed_time(e) for s, e in pairs) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup, steps):
+    """Large sharded Linear M=8192, N=16384, K=16384 (X~N(0,1), W~N(0,1/K), no bias, FP32 accumulate)
+    over all ranks with the total work fixed (strong scaling): column-parallel over N with no
+    collective, and the K-split variant N=1024 (FP32 partial -> NCCL all-reduce or reduce-scatter
+    over NVLink -> bias/activation epilogue). Every rank runs every step; max over ranks."""
+    import numpy as np
+    import oracle
+    sharded = importlib.import_module("rockchip-npu-notes_b200.sharded")
+    m, n, k, n_ks = 8192, 16384, 16384, 1024
+    l2 = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
+    flush = torch.empty(2 * l2 // 4, dtype=torch.float32, device="cuda")
+    out = {}
+    gen = torch.Generator(device="cuda")
+
+    def w_rows(n0, n1, seed):
+        """Rows [n0, n1) of a W whose 256-row blocks are seeded by block index (rank-independent)."""
+        blocks = []
+        for b0 in range(n0 - n0 % 256, n1, 256):
+            gen.manual_seed(seed + b0 // 256)
+            blk = torch.randn(256, k, device="cuda", generator=gen) / k ** 0.5
+            blocks.append(blk[max(n0 - b0, 0):min(n1 - b0, 256)].half())
+        return torch.cat(blocks).cpu().numpy()
+
+    gen.manual_seed(77)
+    x = torch.randn(m, k, device="cuda", generator=gen).half()
+    torch.cuda.synchronize()
+
+    # ---- column-parallel: rank r owns W[n0:n1], writes Y[:, n0:n1]; X replicated
+    col = sharded.ColumnShard(fd, 1, n, k, lambda a, b: w_rows(a, b, 9000), None, world, rank)
+    cols = col.n1 - col.n0
+    y = torch.empty(m, max(cols, 8), device="cuda", dtype=torch.float16)
+    csteps = max(5, min(steps, 40))
+    ms = _timed_steps(torch, dist, world, stream,
+                      lambda: col.run_device(m, x.data_ptr(), k, y.data_ptr(), y.shape[1]), 3, csteps)
+    if b2.status(fd):
+        raise RuntimeError("device status raised in the column-parallel run")
+    flops = 2 * m * n * k
+    worst = 0.0
+    if cols:
+        c = min(cols, 512)
+        rows = torch.tensor([0, 2049, 5000, m - 1], device="cuda")
+        w_chk = w_rows(col.n0, col.n0 + c, 9000)
+        ref = oracle.linear("fp64", x[rows].cpu().numpy(), w_chk, None, post=0, want=("act",))["act"]
+        ok, worst = oracle.tolerance_ok(y[rows, :c].cpu().numpy(), ref)
+        if not ok:
+            raise RuntimeError(f"column-parallel output outside tolerance ({worst:.3f})")
+    col.destroy()
+    del y
+    tflops = flops / (ms * 1e-3) / 1e12
+    out["column_parallel"] = {
+        "m": m, "n": n, "k": k, "scaling": "strong", "collective": None, "ms_per_step": ms, "steps": csteps,
+        "tflops": tflops, "tflops_per_gpu": tflops / world, "frac_per_gpu": tflops / world / peak_tflops,
+        "columns_per_gpu": cols, "worst_err_over_tol_vs_fp64": worst,
+        "l2": "inputs larger than L2 (X 256 MiB + W and Y blocks)"}
+
+    # ---- K-split N=1024: rank r owns X[:, k0:k1], W[:, k0:k1]; FP32 partial reduced over NVLink
+    w_ks = w_rows(0, n_ks, 20000)
+    ks = sharded.KSplitLinear(fd, m, w_ks, None, world, rank, torch, dist)
+    kk = max(ks.k1 - ks.k0, 8)
+    xs = x[:, ks.k0:ks.k0 + kk].contiguous() if ks.k1 > ks.k0 else torch.zeros(m, 8, device="cuda").half()
+    y = torch.zeros(m, n_ks, device="cuda", dtype=torch.float16)
+    torch.cuda.synchronize()
+    flops = 2 * m * n_ks * k
+    collectives = ["all_reduce", "reduce_scatter"] if world > 1 else ["none"]
+    ksteps = max(10, min(steps, 100))
+    for coll in collectives:
+        name = "all_reduce" if coll == "none" else coll
+
+        def fn():
+            ks.forward(m, xs.data_ptr(), kk, y.data_ptr(), n_ks, collective=name)
+
+        with torch.cuda.stream(stream):
+            y.zero_()
+            ms = _timed_steps(torch, dist, world, stream, fn, 3, ksteps, flush=flush)
+        if b2.status(fd):
+            raise RuntimeError("device status raised in the K-split run")
+        r0, r1 = (0, m) if coll != "reduce_scatter" else ks.row_shard(m)
+        rows = torch.tensor(sorted({r0, (r0 + r1) // 2, r1 - 1}), device="cuda")
+        ref = oracle.linear("fp64", x[rows].cpu().numpy(), w_ks, None, post=0, want=("act",))["act"]
+        ok, worst = oracle.tolerance_ok(y[rows].cpu().numpy(), ref)
+        if not ok:
+            raise RuntimeError(f"K-split ({coll}) output outside tolerance ({worst:.3f})")
+        tflops = flops / (ms * 1e-3) / 1e12
+        partial_bytes = m * ks.ldp * 4
+        out[f"k_split_{coll}"] = {
+            "m": m, "n": n_ks, "k": k, "scaling": "strong", "collective": None if coll == "none" else coll,
+            "ms_per_step": ms, "steps": ksteps, "tflops": tflops, "tflops_per_gpu": tflops / world,
+            "frac_per_gpu": tflops / world / peak_tflops, "k_per_gpu": ks.k1 - ks.k0,
+            "fp32_partial_bytes": partial_bytes, "worst_err_over_tol_vs_fp64": worst,
+            "l2": "flushed between steps (write of 2x L2, outside the events)"}
+    ks.destroy()
+    del x, xs, y, flush
+    torch.cuda.empty_cache()
+    return out
 
 
 def bench_gemv(b2, fd, torch, stream, peak_gbs):

@@ -112,6 +112,16 @@ typedef struct {
 } b2_linear_info;
 int b2_linear_get_info(const b2_linear *, b2_linear_info *);
 
+/* ----------------------------------------------------------------------- multi-GPU partition */
+/* Shard `index` of `parts` over [0, total): contiguous ranges whose interior boundaries fall on
+ * multiples of `align` (256 keeps output tiles and 256-wide K tiles whole), sizes differing by
+ * at most one `align` block; trailing shards may be empty when total is small. This is the
+ * per-GPU work split of the column-parallel (N) and K-split layouts, replacing the reference's
+ * per-submit NPU core assignment (research/custom-ops/src/co_schedule.c). Returns 0 or
+ * ROCKET_E_SHAPE for bad arguments. */
+int b2_shard_range(unsigned long long total, unsigned parts, unsigned index, unsigned align,
+                   unsigned long long *begin, unsigned long long *end);
+
 /* ----------------------------------------------------------------------- fault injection */
 enum b2_fault {
     B2_FAULT_NONE = 0,

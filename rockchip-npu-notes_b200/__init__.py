@@ -161,6 +161,8 @@ SIGNATURES = {
     "b2_linear_epilogue_device": (_I, [_P, _U, _P, _Z, _P, _Z]),
     "b2_linear_get_info": (_I, [_P, ctypes.POINTER(B2LinearInfo)]),
     "b2_fault_inject": (None, [_I, _U]),
+    "b2_shard_range": (_I, [ctypes.c_ulonglong, _U, _U, _U, ctypes.POINTER(ctypes.c_ulonglong),
+                            ctypes.POINTER(ctypes.c_ulonglong)]),
 }
 
 _lib = None
@@ -240,6 +242,13 @@ def sm_count(fd):
 
 def fault_inject(kind, nth):
     lib().b2_fault_inject(int(kind), int(nth))
+
+
+def shard_range(total, parts, index, align=256):
+    """[begin, end) of shard `index` of `parts` (b2_shard_range)."""
+    b, e = ctypes.c_ulonglong(), ctypes.c_ulonglong()
+    check("b2_shard_range", lib().b2_shard_range(total, parts, index, align, ctypes.byref(b), ctypes.byref(e)))
+    return b.value, e.value
 
 
 def counters():

@@ -93,3 +93,19 @@ int co_linear_plan_tile(const co_linear_plan *p, unsigned index, co_linear_tile_
 int co_linear_plan_init(co_linear_plan *out, unsigned m, unsigned k, unsigned n, size_t budget) {
     return co_linear_plan_init_ex(out, m, k, n, 1, CO_LINEAR_HSIG, budget);
 }
+
+/* ------------------------------------------------------------------------------ GPU shards */
+int b2_shard_range(unsigned long long total, unsigned parts, unsigned index, unsigned align,
+                   unsigned long long *begin, unsigned long long *end) {
+    if (!begin || !end || !parts || index >= parts || !align) return ROCKET_E_SHAPE;
+    const unsigned long long blocks = (total + align - 1) / align;
+    const unsigned long long base = blocks / parts, extra = blocks % parts;
+    const unsigned long long b0 = index * base + (index < extra ? index : extra);
+    const unsigned long long nb = base + (index < extra ? 1 : 0);
+    unsigned long long lo = b0 * align, hi = (b0 + nb) * align;
+    if (lo > total) lo = total;
+    if (hi > total) hi = total;
+    *begin = lo;
+    *end = hi;
+    return 0;
+}
