@@ -259,6 +259,10 @@ def main():
     ok, worst = oracle.tolerance_ok(y0[rows].cpu().numpy(), ref)
     if not ok:
         raise RuntimeError(f"bench output outside tolerance (worst err/tol {worst:.3f})")
+    gi = sets[0][3].info()
+    kernel_desc = (f"tcgen05 persistent GEMM, {gi.tile_m}x{gi.tile_n} output tile per "
+                   f"{'CTA pair (cta_group::2)' if gi.tile_m == 256 else 'CTA'}, K step {gi.tile_k}, "
+                   f"{gi.stages}-stage TMA ring, {gi.grid} CTAs")
     for _, _, _, op in sets:
         op.destroy()
     del sets
@@ -308,7 +312,7 @@ def main():
             "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
             "config": {"workload": WORKLOAD, "m": M, "n_per_gpu": N_PER_GPU, "k": K,
-                       "accumulate": "fp32", "kernel": "tcgen05 persistent GEMM 128x256x64, 4 stages",
+                       "accumulate": "fp32", "kernel": kernel_desc,
                        "l2": "inputs larger than L2: 4 rotating X/W/Y sets of 96 MiB",
                        "parallelism": f"column-parallel x{world}, no collective"},
             "e2e": {"value": world * FLOPS_PER_GPU / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
@@ -345,21 +349,22 @@ def _timed_steps(torch, dist, world, stream, fn, warmup, steps, flush=None):
     if world > 1:
         dist.barrier()
     pairs = []
-    for _ in range(steps):
-        if flush is not None:
-            flush.zero_()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        fn()
-        e.record(stream)
-        pairs.append((s, e))
-    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        for _ in range(steps):
+            if flush is not None:
+                flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            fn()
+            e.record(stream)
+            pairs.append((s, e))
+        torch.cuda.synchronize()
     ms = sum(s.elapsed_time(e) for s, e in pairs) / steps
     if world > 1:
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    return ms
+    return ms, clocks.summary()
 
 
 def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup, steps):
@@ -394,8 +399,8 @@ def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup,
     cols = col.n1 - col.n0
     y = torch.empty(m, max(cols, 8), device="cuda", dtype=torch.float16)
     csteps = max(5, min(steps, 40))
-    ms = _timed_steps(torch, dist, world, stream,
-                      lambda: col.run_device(m, x.data_ptr(), k, y.data_ptr(), y.shape[1]), 3, csteps)
+    ms, clk = _timed_steps(torch, dist, world, stream,
+                           lambda: col.run_device(m, x.data_ptr(), k, y.data_ptr(), y.shape[1]), 3, csteps)
     if b2.status(fd):
         raise RuntimeError("device status raised in the column-parallel run")
     flops = 2 * m * n * k
@@ -414,7 +419,7 @@ def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup,
     out["column_parallel"] = {
         "m": m, "n": n, "k": k, "scaling": "strong", "collective": None, "ms_per_step": ms, "steps": csteps,
         "tflops": tflops, "tflops_per_gpu": tflops / world, "frac_per_gpu": tflops / world / peak_tflops,
-        "columns_per_gpu": cols, "worst_err_over_tol_vs_fp64": worst,
+        "columns_per_gpu": cols, "worst_err_over_tol_vs_fp64": worst, "clocks_rank0": clk,
         "l2": "inputs larger than L2 (X 256 MiB + W and Y blocks)"}
 
     # ---- K-split N=1024: rank r owns X[:, k0:k1], W[:, k0:k1]; FP32 partial reduced over NVLink
@@ -435,7 +440,7 @@ def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup,
 
         with torch.cuda.stream(stream):
             y.zero_()
-            ms = _timed_steps(torch, dist, world, stream, fn, 3, ksteps, flush=flush)
+            ms, clk = _timed_steps(torch, dist, world, stream, fn, 3, ksteps, flush=flush)
         if b2.status(fd):
             raise RuntimeError("device status raised in the K-split run")
         r0, r1 = (0, m) if coll != "reduce_scatter" else ks.row_shard(m)
@@ -450,7 +455,7 @@ def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup,
             "m": m, "n": n_ks, "k": k, "scaling": "strong", "collective": None if coll == "none" else coll,
             "ms_per_step": ms, "steps": ksteps, "tflops": tflops, "tflops_per_gpu": tflops / world,
             "frac_per_gpu": tflops / world / peak_tflops, "k_per_gpu": ks.k1 - ks.k0,
-            "fp32_partial_bytes": partial_bytes, "worst_err_over_tol_vs_fp64": worst,
+            "fp32_partial_bytes": partial_bytes, "worst_err_over_tol_vs_fp64": worst, "clocks_rank0": clk,
             "l2": "flushed between steps (write of 2x L2, outside the events)"}
     ks.destroy()
     del x, xs, y, flush
@@ -458,39 +463,67 @@ def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup,
     return out
 
 
+def _eager_and_graph_ms(torch, stream, launch, reps):
+    """Mean ms per call of launch(i), i = 0..reps-1, issued eagerly and as one replayed CUDA graph
+    (a decode step runs as a graph: no host launch overhead between kernels)."""
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for i in range(reps):
+        launch(i)
+    e.record(stream)
+    e.synchronize()
+    eager = s.elapsed_time(e) / reps
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(reps):
+            launch(i)
+    best = None
+    with torch.cuda.stream(stream):          # replay() launches on the current stream
+        g.replay()
+        stream.synchronize()
+        for _ in range(3):
+            s.record(stream)
+            g.replay()
+            e.record(stream)
+            e.synchronize()
+            t = s.elapsed_time(e) / reps
+            best = t if best is None else min(best, t)
+    del g
+    return eager, best
+
+
 def bench_gemv(b2, fd, torch, stream, peak_gbs):
-    """M=1 projections of a SmolLM-135M-shaped layer, weights rotated over >= 4x L2."""
+    """M=1 projections of a SmolLM-135M-shaped layer, weights rotated over >= 4x L2; each timed as
+    eager launches and as a replayed CUDA graph of the same launches (the headline per projection)."""
     import numpy as np
     l2 = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
-    out = {"l2_bytes": l2, "projections": {}}
+    out = {"l2_bytes": l2, "timing": "CUDA graph of back-to-back launches (us, gb_s); eager_us beside it",
+           "projections": {}}
     layer_bytes, layer_ms = 0, 0.0
     gen = torch.Generator(device="cuda").manual_seed(7)
     for name, n, k in GEMV_LAYER:
         wbytes = 2 * n * k
-        copies = max(2, -(-4 * l2 // wbytes))
-        copies = min(copies, 2048)
-        ops = []
+        copies = min(2048, max(2, -(-4 * l2 // wbytes)))
         w_host = (np.random.default_rng(n * k).standard_normal((n, k)) * 0.02).astype(np.float16)
         # one operator per weight copy (same values, distinct HBM buffers): copies*bytes >= 4x L2
-        for _ in range(copies):
-            ops.append(b2.Linear(fd, 1, k, n, w_host, None, post=b2.CO_LINEAR_NONE, acc=b2.ACC_FP32, compat=False))
+        ops = [b2.Linear(fd, 1, k, n, w_host, None, post=b2.CO_LINEAR_NONE, acc=b2.ACC_FP32, compat=False)
+               for _ in range(copies)]
         x = torch.randn(1, k, device="cuda", generator=gen).half()
         y = torch.empty(1, n, device="cuda", dtype=torch.float16)
-        reps = max(64, len(ops) * 4)
-        for i in range(len(ops)):
-            ops[i].run_device(1, x.data_ptr(), k, y.data_ptr(), n)
+        torch.cuda.synchronize()
+        for op in ops:
+            op.run_device(1, x.data_ptr(), k, y.data_ptr(), n)
         b2.sync(fd)
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        for i in range(reps):
-            ops[i % len(ops)].run_device(1, x.data_ptr(), k, y.data_ptr(), n)
-        e.record(stream)
-        e.synchronize()
-        ms = s.elapsed_time(e) / reps
+        reps = max(64, min(4 * copies, 2048))
+        eager, ms = _eager_and_graph_ms(
+            torch, stream, lambda i: ops[i % copies].run_device(1, x.data_ptr(), k, y.data_ptr(), n), reps)
+        if b2.status(fd):
+            raise RuntimeError(f"device status raised in the {name} GEMV")
         nbytes = 2 * n * k + 2 * k + 2 * n
         gbs = nbytes / (ms * 1e-3) / 1e9
         out["projections"][name] = {"n": n, "k": k, "bytes": nbytes, "us": ms * 1e3, "gb_s": gbs,
-                                    "frac": gbs / peak_gbs, "weight_copies": len(ops)}
+                                    "frac": gbs / peak_gbs, "eager_us": eager * 1e3, "weight_copies": copies,
+                                    "kernel": "streamed (bulk-copy ring, mma.sync)" if k <= 2048 else "per-lane"}
         if name != "lm_head":
             layer_bytes += nbytes
             layer_ms += ms
@@ -498,7 +531,46 @@ def bench_gemv(b2, fd, torch, stream, peak_gbs):
             op.destroy()
     out["layer_7_projections"] = {"bytes": layer_bytes, "us": layer_ms * 1e3,
                                   "gb_s": layer_bytes / (layer_ms * 1e-3) / 1e9,
-                                  "frac": layer_bytes / (layer_ms * 1e-3) / 1e9 / peak_gbs}
+                                  "frac": layer_bytes / (layer_ms * 1e-3) / 1e9 / peak_gbs,
+                                  "launches": 7}
+
+    # the same 7 projections as ONE grouped launch (b2_linear_group_run_device); q/k/v/gate/up read
+    # one shared input, o and down their own; weight sets rotated over >= 4x L2
+    layer = [(name, n, k) for name, n, k in GEMV_LAYER if name != "lm_head"]
+    set_bytes = sum(2 * n * k for _, n, k in layer)
+    copies = min(256, max(2, -(-4 * l2 // set_bytes)))
+    rng = np.random.default_rng(5)
+    w_host = {name: (rng.standard_normal((n, k)) * 0.02).astype(np.float16) for name, n, k in layer}
+    sets = [[b2.Linear(fd, 1, k, n, w_host[name], None, post=b2.CO_LINEAR_NONE, acc=b2.ACC_FP32, compat=False)
+             for name, n, k in layer] for _ in range(copies)]
+    xin = {"h": torch.randn(1, 576, device="cuda", generator=gen).half(),
+           "o": torch.randn(1, 576, device="cuda", generator=gen).half(),
+           "f": torch.randn(1, 1536, device="cuda", generator=gen).half()}
+    src = {"q": "h", "k": "h", "v": "h", "gate": "h", "up": "h", "o": "o", "down": "f"}
+    ys = [torch.empty(1, n, device="cuda", dtype=torch.float16) for _, n, _ in layer]
+    xp = [xin[src[name]].data_ptr() for name, _, _ in layer]
+    ldx = [k for _, _, k in layer]
+    yp = [y.data_ptr() for y in ys]
+    ldy = [n for _, n, _ in layer]
+    torch.cuda.synchronize()
+    for ops in sets:
+        b2.group_run_device(ops, 1, xp, ldx, yp, ldy)
+    b2.sync(fd)
+    reps = max(64, 4 * copies)
+    launches0 = b2.counters()["launches"]
+    b2.group_run_device(sets[0], 1, xp, ldx, yp, ldy)
+    group_launches = b2.counters()["launches"] - launches0
+    eager, ms = _eager_and_graph_ms(torch, stream, lambda i: b2.group_run_device(sets[i % copies], 1, xp, ldx, yp, ldy),
+                                    reps)
+    if b2.status(fd):
+        raise RuntimeError("device status raised in the grouped GEMV run")
+    gbytes = sum(2 * n * k + 2 * k + 2 * n for _, n, k in layer)
+    out["layer_7_projections_grouped"] = {"bytes": gbytes, "us": ms * 1e3, "gb_s": gbytes / (ms * 1e-3) / 1e9,
+                                          "frac": gbytes / (ms * 1e-3) / 1e9 / peak_gbs, "eager_us": eager * 1e3,
+                                          "launches": group_launches, "weight_sets": copies}
+    for ops in sets:
+        for op in ops:
+            op.destroy()
     out["peak_gbs"] = peak_gbs
     return out
 

@@ -101,6 +101,22 @@ int b2_linear_epilogue_device(b2_linear *, unsigned m, const float *partial, siz
 #define B2_NOALLOC_SCRATCH_BYTES (8u << 20)
 int b2_linear_run_device_noalloc(b2_linear *, unsigned m, const void *x, size_t ldx, void *y, size_t ldy);
 
+/* Grouped small-M run: Y_i[m, ldy_i] = act_i(X_i W_i^T + b_i) for `count` independent operators on
+ * the same handle (same GPU), for example the Q/K/V or gate/up projections of one decoder layer at
+ * decode time. It replaces the projection step of the reference's multi-output graph call
+ * (research/custom-ops/src/co_decoder.c:128-129, co_graph_run_many in
+ * research/custom-ops/include/co_graph.h:77), which produces Q, K and V from one input.
+ * Operators with m <= 2 and k <= 2048 share ONE kernel launch (the weight-streaming GEMV); any
+ * other member runs as its own b2_linear_run_device launch. Each result is bit-identical to that
+ * operator's own b2_linear_run_device (CO_SEPARATE operators are finished in the same launch with
+ * the same arithmetic as their separate epilogue). X_i and Y_i follow b2_linear_run_device's
+ * rules; the X_i may alias (a shared input). Asynchronous on the handle's stream.
+ * 1 <= count <= B2_GROUP_MAX, else ROCKET_E_SHAPE; operators on different handles: ROCKET_E_SHAPE. */
+#define B2_GROUP_MAX 16u
+int b2_linear_group_run_device(b2_linear *const *ops, unsigned count, unsigned m,
+                               const void *const *x, const size_t *ldx, void *const *y,
+                               const size_t *ldy);
+
 typedef struct {
     unsigned m, k, n;
     unsigned kernel;             /* 0 = tcgen05 GEMM, 1 = GEMV (small M) */

@@ -163,6 +163,8 @@ SIGNATURES = {
     "b2_fault_inject": (None, [_I, _U]),
     "b2_shard_range": (_I, [ctypes.c_ulonglong, _U, _U, _U, ctypes.POINTER(ctypes.c_ulonglong),
                             ctypes.POINTER(ctypes.c_ulonglong)]),
+    "b2_linear_group_run_device": (_I, [ctypes.POINTER(_P), _U, _U, ctypes.POINTER(_P), ctypes.POINTER(_Z),
+                                        ctypes.POINTER(_P), ctypes.POINTER(_Z)]),
 }
 
 _lib = None
@@ -249,6 +251,15 @@ def shard_range(total, parts, index, align=256):
     b, e = ctypes.c_ulonglong(), ctypes.c_ulonglong()
     check("b2_shard_range", lib().b2_shard_range(total, parts, index, align, ctypes.byref(b), ctypes.byref(e)))
     return b.value, e.value
+
+
+def group_run_device(ops, m, x_ptrs, ldx, y_ptrs, ldy):
+    """b2_linear_group_run_device over Linear objects `ops` (device pointers, per-op pitches)."""
+    n = len(ops)
+    arr = lambda t, v: (t * n)(*v)
+    check("b2_linear_group_run_device",
+          lib().b2_linear_group_run_device(arr(_P, [o.h for o in ops]), n, m, arr(_P, x_ptrs), arr(_Z, ldx),
+                                           arr(_P, y_ptrs), arr(_Z, ldy)))
 
 
 def counters():

@@ -78,6 +78,11 @@ typedef struct {
  * *launches receives the number of kernels launched. */
 int b2d_linear(b2_dev *, const b2k_linear *, unsigned *launches);
 int b2d_linear_config(b2_dev *, const b2k_linear *, b2k_config *);
+/* Runs `count` (<= B2D_GROUP_MAX) independent fused Linears with the same m. Those the streamed
+ * small-M kernel serves (m <= 2, k <= 2048) share one launch; any other runs as b2d_linear.
+ * Every op must have fused = 1 and raw_only = 0. */
+#define B2D_GROUP_MAX 16u
+int b2d_linear_group(b2_dev *, const b2k_linear *ops, unsigned count, unsigned *launches);
 /* y = act(partial + bias) with the same arithmetic as the fused epilogue of mode `acc`. */
 int b2d_epilogue(b2_dev *, unsigned m, unsigned n, const float *partial, size_t ldp,
                  const void *bias, int post, int acc, void *y, size_t ldy);

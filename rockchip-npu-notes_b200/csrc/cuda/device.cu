@@ -196,7 +196,8 @@ int b2d_linear_config(b2_dev *d, const b2k_linear *a, b2k_config *cfg) {
         cfg->tile_m = a->m;
         cfg->tile_n = 8;
         cfg->tile_k = 256;
-        cfg->grid = b2::gemv::grid_for((int)a->n, d->sm_count);
+        cfg->grid = b2::gemv::grid_for((int)a->m, (int)a->n, (int)a->k, (long long)a->ldw, d->sm_count);
+        cfg->stages = b2::gemv::streamed((int)a->m, (int)a->k) ? 12 : 0;
     } else {
         cfg->kernel = 0;
         b2::gemm::config_for((int)a->m, (int)a->n, d->sm_count, &cfg->tile_m, &cfg->tile_n, &cfg->stages);
@@ -206,13 +207,16 @@ int b2d_linear_config(b2_dev *d, const b2k_linear *a, b2k_config *cfg) {
     return 0;
 }
 
+static bool linear_args_ok(const b2k_linear *a) {
+    return a->m && a->n && a->k && a->x && a->w && a->ldx % 8 == 0 && a->ldw % 8 == 0 && a->ldx >= a->k &&
+           a->ldw >= a->k && aligned16(a->x) && aligned16(a->w) && a->m <= (1u << 24) && a->n <= (1u << 24) &&
+           a->k <= (1u << 24);
+}
+
 int b2d_linear(b2_dev *d, const b2k_linear *a, unsigned *launches) {
     *launches = 0;
     if (!set_device(d)) return ROCKET_E_DEVICE;
-    if (!a->m || !a->n || !a->k || !a->x || !a->w || a->ldx % 8 || a->ldw % 8 || a->ldx < a->k ||
-        a->ldw < a->k || !aligned16(a->x) || !aligned16(a->w) || a->m > (1u << 24) || a->n > (1u << 24) ||
-        a->k > (1u << 24))
-        return ROCKET_E_SHAPE;
+    if (!linear_args_ok(a)) return ROCKET_E_SHAPE;
     const bool fold = a->acc == 0 && !a->raw_only;
     int out_mode;
     if (a->raw_only) out_mode = b2::gemm::OUT_RAW32;
@@ -261,6 +265,43 @@ int b2d_linear(b2_dev *d, const b2k_linear *a, unsigned *launches) {
     e = b2::aux::epilogue(ep, d->stream, d->sm_count);
     if (e != cudaSuccess) return rc_of(e);
     *launches = 2;
+    return 0;
+}
+
+int b2d_linear_group(b2_dev *d, const b2k_linear *ops, unsigned count, unsigned *launches) {
+    *launches = 0;
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (!ops || !count || count > B2D_GROUP_MAX) return ROCKET_E_SHAPE;
+    for (unsigned i = 0; i < count; ++i) {
+        const b2k_linear *a = &ops[i];
+        if (!linear_args_ok(a) || a->m != ops[0].m || !a->fused || a->raw_only || !a->y || a->ldy < a->n)
+            return ROCKET_E_SHAPE;
+    }
+    b2::gemv::Group g = {};
+    g.M = (int)ops[0].m;
+    g.flags = d->flags_dev;
+    for (unsigned i = 0; i < count; ++i) {
+        const b2k_linear *a = &ops[i];
+        if (!b2::gemv::streamed((int)a->m, (int)a->k)) continue;
+        g.prob[g.count++] = b2::gemv::Problem{static_cast<const __half *>(a->x), (long long)a->ldx,
+                                              static_cast<const __half *>(a->w), (long long)a->ldw,
+                                              static_cast<const __half *>(a->bias), static_cast<__half *>(a->y),
+                                              (long long)a->ldy, nullptr, 0, (int)a->n, (int)a->k,
+                                              b2::gemv::OUT_FINAL, a->post, a->acc == 0 ? 1 : 0, 0, 0, 0, 0};
+    }
+    if (g.count) {
+        unsigned l = 0;
+        const cudaError_t e = b2::gemv::launch_group(g, d->stream, d->sm_count, nullptr, &l);
+        *launches = l;
+        if (e != cudaSuccess) return rc_of(e);
+    }
+    for (unsigned i = 0; i < count; ++i) {
+        if (b2::gemv::streamed((int)ops[i].m, (int)ops[i].k)) continue;
+        unsigned l = 0;
+        const int rc = b2d_linear(d, &ops[i], &l);
+        *launches += l;
+        if (rc) return rc;
+    }
     return 0;
 }
 

@@ -7,7 +7,7 @@
 // with one launch. Two variants share the code (template CG = CTA group):
 //   CG=2  a cluster of two CTAs on a TPC computes a 256x256 output tile with the 2-SM UMMA
 //         (tcgen05.mma.cta_group::2, M=256 N=256 K=16): each CTA stages its own 128 rows of X and
-//         128 rows of W per 64-wide K block (32 KB, 6-stage ring), so per SM the shared-memory
+//         128 rows of W per 64-wide K block (32 KB, 7-stage ring), so per SM the shared-memory
 //         and L2 traffic per FLOP is two thirds of the single-SM tile. Used for M > 128.
 //   CG=1  one CTA computes a 128x256 tile with tcgen05.mma.cta_group::1 (48 KB, 4-stage ring).
 // Roles per CTA (384 threads):
@@ -35,6 +35,7 @@
 
 #include "common.cuh"
 #include "gemm_sm100.h"
+#include "mbarrier.cuh"
 
 namespace b2 {
 namespace gemm {
@@ -42,7 +43,6 @@ namespace gemm {
 constexpr int BK = 64;
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 128 + EPI_WARPS * 32;
-constexpr uint64_t WAIT_LIMIT_NS = 1000000000ull;   // 1 s per wait; a healthy wait is microseconds
 constexpr uint32_t SMEM_LIMIT = 232448;              // dynamic shared memory per CTA on sm_100
 constexpr int TILE_N = 256;                          // output columns per tile
 
@@ -65,9 +65,6 @@ struct Cfg {
 };
 
 // ----------------------------------------------------------------------------- PTX wrappers
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -82,64 +79,9 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Waits for the phase of parity `parity` to complete. Returns false when the CTA is aborting or
-// the wait exceeded WAIT_LIMIT_NS (then the timeout flag is raised and the CTA aborts).
-__device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                                           unsigned *flags) {
-    if (mbar_try_wait(bar, parity)) return true;
-    uint64_t t0 = 0;
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 0) {   // the abort flag and the clock are checked every 256 polls
-            if (*abort_flag) return false;
-            const uint64_t t = global_ns();
-            if (!t0) {
-                t0 = t;
-            } else if (t - t0 > WAIT_LIMIT_NS) {
-                *abort_flag = 1;
-                raise_flag(flags, FLAG_TIMEOUT);
-                return false;
-            }
-        }
-    }
-}
-// Bounded wait used only while draining after an abort (ignores the abort flag).
-__device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity) {
-    const uint64_t t0 = global_ns();
-    while (!mbar_try_wait(bar, parity))
-        if (global_ns() - t0 > WAIT_LIMIT_NS) return;
-}
-
 template <int CG>
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1) {
     if constexpr (CG == 2) {

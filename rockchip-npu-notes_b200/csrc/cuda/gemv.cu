@@ -1,25 +1,105 @@
 // gemv.cu -- memory-bound small-M Linear (M <= 8): y[r, n] = act(x[r, :] . W[n, :] + b[n]).
 //
 // The reference runs M=1 decode through the same NPU matmul with the row count padded to 12
-// (research/scheduling/GEMM-GEMV-CONCURRENCY.md:24-30 in the reference project); on B200 the
-// M<=8 case is a weight stream: each warp owns one W row at a time and every lane reads 16 bytes
-// (8 FP16) per 256-element K tile with read-only, L1-bypassing loads, so one K tile of the
-// reference's FP16-K-TILING scheme is exactly one load per lane. The x rows are re-read from
-// L1/L2 (tiny). Per-tile FP16 folding (tile-16 mode) reduces each tile across the warp with
-// shuffles before the fold; FP32 mode reduces once per row. Several tiles' loads are issued
-// before any arithmetic to keep enough bytes in flight to saturate HBM.
+// (research/scheduling/GEMM-GEMV-CONCURRENCY.md:24-30 in the reference project) and produces a
+// decoder layer's Q/K/V projections from one input in one graph call
+// (research/custom-ops/src/co_decoder.c:128-129). On B200 the small-M case is a weight stream,
+// served by two kernels with the same per-element arithmetic:
+//
+// Streamed kernel (M <= 8, K <= 2048: every decode projection of a small decoder):
+//   one persistent CTA per SM. Lanes 0-11 of warp 0 stream the weights with cp.async.bulk into
+//   12 slots of 16 KB shared memory (lane s feeds slot s), each slot a block of whole W rows --
+//   rows [n0, n0 + R) of a row-major [N, ldw] matrix are one contiguous byte range, so one bulk
+//   copy moves them; up to 192 KB are in flight per SM. Consumer warp s takes the units landing
+//   in slot s and computes them on the tensor cores (below). The launch's x rows are copied once per CTA into a 32 KB shared table (problems
+//   that share an input share the entry), filled by the consumer warps while the first weights
+//   are in flight. A launch covers a group of up to GROUP_MAX independent projections (same M):
+//   units of R rows from all of them are spread over the CTAs.
+// Per-lane-load kernel (the other M <= 8 shapes): each warp owns one W row at a time and every
+//   lane reads 16 bytes per 256-element K tile with read-only, L1-bypassing loads; several tiles'
+//   loads are issued before any arithmetic. The grid is the number of co-resident CTAs.
+//
+// Arithmetic: the per-lane-load kernel sums each lane's 8 products with fmaf in element order,
+// accumulates over K tiles and reduces across the warp; the streamed kernel sums on the tensor
+// cores (mma.sync m16n8k16, FP16 inputs, FP32 accumulation: W rows as A, up to 8 x rows as B, so a
+// batch of 8 costs what one x row does). Both accumulate in FP32 (tile-16 mode: per 256-K tile,
+// then the FP16 fold of the reference's FP16-K-TILING) and finish with the bias/activation of
+// common.cuh; they agree with each other and the oracle within the operator's tolerance, and one
+// x row's result never depends on the other rows of the batch.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "common.cuh"
 #include "gemv.h"
+#include "mbarrier.cuh"
 
 namespace b2 {
 namespace gemv {
 
-constexpr int THREADS = 256;
-constexpr int UNROLL = 4;
+namespace {
+
+// ----------------------------------------------------------------------------- shared arithmetic
+// Dot product of 8 FP16 weights with 8 x values (as FP32); elements at index >= valid contribute
+// nothing.
+__device__ __forceinline__ float dot8(uint4 w, const float (&xv)[8], int valid) {
+    const __half2 *hw = reinterpret_cast<const __half2 *>(&w);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 fw = __half22float2(hw[i]);
+        if (2 * i < valid) s = fmaf(fw.x, xv[2 * i], s);
+        if (2 * i + 1 < valid) s = fmaf(fw.y, xv[2 * i + 1], s);
+    }
+    return s;
+}
+
+__device__ __forceinline__ void widen8(uint4 v, float (&out)[8]) {
+    const __half2 *h = reinterpret_cast<const __half2 *>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        out[2 * i] = f.x;
+        out[2 * i + 1] = f.y;
+    }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Lane r writes output row r of column n. Returns true if a final FP16 output is not finite.
+template <int MR>
+__device__ __forceinline__ bool finish_row(int M, int lane, int n, int out_mode, int fold, int post,
+                                           const __half *bias, __half *y, long long ldy, float *partial,
+                                           long long ldp, const float (&acc)[MR], const float (&run)[MR]) {
+    const bool has_bias = bias != nullptr;
+    const float b = has_bias ? __half2float(bias[n]) : 0.0f;
+    bool bad = false;
+#pragma unroll
+    for (int r = 0; r < MR; ++r) {
+        if (r >= M) break;
+        const float total = fold ? run[r] : warp_sum(acc[r]);
+        if (lane != r) continue;
+        if (out_mode == OUT_RAW32) {
+            partial[(size_t)r * ldp + n] = total;
+        } else if (out_mode == OUT_RAW16) {
+            y[(size_t)r * ldy + n] = __float2half_rn(total);
+        } else {
+            const float v = fold ? finish_tile16(total, b, has_bias, post) : finish_fp32(total, b, post);
+            const __half h = __float2half_rn(v);
+            bad |= half_nonfinite(h);
+            y[(size_t)r * ldy + n] = h;
+        }
+    }
+    return bad;
+}
+
+// ----------------------------------------------------------------------------- per-lane-load kernel
+constexpr int D_THREADS = 256;
+constexpr int D_UNROLL = 4;
 
 __device__ __forceinline__ uint4 ld_stream(const __half *p) {
     uint4 v;
@@ -29,47 +109,26 @@ __device__ __forceinline__ uint4 ld_stream(const __half *p) {
     return v;
 }
 
-// Dot product of 8 FP16 pairs; elements at index >= valid contribute nothing.
-__device__ __forceinline__ float dot8(uint4 a, uint4 b, int valid) {
-    const __half2 *ha = reinterpret_cast<const __half2 *>(&a);
-    const __half2 *hb = reinterpret_cast<const __half2 *>(&b);
-    float s = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 fa = __half22float2(ha[i]), fb = __half22float2(hb[i]);
-        if (2 * i < valid) s = fmaf(fa.x, fb.x, s);
-        if (2 * i + 1 < valid) s = fmaf(fa.y, fb.y, s);
-    }
-    return s;
-}
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
 template <int MR>
-__global__ void __launch_bounds__(THREADS) gemv_kernel(const Params p) {
+__global__ void __launch_bounds__(D_THREADS) gemv_direct_kernel(const Params p) {
     const int lane = threadIdx.x & 31;
-    const int warps = (gridDim.x * THREADS) >> 5;
+    const int warps = (gridDim.x * D_THREADS) >> 5;
     const int nchunk = (p.K + 255) >> 8;
-    const bool has_bias = p.bias != nullptr;
     bool bad = false;
-    for (int n = (blockIdx.x * THREADS + threadIdx.x) >> 5; n < p.N; n += warps) {
+    for (int n = (blockIdx.x * D_THREADS + threadIdx.x) >> 5; n < p.N; n += warps) {
         const __half *wrow = p.w + (size_t)n * p.ldw;
         float acc[MR], run[MR];
 #pragma unroll
         for (int r = 0; r < MR; ++r) acc[r] = run[r] = 0.0f;
-        for (int c0 = 0; c0 < nchunk; c0 += UNROLL) {
-            uint4 wv[UNROLL];
+        for (int c0 = 0; c0 < nchunk; c0 += D_UNROLL) {
+            uint4 wv[D_UNROLL];
 #pragma unroll
-            for (int u = 0; u < UNROLL; ++u) {
+            for (int u = 0; u < D_UNROLL; ++u) {
                 const int k8 = (c0 + u) * 256 + lane * 8;
                 wv[u] = (c0 + u < nchunk && k8 < p.K) ? ld_stream(wrow + k8) : make_uint4(0, 0, 0, 0);
             }
 #pragma unroll
-            for (int u = 0; u < UNROLL; ++u) {
+            for (int u = 0; u < D_UNROLL; ++u) {
                 const int c = c0 + u;
                 if (c >= nchunk) break;                       // uniform across the warp
                 const int k8 = c * 256 + lane * 8;
@@ -77,49 +136,415 @@ __global__ void __launch_bounds__(THREADS) gemv_kernel(const Params p) {
 #pragma unroll
                 for (int r = 0; r < MR; ++r) {
                     if (r >= p.M) break;
-                    const uint4 xv = valid ? __ldg(reinterpret_cast<const uint4 *>(p.x + (size_t)r * p.ldx + k8))
-                                           : make_uint4(0, 0, 0, 0);
+                    float xv[8];
+                    widen8(valid ? __ldg(reinterpret_cast<const uint4 *>(p.x + (size_t)r * p.ldx + k8))
+                                 : make_uint4(0, 0, 0, 0),
+                           xv);
                     const float s = dot8(wv[u], xv, valid);
                     if (p.fold) run[r] = fold16(run[r], warp_sum(s), c == 0);
                     else acc[r] += s;
                 }
             }
         }
-        const float b = has_bias ? __half2float(p.bias[n]) : 0.0f;
-#pragma unroll
-        for (int r = 0; r < MR; ++r) {
-            if (r >= p.M) break;
-            const float total = p.fold ? run[r] : warp_sum(acc[r]);
-            if (lane != r) continue;
-            if (p.out_mode == OUT_RAW32) {
-                p.partial[(size_t)r * p.ldp + n] = total;
-            } else if (p.out_mode == OUT_RAW16) {
-                p.y[(size_t)r * p.ldy + n] = __float2half_rn(total);
-            } else {
-                const float v = p.fold ? finish_tile16(total, b, has_bias, p.post) : finish_fp32(total, b, p.post);
-                const __half h = __float2half_rn(v);
-                bad |= half_nonfinite(h);
-                p.y[(size_t)r * p.ldy + n] = h;
-            }
-        }
+        bad |= finish_row<MR>(p.M, lane, n, p.out_mode, p.fold, p.post, p.bias, p.y, p.ldy, p.partial, p.ldp, acc,
+                              run);
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) raise_flag(p.flags, FLAG_NONFINITE_OUTPUT);
 }
 
-unsigned grid_for(int N, int sm_count) {
-    const long long need = ((long long)N + (THREADS / 32) - 1) / (THREADS / 32);
-    const long long cap = (long long)sm_count * 8;
+// ----------------------------------------------------------------------------- streamed kernel
+constexpr int S_CONSUMERS = 12;                     // consumer warps
+constexpr int S_SLOTS_PER_CONSUMER = 1;             // a slot refills while its consumer works on the other
+constexpr int S_STAGES = S_CONSUMERS * S_SLOTS_PER_CONSUMER;   // one producer lane each: <= 32
+constexpr int S_THREADS = 32 * (1 + S_CONSUMERS);
+constexpr uint32_t S_STAGE_BYTES = (196608u / S_STAGES) & ~127u;
+static_assert(S_STAGES <= 32, "one producer lane per slot");
+struct Meta {
+    int prob, row0, rows, pad;   // prob < 0: no more units
+};
+// ring | x table | meta | full and empty barriers | abort flag | the group's problems (copied
+// from the kernel parameter once per CTA: dynamically indexed parameter reads are slow)
+constexpr uint32_t S_X_OFFSET = S_STAGES * S_STAGE_BYTES;
+constexpr uint32_t S_META_OFFSET = S_X_OFFSET + STREAM_X_BYTES;
+constexpr uint32_t S_BAR_OFFSET = S_META_OFFSET + S_STAGES * sizeof(Meta);
+constexpr uint32_t S_ABORT_OFFSET = S_BAR_OFFSET + 2 * S_STAGES * 8;
+constexpr uint32_t S_PROB_OFFSET = S_ABORT_OFFSET + 16;
+constexpr uint32_t S_SMEM_BYTES = S_PROB_OFFSET + GROUP_MAX * sizeof(Problem);
+static_assert(S_BAR_OFFSET % 8 == 0 && S_PROB_OFFSET % 8 == 0 && sizeof(Problem) % 8 == 0, "alignment");
+static_assert(S_SMEM_BYTES <= 232448, "shared memory");
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+// D += A * B, m16n8k16, FP16 inputs, FP32 accumulation.
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Lane `slot` of warp 0 feeds ring slot `slot`: it streams this CTA's units q = slot, slot +
+// S_STAGES, ... (unit u = blockIdx.x + q * gridDim.x) into that slot, then an end marker. The
+// slots' producers run side by side, so the latency of the barrier and bulk-copy instructions of
+// one slot overlaps the others'. On abort a lane waits (bounded) for its own copy in flight.
+__device__ __forceinline__ void produce(const Group &g, const Problem *prob, uint8_t *smem, Meta *meta, uint32_t full0,
+                                        uint32_t empty0, volatile int *abort_flag, int slot) {
+    const int count = g.count, units = g.units;
+    const uint32_t full = full0 + 8 * slot, empty = empty0 + 8 * slot;
+    const uint32_t dst = smem_u32(smem + (size_t)slot * S_STAGE_BYTES);
+    uint32_t ph = 0;
+    bool armed = false, ok = true;
+    int pi = 0;
+    // the current problem's fields, reloaded only when the unit index crosses into the next one
+    int next_begin = count > 1 ? prob[1].unit_begin : units;
+    int begin = prob[0].unit_begin, R = prob[0].rows_per_unit, N = prob[0].N;
+    long long ldw = prob[0].ldw;
+    const __half *w = prob[0].w;
+    for (int u = blockIdx.x + slot * gridDim.x; u < units; u += S_STAGES * gridDim.x) {
+        if (u >= next_begin) {
+            while (pi + 1 < count && u >= prob[pi + 1].unit_begin) ++pi;
+            next_begin = pi + 1 < count ? prob[pi + 1].unit_begin : units;
+            begin = prob[pi].unit_begin;
+            R = prob[pi].rows_per_unit;
+            N = prob[pi].N;
+            ldw = prob[pi].ldw;
+            w = prob[pi].w;
+        }
+        const int row0 = (u - begin) * R;
+        const int rows = min(R, N - row0);
+        if (!wait_phase(empty, ph ^ 1u, abort_flag, g.flags)) {
+            ok = false;
+            break;
+        }
+        meta[slot] = Meta{pi, row0, rows, 0};
+        const uint32_t bytes = (uint32_t)rows * (uint32_t)ldw * 2u;
+        mbar_arrive_expect_tx(full, bytes);
+        bulk_g2s(dst, w + (size_t)row0 * ldw, bytes, full);
+        armed = true;
+        ph ^= 1u;
+    }
+    if (ok && wait_phase(empty, ph ^ 1u, abort_flag, g.flags)) {
+        meta[slot] = Meta{-1, 0, 0, 0};
+        mbar_arrive(full);
+        return;
+    }
+    if (armed) drain_phase(full, ph ^ 1u);   // the last copy this lane issued
+}
+
+// Rows [0, rows) of a unit staged at `stage` (row pitch ldw), x rows (pitch round8(K), zero past
+// K) from the shared x table: 16-row blocks, one m16n8k16 MMA per 16 K with the W rows as A
+// (row-major) and up to 8 x rows as B. Lane (g = lane/4, t = lane%4) supplies, per 32-wide K
+// window, the 8 consecutive elements at window + 8t of W rows g and g+8 and of x row g; those 8
+// elements are the k-slots {2t, 2t+1, 2t+8, 2t+9} of two consecutive MMAs. The dot product only
+// needs A and B to use the same k order, and this order depends on t alone. Four accumulators
+// (one per 16-wide slice of a 64-wide step) keep consecutive MMAs independent; their sum is the
+// tile sum (tile-16) or the row total (FP32). The accumulator of lane (g, t) holds rows g and g+8
+// for x rows 2t and 2t+1.
+__device__ __forceinline__ bool process_unit(const Problem &pr, int M, const __half *stage, const __half *xtab,
+                                             int row0, int rows, int lane) {
+    const int g = lane >> 2, t4 = lane & 3;
+    const long long ldw = pr.ldw;
+    const int K = pr.K, K8 = (K + 7) & ~7, tiles = (K + 255) >> 8;
+    const bool fold = pr.fold != 0;
+    const __half *xrow = g < M ? xtab + pr.x_off + (size_t)g * K8 : nullptr;   // zero past K
+    const bool has_bias = pr.bias != nullptr;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    bool bad = false;
+    for (int rb = 0; rb < rows; rb += 16) {
+        const int ra = rb + g, rc = rb + g + 8;
+        const bool va = ra < rows, vc = rc < rows;
+        const __half *wa = stage + (size_t)ra * ldw, *wc = stage + (size_t)rc * ldw;
+        float acc[4][4] = {}, run[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int tile = 0; tile < tiles; ++tile) {
+            if (fold) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) acc[j][i] = 0.0f;
+            }
+            const int kend = min(K8, tile * 256 + 256);
+#pragma unroll 2
+            for (int kw = tile * 256; kw < kend; kw += 64) {
+                const int k0 = kw + t4 * 8, k1 = k0 + 32;
+                const bool l0 = k0 < K8, l1 = k1 < K8;
+                const uint4 a0 = (va && l0) ? *reinterpret_cast<const uint4 *>(wa + k0) : z;
+                const uint4 a1 = (va && l1) ? *reinterpret_cast<const uint4 *>(wa + k1) : z;
+                const uint4 b0 = (vc && l0) ? *reinterpret_cast<const uint4 *>(wc + k0) : z;
+                const uint4 b1 = (vc && l1) ? *reinterpret_cast<const uint4 *>(wc + k1) : z;
+                const uint4 x0 = (xrow && l0) ? *reinterpret_cast<const uint4 *>(xrow + k0) : z;
+                const uint4 x1 = (xrow && l1) ? *reinterpret_cast<const uint4 *>(xrow + k1) : z;
+                mma16816(acc[0], a0.x, b0.x, a0.y, b0.y, x0.x, x0.y);
+                mma16816(acc[1], a0.z, b0.z, a0.w, b0.w, x0.z, x0.w);
+                mma16816(acc[2], a1.x, b1.x, a1.y, b1.y, x1.x, x1.y);
+                mma16816(acc[3], a1.z, b1.z, a1.w, b1.w, x1.z, x1.w);
+            }
+            if (fold) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    run[i] = fold16(run[i], (acc[0][i] + acc[1][i]) + (acc[2][i] + acc[3][i]), tile == 0);
+            }
+        }
+        // lane (g, t4): element 0 row g / x row 2t4, 1 row g / x row 2t4+1, 2 and 3 the same for row g+8
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = (i < 2 ? ra : rc), xr = 2 * t4 + (i & 1);
+            if (r >= rows || xr >= M) continue;
+            const int n = row0 + r;
+            const float total = fold ? run[i] : (acc[0][i] + acc[1][i]) + (acc[2][i] + acc[3][i]);
+            if (pr.out_mode == OUT_RAW32) {
+                pr.partial[(size_t)xr * pr.ldp + n] = total;
+            } else if (pr.out_mode == OUT_RAW16) {
+                pr.y[(size_t)xr * pr.ldy + n] = __float2half_rn(total);
+            } else {
+                const float b = has_bias ? __half2float(pr.bias[n]) : 0.0f;
+                const float v = fold ? finish_tile16(total, b, has_bias, pr.post) : finish_fp32(total, b, pr.post);
+                const __half h = __float2half_rn(v);
+                bad |= half_nonfinite(h);
+                pr.y[(size_t)xr * pr.ldy + n] = h;
+            }
+        }
+    }
+    return bad;
+}
+
+__global__ void __launch_bounds__(S_THREADS, 1) gemv_stream_kernel(const __grid_constant__ Group g) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    Meta *meta = reinterpret_cast<Meta *>(smem + S_META_OFFSET);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S_BAR_OFFSET);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + S_ABORT_OFFSET);
+    Problem *prob = reinterpret_cast<Problem *>(smem + S_PROB_OFFSET);
+    __half *xtab = reinterpret_cast<__half *>(smem + S_X_OFFSET);
+    const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S_STAGES;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S_STAGES; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    {
+        const int words = g.count * (int)(sizeof(Problem) / 8);
+        const unsigned long long *src = reinterpret_cast<const unsigned long long *>(g.prob);
+        unsigned long long *dst = reinterpret_cast<unsigned long long *>(prob);
+        for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+    if (warp == 0) {
+        if (lane < S_STAGES) produce(g, prob, smem, meta, full0, empty0, abort_flag, lane);
+        return;
+    }
+
+    // The consumer warps fill the x table (x rows, zero past K) while the producer streams W.
+    {
+        const int ct = threadIdx.x - 32, nct = S_CONSUMERS * 32;
+        for (int e = 0; e < g.nx; ++e) {
+            const XSource xs = g.xsrc[e];
+            const int K8 = (xs.K + 7) & ~7, per_row = K8 / 8;
+            for (int i = ct; i < g.M * per_row; i += nct) {
+                const int r = i / per_row, k = (i - r * per_row) * 8;
+                uint4 v = __ldg(reinterpret_cast<const uint4 *>(xs.x + (size_t)r * xs.ldx + k));
+                if (k + 8 > xs.K) {
+                    uint32_t *wv = reinterpret_cast<uint32_t *>(&v);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (k + 2 * j >= xs.K) wv[j] = 0u;
+                        else if (k + 2 * j + 1 >= xs.K) wv[j] &= 0x0000ffffu;
+                    }
+                }
+                *reinterpret_cast<uint4 *>(xtab + xs.off + (size_t)r * K8 + k) = v;
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(nct) : "memory");
+    }
+
+    // Consumer warp c owns slots c, c + S_CONSUMERS, ... and visits them in turn, which is the
+    // order of its units (slot s holds units s, s + S_STAGES, ...); it stops at the first end marker.
+    const int c = warp - 1;
+    bool bad = false;
+    uint32_t ph = 0;
+    for (int j = 0;;) {
+        const int slot = c + S_CONSUMERS * j;
+        // Every lane waits (each gets the barrier's acquire); the warp leaves together.
+        const bool ok = __all_sync(0xffffffffu, wait_phase(full0 + 8 * slot, ph, abort_flag, g.flags));
+        if (!ok) break;
+        const Meta mt = meta[slot];
+        if (mt.prob < 0) break;
+        const __half *stage = reinterpret_cast<const __half *>(smem + (size_t)slot * S_STAGE_BYTES);
+        bad |= process_unit(prob[mt.prob], g.M, stage, xtab, mt.row0, mt.rows, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * slot);
+        if (++j == S_SLOTS_PER_CONSUMER) {
+            j = 0;
+            ph ^= 1u;
+        }
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) raise_flag(g.flags, FLAG_NONFINITE_OUTPUT);
+}
+
+// ----------------------------------------------------------------------------- host helpers
+int device_index() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return dev;
+}
+
+cudaError_t stream_attr() {
+    static bool done[64] = {};
+    const int dev = device_index();
+    if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
+    const cudaError_t e =
+        cudaFuncSetAttribute(gemv_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM_BYTES);
+    if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
+    return e;
+}
+
+template <int MR>
+int direct_blocks_per_sm() {
+    static int cached = 0;
+    if (!cached) {
+        int b = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, gemv_direct_kernel<MR>, D_THREADS, 0) != cudaSuccess ||
+            b < 1) {
+            cudaGetLastError();
+            b = 1;
+        }
+        cached = b;
+    }
+    return cached;
+}
+
+int direct_blocks(int M) {
+    if (M <= 1) return direct_blocks_per_sm<1>();
+    if (M <= 2) return direct_blocks_per_sm<2>();
+    if (M <= 4) return direct_blocks_per_sm<4>();
+    return direct_blocks_per_sm<MAX_M>();
+}
+
+unsigned direct_grid(int M, int N, int sm_count) {
+    const long long need = ((long long)N + (D_THREADS / 32) - 1) / (D_THREADS / 32);
+    const long long cap = (long long)sm_count * direct_blocks(M);
     return (unsigned)(need < cap ? need : cap);
 }
 
+// Rows per unit: spread the group's weight bytes over about two units per SM, one stage at most.
+void plan_units(Group &g, int sm_count) {
+    long long total = 0;
+    for (int i = 0; i < g.count; ++i) total += (long long)g.prob[i].N * g.prob[i].ldw * 2;
+    long long target = total / (2LL * (sm_count > 0 ? sm_count : 1));
+    if (target > (long long)S_STAGE_BYTES) target = S_STAGE_BYTES;
+    int units = 0;
+    for (int i = 0; i < g.count; ++i) {
+        Problem &p = g.prob[i];
+        const long long row_bytes = p.ldw * 2;
+        long long r = target / row_bytes;
+        const long long rmax = (long long)S_STAGE_BYTES / row_bytes;
+        if (r < 1) r = 1;
+        if (r > rmax) r = rmax;
+        p.rows_per_unit = (int)r;
+        p.unit_begin = units;
+        units += (int)((p.N + r - 1) / r);
+    }
+    g.units = units;
+}
+
+}  // namespace
+
+bool streamed(int M, int K) { return M >= 1 && M <= STREAM_MAX_M && K >= 1 && K <= STREAM_MAX_K; }
+
+namespace {
+
+// Assigns x-table offsets to problems [first, last) of `all` (sharing entries for the same x, ldx
+// and K) and copies them into `g`. Returns the index after the last problem that fits.
+int pack_group(const Group &all, int first, Group &g) {
+    g.count = 0;
+    g.nx = 0;
+    g.M = all.M;
+    g.flags = all.flags;
+    int used = 0;
+    int i = first;
+    for (; i < all.count; ++i) {
+        Problem p = all.prob[i];
+        int e = 0;
+        while (e < g.nx && !(g.xsrc[e].x == p.x && g.xsrc[e].ldx == p.ldx && g.xsrc[e].K == p.K)) ++e;
+        if (e == g.nx) {
+            const int need = all.M * ((p.K + 7) & ~7);
+            if ((used + need) * 2 > STREAM_X_BYTES) break;
+            g.xsrc[g.nx++] = XSource{p.x, p.ldx, p.K, used};
+            used += need;
+        }
+        p.x_off = g.xsrc[e].off;
+        g.prob[g.count++] = p;
+    }
+    return i;
+}
+
+}  // namespace
+
+cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned *grid_out, unsigned *launches) {
+    if (launches) *launches = 0;
+    if (all.count < 1 || all.count > GROUP_MAX || all.M < 1 || all.M > STREAM_MAX_M) return cudaErrorInvalidValue;
+    for (int i = 0; i < all.count; ++i) {
+        const Problem &p = all.prob[i];
+        if (!streamed(all.M, p.K) || p.N < 1 || p.ldw < p.K || p.ldw % 8 || p.ldw * 2 > (long long)S_STAGE_BYTES ||
+            p.ldx < p.K || p.ldx % 8 || (reinterpret_cast<uintptr_t>(p.w) & 15) ||
+            (reinterpret_cast<uintptr_t>(p.x) & 15))
+            return cudaErrorInvalidValue;
+    }
+    const cudaError_t e = stream_attr();
+    if (e != cudaSuccess) return e;
+    for (int first = 0; first < all.count;) {
+        Group g{};
+        const int next = pack_group(all, first, g);
+        if (next == first) return cudaErrorInvalidValue;   // one problem always fits the table
+        plan_units(g, sm_count);
+        const unsigned grid = (unsigned)(g.units < sm_count ? g.units : sm_count);
+        if (grid_out) *grid_out = grid;
+        gemv_stream_kernel<<<grid, S_THREADS, S_SMEM_BYTES, stream>>>(g);
+        const cudaError_t le = cudaGetLastError();
+        if (le != cudaSuccess) return le;
+        if (launches) ++*launches;
+        first = next;
+    }
+    return cudaSuccess;
+}
+
+unsigned grid_for(int M, int N, int K, long long ldw, int sm_count) {
+    if (!streamed(M, K)) return direct_grid(M, N, sm_count);
+    Group g = {};
+    g.count = 1;
+    g.M = M;
+    g.prob[0].N = N;
+    g.prob[0].K = K;
+    g.prob[0].ldw = ldw;
+    plan_units(g, sm_count);
+    return (unsigned)(g.units < sm_count ? g.units : sm_count);
+}
+
 cudaError_t launch(const Params &p, cudaStream_t stream, int sm_count, unsigned *grid_out) {
-    const unsigned grid = grid_for(p.N, sm_count);
+    if (p.M < 1 || p.M > MAX_M) return cudaErrorInvalidValue;
+    if (streamed(p.M, p.K)) {
+        Group g = {};
+        g.count = 1;
+        g.M = p.M;
+        g.flags = p.flags;
+        g.prob[0] = Problem{p.x, p.ldx, p.w, p.ldw, p.bias, p.y, p.ldy, p.partial, p.ldp,
+                            p.N, p.K, p.out_mode, p.post, p.fold, 0, 0, 0, 0};
+        return launch_group(g, stream, sm_count, grid_out, nullptr);
+    }
+    const unsigned grid = direct_grid(p.M, p.N, sm_count);
     if (grid_out) *grid_out = grid;
-    if (p.M <= 1) gemv_kernel<1><<<grid, THREADS, 0, stream>>>(p);
-    else if (p.M <= 2) gemv_kernel<2><<<grid, THREADS, 0, stream>>>(p);
-    else if (p.M <= 4) gemv_kernel<4><<<grid, THREADS, 0, stream>>>(p);
-    else if (p.M <= MAX_M) gemv_kernel<MAX_M><<<grid, THREADS, 0, stream>>>(p);
-    else return cudaErrorInvalidValue;
+    if (p.M <= 1) gemv_direct_kernel<1><<<grid, D_THREADS, 0, stream>>>(p);
+    else if (p.M <= 2) gemv_direct_kernel<2><<<grid, D_THREADS, 0, stream>>>(p);
+    else if (p.M <= 4) gemv_direct_kernel<4><<<grid, D_THREADS, 0, stream>>>(p);
+    else gemv_direct_kernel<MAX_M><<<grid, D_THREADS, 0, stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -400,6 +400,33 @@ int b2_linear_run_device(b2_linear *c, unsigned m, const void *x, size_t ldx, vo
     return rc;
 }
 
+/* Grouped small-M run: every member is finished in its launch (fused form), which for the
+ * separate (CO_SEPARATE) arm is the same arithmetic as its epilogue kernel. */
+int b2_linear_group_run_device(b2_linear *const *ops, unsigned count, unsigned m,
+                               const void *const *x, const size_t *ldx, void *const *y,
+                               const size_t *ldy) {
+    if (!ops || !x || !ldx || !y || !ldy || count < 1 || count > B2_GROUP_MAX) return ROCKET_E_SHAPE;
+    b2k_linear a[B2_GROUP_MAX];
+    for (unsigned i = 0; i < count; ++i) {
+        const co_linear_hsig *c = ops[i];
+        if (!device_args_ok(c, m, x[i], ldx[i], y[i], ldy[i], 0) || c->fd != ops[0]->fd)
+            return ROCKET_E_SHAPE;
+        a[i] = (b2k_linear){.m = m, .n = c->plan.n, .k = c->plan.k, .x = x[i], .ldx = ldx[i],
+                            .w = c->w, .ldw = c->ldw, .bias = c->bias, .y = y[i], .ldy = ldy[i],
+                            .post = c->post == CO_LINEAR_HSIG, .acc = (int)c->acc, .fused = 1,
+                            .raw_only = 0};
+    }
+    if (b2h_fault(B2_FAULT_LAUNCH)) return ROCKET_E_DEVICE;
+    unsigned launches = 0;
+    int rc = b2d_linear_group(b2h_dev(ops[0]->fd), a, count, &launches);
+    for (unsigned i = 0; i < count; ++i) {
+        const co_linear_hsig *c = ops[i];
+        b2h_count_run(c->mode == CO_CHAIN ? c->plan.chain_submits : c->plan.tasks, c->plan.tasks,
+                      i == 0 ? launches : 0);
+    }
+    return rc;
+}
+
 /* Allocation-free unfused FP32 arm: the FP32 accumulator goes to the library's static device
  * scratch (b2d_noalloc_scratch) instead of a cudaMalloc'ed workspace. */
 int b2_linear_run_device_noalloc(b2_linear *c, unsigned m, const void *x, size_t ldx, void *y,
