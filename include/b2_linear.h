@@ -106,8 +106,11 @@ int b2_linear_run_device_noalloc(b2_linear *, unsigned m, const void *x, size_t 
  * decode time. It replaces the projection step of the reference's multi-output graph call
  * (research/custom-ops/src/co_decoder.c:128-129, co_graph_run_many in
  * research/custom-ops/include/co_graph.h:77), which produces Q, K and V from one input.
- * Operators with m <= 2 and k <= 2048 share ONE kernel launch (the weight-streaming GEMV); any
- * other member runs as its own b2_linear_run_device launch. Each result is bit-identical to that
+ * Operators with m <= 8 and k <= 2048 share ONE kernel launch (the weight-streaming GEMV) as long
+ * as their distinct inputs (m x k each; members passing the same X share it) fit its 32 KB
+ * shared-memory table; otherwise they are packed in order into consecutive launches that each
+ * fit. Any other member runs as its own b2_linear_run_device launch. Each result is bit-identical
+ * to that
  * operator's own b2_linear_run_device (CO_SEPARATE operators are finished in the same launch with
  * the same arithmetic as their separate epilogue). X_i and Y_i follow b2_linear_run_device's
  * rules; the X_i may alias (a shared input). Asynchronous on the handle's stream.
