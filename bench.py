@@ -462,6 +462,32 @@ def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup,
             "fp32_partial_bytes": partial_bytes, "worst_err_over_tol_vs_fp64": worst, "clocks_rank0": clk,
             "l2": "flushed between steps (write of 2x L2, outside the events)"}
     ks.destroy()
+
+    # fused K-split: partial row blocks stored into their owner's memory by the GEMM epilogue
+    # (NVLink), round signal, owner reduction + epilogue (b2_ksplit_*)
+    fk = sharded.FusedKSplit(fd, m, w_ks, None, world, rank, torch, dist)
+    y.zero_()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        ms, clk = _timed_steps(torch, dist, world, stream,
+                               lambda: fk.run(m, xs.data_ptr(), kk, y.data_ptr(), n_ks), 3, ksteps, flush=flush)
+    if b2.status(fd):
+        raise RuntimeError("device status raised in the fused K-split run")
+    r0, r1 = fk.rows(m)
+    rows = torch.tensor(sorted({r0, (r0 + r1) // 2, r1 - 1}), device="cuda")
+    ref = oracle.linear("fp64", x[rows].cpu().numpy(), w_ks, None, post=0, want=("act",))["act"]
+    ok, worst = oracle.tolerance_ok(y[rows].cpu().numpy(), ref)
+    if not ok:
+        raise RuntimeError(f"fused K-split output outside tolerance ({worst:.3f})")
+    tflops = flops / (ms * 1e-3) / 1e12
+    out["k_split_fused"] = {
+        "m": m, "n": n_ks, "k": k, "scaling": "strong",
+        "collective": "GEMM epilogue stores to the owner over NVLink + signal + owner reduction (b2_ksplit_run)",
+        "ms_per_step": ms, "steps": ksteps, "tflops": tflops, "tflops_per_gpu": tflops / world,
+        "frac_per_gpu": tflops / world / peak_tflops, "k_per_gpu": fk.k1 - fk.k0, "rows_per_gpu": r1 - r0,
+        "worst_err_over_tol_vs_fp64": worst, "clocks_rank0": clk,
+        "l2": "flushed between steps (write of 2x L2, outside the events)"}
+    fk.destroy()
     del x, xs, y, flush
     torch.cuda.empty_cache()
     return out

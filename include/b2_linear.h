@@ -141,6 +141,36 @@ int b2_linear_get_info(const b2_linear *, b2_linear_info *);
 int b2_shard_range(unsigned long long total, unsigned parts, unsigned index, unsigned align,
                    unsigned long long *begin, unsigned long long *end);
 
+/* ----------------------------------------------------------------------- fused K-split */
+/* K-split of one Linear over `world` GPUs of a node, one process per GPU, with the partial sums
+ * added in the owner's memory. Replaces the reference's in-operator K accumulation
+ * (research/custom-ops/src/custom_ops.c:297-330, FP16 ping-pong partials on one NPU) for shapes
+ * whose N is too small to split by columns. Rank r creates its operator over W[:, k0:k1] (the
+ * b2_shard_range of K, FP32 accumulation) and a b2_ksplit; ranks exchange the blobs of
+ * b2_ksplit_export (any host channel, e.g. torch.distributed) and pass all of them, in rank order,
+ * to b2_ksplit_connect. A round (b2_ksplit_run, every rank, same m):
+ *   - the rank's GEMM stores row block q of its FP32 partial straight into rank q's buffer over
+ *     NVLink (rows [q*R, (q+1)*R), R = ceil(m_max / world) rounded up to a multiple of 32);
+ *   - it signals the round to every rank;
+ *   - it waits (at most 1 s, then B2_STATUS_TIMEOUT) for every rank's signal and writes
+ *     Y[rows of this rank] = act(sum of the world partials in rank order + b) in FP16.
+ * Y is the caller's full [m, ldy] device matrix; only this rank's rows (b2_ksplit_rows) are
+ * written. Three launches, asynchronous on the operator's handle stream; every rank must run the
+ * same number of rounds. m > 8 (the routed output is a GEMM epilogue), m <= m_max. All ranks must
+ * use the same world, m_max and N: b2_ksplit_connect checks the declared layouts and returns
+ * ROCKET_E_SHAPE on any mismatch. The first round after connecting is also when peer access is
+ * enabled. world = 1 needs no connect (a local reduction). */
+#define B2_KSPLIT_MAX_WORLD 8u
+#define B2_KSPLIT_BLOB_BYTES 96u
+typedef struct b2_ksplit b2_ksplit;
+int b2_ksplit_create(b2_linear *op, unsigned world, unsigned rank, unsigned m_max, b2_ksplit **out);
+int b2_ksplit_export(const b2_ksplit *, unsigned char blob[B2_KSPLIT_BLOB_BYTES]);
+int b2_ksplit_connect(b2_ksplit *, const unsigned char *blobs /* world x B2_KSPLIT_BLOB_BYTES */);
+/* First row and row count of Y that this rank writes for a round of m rows. */
+int b2_ksplit_rows(const b2_ksplit *, unsigned m, unsigned *row0, unsigned *rows);
+int b2_ksplit_run(b2_ksplit *, unsigned m, const void *x, size_t ldx, void *y, size_t ldy);
+void b2_ksplit_destroy(b2_ksplit *);
+
 /* ----------------------------------------------------------------------- fault injection */
 enum b2_fault {
     B2_FAULT_NONE = 0,

@@ -165,7 +165,14 @@ SIGNATURES = {
                             ctypes.POINTER(ctypes.c_ulonglong)]),
     "b2_linear_group_run_device": (_I, [ctypes.POINTER(_P), _U, _U, ctypes.POINTER(_P), ctypes.POINTER(_Z),
                                         ctypes.POINTER(_P), ctypes.POINTER(_Z)]),
+    "b2_ksplit_create": (_I, [_P, _U, _U, _U, ctypes.POINTER(_P)]),
+    "b2_ksplit_export": (_I, [_P, ctypes.c_char_p]),
+    "b2_ksplit_connect": (_I, [_P, ctypes.c_char_p]),
+    "b2_ksplit_rows": (_I, [_P, _U, ctypes.POINTER(_U), ctypes.POINTER(_U)]),
+    "b2_ksplit_run": (_I, [_P, _U, _P, _Z, _P, _Z]),
+    "b2_ksplit_destroy": (None, [_P]),
 }
+KSPLIT_BLOB_BYTES = 96
 
 _lib = None
 

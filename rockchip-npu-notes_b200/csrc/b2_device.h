@@ -104,6 +104,28 @@ int b2d_cube_to_rowmajor(b2_dev *, const b2k_cube_tile *tiles, unsigned count, v
 int b2d_rowmajor_to_cube(b2_dev *, const void *src, size_t ld, const b2k_cube_tile *tiles,
                          unsigned count);
 
+/* ---------------------------------------------------------------------- peer memory (CUDA IPC) */
+#define B2D_IPC_HANDLE_BYTES 64
+/* Exports a b2d_malloc'ed allocation for other processes on this node. */
+int b2d_ipc_export(b2_dev *, const void *ptr, unsigned char out[B2D_IPC_HANDLE_BYTES]);
+/* Maps another process's exported allocation into this device's address space (peer access over
+ * NVLink); b2d_ipc_close unmaps it. */
+int b2d_ipc_open(b2_dev *, const unsigned char in[B2D_IPC_HANDLE_BYTES], void **ptr);
+int b2d_ipc_close(b2_dev *, void *ptr);
+
+/* One fused K-split round (ksplit.cu): the routed raw-FP32 GEMM of `a` (a->fused = 0,
+ * a->raw_only = 1), the round signal to every rank, and the reduction + epilogue of the owned
+ * rows into y_own. `bufs[q]` is rank q's buffer as mapped here (bufs[rank] = the local one). */
+typedef struct {
+    unsigned world, rank, rows_per_rank, own_rows;
+    size_t ldp;
+    void *bufs[8];
+    const void *bias;
+    int post;
+    void *y_own; size_t ldy;
+} b2k_ksplit;
+int b2d_ksplit_round(b2_dev *, const b2k_linear *a, const b2k_ksplit *ks, unsigned *launches);
+
 /* Ordinal of the CUDA device behind a handle (-1 for NULL). */
 int b2d_ordinal(b2_dev *);
 

@@ -16,6 +16,7 @@
 #include "common.cuh"
 #include "gemm_sm100.h"
 #include "gemv.h"
+#include "ksplit.h"
 #include "rocket_b200.h"
 
 struct b2_dev {
@@ -302,6 +303,97 @@ int b2d_linear_group(b2_dev *d, const b2k_linear *ops, unsigned count, unsigned 
         *launches += l;
         if (rc) return rc;
     }
+    return 0;
+}
+
+int b2d_ipc_export(b2_dev *d, const void *ptr, unsigned char out[B2D_IPC_HANDLE_BYTES]) {
+    if (!set_device(d) || !ptr || !out) return ROCKET_E_SHAPE;
+    static_assert(sizeof(cudaIpcMemHandle_t) == B2D_IPC_HANDLE_BYTES, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void *>(ptr));
+    if (e != cudaSuccess) return rc_of(e);
+    memcpy(out, &h, sizeof(h));
+    return 0;
+}
+
+int b2d_ipc_open(b2_dev *d, const unsigned char in[B2D_IPC_HANDLE_BYTES], void **ptr) {
+    if (!set_device(d) || !in || !ptr) return ROCKET_E_SHAPE;
+    *ptr = nullptr;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, in, sizeof(h));
+    return rc_of(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int b2d_ipc_close(b2_dev *d, void *ptr) {
+    if (!set_device(d) || !ptr) return ROCKET_E_SHAPE;
+    return rc_of(cudaIpcCloseMemHandle(ptr));
+}
+
+int b2d_ksplit_round(b2_dev *d, const b2k_linear *a, const b2k_ksplit *ks, unsigned *launches) {
+    *launches = 0;
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (!a || !ks || !linear_args_ok(a) || a->m <= B2D_GEMV_MAX_M || ks->world < 1 ||
+        ks->world > (unsigned)b2::ksplit::MAX_WORLD || ks->rank >= ks->world || !ks->rows_per_rank ||
+        ks->rows_per_rank % 32 ||
+        a->m > ks->world * ks->rows_per_rank || ks->ldp < a->n || ks->ldp % 4 || ks->own_rows > ks->rows_per_rank ||
+        (ks->own_rows && (!ks->y_own || ks->ldy < a->n)))
+        return ROCKET_E_SHAPE;
+    for (unsigned q = 0; q < ks->world; ++q)
+        if (!ks->bufs[q]) return ROCKET_E_SHAPE;
+    using namespace b2::ksplit;
+    const size_t slot = (size_t)ks->rows_per_rank * ks->ldp;
+    const long long plane = (long long)(slot * ks->world);
+    auto planes_of = [&](unsigned q) {
+        return reinterpret_cast<float *>(static_cast<char *>(ks->bufs[q]) + PLANES_OFFSET);
+    };
+    char *mine = static_cast<char *>(ks->bufs[ks->rank]);
+    unsigned *seq = reinterpret_cast<unsigned *>(mine + SEQ_OFFSET);
+
+    // 1. GEMM, raw FP32, row block q routed to rank q's slot for this rank
+    b2::gemm::Params p = {};
+    p.M = (int)a->m; p.N = (int)a->n; p.K = (int)a->k;
+    p.ldp = (long long)ks->ldp;
+    p.out_mode = b2::gemm::OUT_RAW32;
+    p.vec_p = 1;
+    p.flags = d->flags_dev;
+    for (unsigned q = 0; q < ks->world; ++q) p.route_dst[q] = planes_of(q) + ks->rank * slot;
+    p.route_plane = plane;
+    p.route_seq = seq;
+    p.route_rows = (int)ks->rows_per_rank;
+    p.partial = p.route_dst[ks->rank];
+    b2::gemm::Shape s = {a->x, a->ldx, a->w, a->ldw};
+    cudaError_t e = b2::gemm::launch(s, p, d->stream, d->ordinal, d->sm_count, nullptr);
+    if (e != cudaSuccess) return rc_of(e);
+    *launches = 1;
+
+    // 2. round signal
+    SignalParams sp = {};
+    sp.seq = seq;
+    sp.world = (int)ks->world;
+    for (unsigned q = 0; q < ks->world; ++q)
+        sp.peer_flag[q] = reinterpret_cast<unsigned *>(static_cast<char *>(ks->bufs[q]) + FLAGS_OFFSET) + ks->rank;
+    if ((e = b2::ksplit::signal(sp, d->stream)) != cudaSuccess) return rc_of(e);
+    *launches = 2;
+
+    // 3. reduction of the owned rows
+    ReduceParams rp = {};
+    rp.seq = seq;
+    rp.flags = reinterpret_cast<const unsigned *>(mine + FLAGS_OFFSET);
+    rp.planes = planes_of(ks->rank);
+    rp.plane_floats = plane;
+    rp.world = (int)ks->world;
+    rp.rows_per_rank = (int)ks->rows_per_rank;
+    rp.rows = (int)ks->own_rows;
+    rp.n = (int)a->n;
+    rp.ldp = (long long)ks->ldp;
+    rp.vec = ks->own_rows ? (aligned16(ks->y_own) && ks->ldy % 8 == 0) : 0;
+    rp.bias = static_cast<const __half *>(ks->bias);
+    rp.post = ks->post;
+    rp.y = static_cast<__half *>(ks->y_own);
+    rp.ldy = (long long)ks->ldy;
+    rp.status = d->flags_dev;
+    if ((e = b2::ksplit::reduce(rp, d->stream, d->sm_count)) != cudaSuccess) return rc_of(e);
+    *launches = ks->own_rows ? 3 : 2;
     return 0;
 }
 

@@ -296,6 +296,10 @@ __device__ __forceinline__ void epilogue_role(const Params &p, int warp, int lan
     uint32_t acc_used = 0;
     bool ok = true, bad = false;
     __half2 run[HALF / 2];                 // per-256-K FP16 running sum (tile-16 modes)
+    // routed raw output: the parity plane of this round (the signal step increments the counter)
+    unsigned route_par = 0;
+    if constexpr (MODE == EPI_RAW32)
+        if (p.route_rows > 0) route_par = (*reinterpret_cast<const volatile unsigned *>(p.route_seq) + 1u) & 1u;
     for (int tile = cluster_id; ok && tile < p.num_tiles; tile += num_clusters) {
         int mb, nb;
         tile_coords(tile, p, mb, nb);
@@ -325,7 +329,27 @@ __device__ __forceinline__ void epilogue_role(const Params &p, int warp, int lan
                 }
                 const int cb = col0 + 32 * j;
                 if constexpr (MODE == EPI_RAW32) {
-                    if (row_ok) store32f(p.partial + (size_t)row * p.ldp, cb, p.N, p.vec_p, v);
+                    if (p.route_rows > 0) {
+                        // Routed: the owner's slot is stored in 32-row panels, column by column
+                        // ((r / 32) * 32 * ldp + c * 32 + r % 32), so each store instruction of the
+                        // warp (32 consecutive rows of one column) is one 128-byte line over NVLink.
+                        // route_rows is a multiple of 32: a warp's rows share one owner and panel.
+                        if (row_ok) {
+                            const int q = row / p.route_rows;
+                            float *base = p.route_dst[0];
+#pragma unroll
+                            for (int i = 1; i < ROUTE_MAX; ++i)
+                                if (i == q) base = p.route_dst[i];
+                            const int r = row - q * p.route_rows;
+                            float *dst = base + (size_t)route_par * p.route_plane + (size_t)(r >> 5) * 32 * p.ldp +
+                                         (size_t)cb * 32 + (r & 31);
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                if (cb + i < p.N) dst[(size_t)i * 32] = v[i];
+                        }
+                    } else if (row_ok) {
+                        store32f(p.partial + (size_t)row * p.ldp, cb, p.N, p.vec_p, v);
+                    }
                 } else if constexpr (MODE == EPI_FP32) {
                     float b[32];
                     load_bias32(p.bias, cb, p.N, b);
@@ -368,6 +392,8 @@ __device__ __forceinline__ void epilogue_role(const Params &p, int warp, int lan
             ++acc_used;
         }
     }
+    if constexpr (MODE == EPI_RAW32)
+        if (p.route_rows > 0) __threadfence_system();   // peer stores before the round's signal
     if (__any_sync(0xffffffffu, bad) && lane == 0) raise_flag(p.flags, FLAG_NONFINITE_OUTPUT);
 }
 

@@ -13,6 +13,8 @@ enum OutMode : int {
     OUT_RAW32 = 2,   // partial = the FP32 accumulator over the whole K
 };
 
+constexpr int ROUTE_MAX = 8;   // ranks a routed raw output can address
+
 struct Params {
     int M, N, K;
     int num_m_blocks, num_n_blocks, num_tiles, num_kb, kb_per_chunk;
@@ -24,6 +26,15 @@ struct Params {
     int out_mode, post, fold, vec_y, vec_p;
     int group_m;                 // tile raster: bands of group_m m-blocks (0 = column-major)
     unsigned *flags;             // status flag words (common.cuh)
+    // Routed raw output (fused K-split, out_mode OUT_RAW32): with route_rows > 0 (a multiple of 32),
+    // accumulator row r goes to owner q = r / route_rows, as row r' = r - q * route_rows of parity
+    // plane ((*route_seq + 1) & 1) at route_dst[q] (another GPU's memory for q != this rank,
+    // written with plain stores over NVLink), element (r', c) at (r'/32)*32*ldp + c*32 + r'%32;
+    // route_rows == 0 writes `partial` row-major.
+    float *route_dst[ROUTE_MAX];
+    long long route_plane;       // floats between the two parity planes
+    const unsigned *route_seq;   // this rank's round counter, read by the epilogue
+    int route_rows;
 };
 
 struct Shape {

@@ -28,4 +28,10 @@ int b2h_plan(co_linear_plan *out, unsigned m, unsigned k, unsigned n, int has_bi
              enum co_linear_post post, size_t budget, unsigned max_dim, int compat);
 size_t b2h_context_bytes(unsigned m, unsigned k, unsigned n, int has_bias);
 
+/* Operator accessors for other host files (linear.c). */
+int b2h_linear_fd(const b2_linear *op);
+/* Raw-FP32-partial launch descriptor of `op` for device X [m, ldx] (no bias, no activation in
+ * the GEMM; bias/post copied into the descriptor for a later epilogue). 0 or ROCKET_E_SHAPE. */
+int b2h_linear_desc(const b2_linear *op, unsigned m, const void *x, size_t ldx, b2k_linear *out);
+
 #endif

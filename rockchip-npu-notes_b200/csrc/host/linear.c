@@ -476,6 +476,17 @@ int b2_linear_epilogue_device(b2_linear *c, unsigned m, const float *partial, si
     return rc;
 }
 
+int b2h_linear_fd(const b2_linear *c) { return c ? c->fd : -1; }
+
+int b2h_linear_desc(const b2_linear *c, unsigned m, const void *x, size_t ldx, b2k_linear *out) {
+    if (!c || !out || !x || m < 1 || m > B2_MAX_DIM || ldx < c->plan.k || ldx % 8 || ((uintptr_t)x & 15))
+        return ROCKET_E_SHAPE;
+    *out = (b2k_linear){.m = m, .n = c->plan.n, .k = c->plan.k, .x = x, .ldx = ldx, .w = c->w,
+                        .ldw = c->ldw, .bias = c->bias, .post = c->post == CO_LINEAR_HSIG,
+                        .acc = B2_ACC_FP32, .fused = 0, .raw_only = 1};
+    return 0;
+}
+
 int b2_linear_get_info(const b2_linear *c, b2_linear_info *info) {
     if (!c || !info) return ROCKET_E_SHAPE;
     b2k_linear a = {.m = c->plan.m, .n = c->plan.n, .k = c->plan.k, .x = c->x, .ldx = c->ldx,

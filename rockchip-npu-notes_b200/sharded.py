@@ -7,8 +7,11 @@ The reference runs on one RK3588 and only chooses an NPU core per submit
   X is replicated; no collective touches the data path.
 * K-split (``KSplitLinear``): rank r owns X[:, k0:k1] and W[:, k0:k1] and produces the raw FP32
   partial X_r W_r^T (b2_linear_partial_device); the partials are summed with an NCCL all-reduce
-  over NVLink, then every rank applies bias and activation (b2_linear_epilogue_device). This is for
+  or reduce-scatter over NVLink, then bias and activation (b2_linear_epilogue_device). This is for
   shapes whose N is too small to split.
+* Fused K-split (``FusedKSplit``, b2_ksplit_*): the same split, but the GEMM epilogue stores each
+  row block of the partial straight into its owner's memory over NVLink while later tiles are
+  still multiplying, and the owner adds the world partials with bias and activation.
 
 Shard boundaries come from b2_shard_range (256-aligned, so 256-wide K tiles and output tiles stay
 whole).
@@ -122,4 +125,48 @@ class KSplitLinear:
             self.op.epilogue_device(r1 - r0, out.data_ptr(), self.ldp, y_ptr + r0 * ldy * 2, ldy)
 
     def destroy(self):
+        self.op.destroy()
+
+
+class FusedKSplit:
+    """This rank's part of a fused K-split Linear (b2_ksplit_*): owns X[:, k0:k1], W[:, k0:k1] and
+    writes rows ``rows(m)`` of Y. ``dist`` may be None when world == 1. The library must run on
+    torch's current stream when ``run`` is called (the caller sets it with b2.set_stream)."""
+
+    def __init__(self, fd, m_max, w_full, bias_full, world, rank, torch, dist, post=_b2.CO_LINEAR_NONE):
+        import ctypes
+        n, k = w_full.shape
+        self.k0, self.k1 = k_shard(k, world, rank)
+        if self.k1 <= self.k0:
+            raise ValueError("every rank needs a non-empty K slice")
+        self.op = _b2.Linear(fd, 1, self.k1 - self.k0, n, np.ascontiguousarray(w_full[:, self.k0:self.k1]), bias_full,
+                             post=post, mode=_b2.CO_SEPARATE, acc=_b2.ACC_FP32, compat=False)
+        L = _b2.lib()
+        h = ctypes.c_void_p()
+        _b2.check("b2_ksplit_create", L.b2_ksplit_create(self.op.h, world, rank, m_max, ctypes.byref(h)))
+        self.h, self.world, self.rank = h, world, rank
+        if world > 1:
+            blob = ctypes.create_string_buffer(_b2.KSPLIT_BLOB_BYTES)
+            _b2.check("b2_ksplit_export", L.b2_ksplit_export(self.h, blob))
+            dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+            mine = torch.frombuffer(bytearray(blob.raw), dtype=torch.uint8).to(dev)
+            parts = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(parts, mine)
+            blobs = b"".join(bytes(t.cpu().numpy()) for t in parts)
+            _b2.check("b2_ksplit_connect", L.b2_ksplit_connect(self.h, blobs))
+
+    def rows(self, m):
+        import ctypes
+        r0, nr = ctypes.c_uint(), ctypes.c_uint()
+        _b2.check("b2_ksplit_rows", _b2.lib().b2_ksplit_rows(self.h, m, ctypes.byref(r0), ctypes.byref(nr)))
+        return r0.value, r0.value + nr.value
+
+    def run(self, m, x_ptr, ldx, y_ptr, ldy):
+        """x_ptr: this rank's X[:, k0:k1] [m, ldx]; y_ptr: Y [m, ldy] (rows(m) written)."""
+        _b2.check("b2_ksplit_run", _b2.lib().b2_ksplit_run(self.h, m, x_ptr, ldx, y_ptr, ldy))
+
+    def destroy(self):
+        if self.h:
+            _b2.lib().b2_ksplit_destroy(self.h)
+            self.h = None
         self.op.destroy()
