@@ -1,0 +1,288 @@
+/* mock_device.c -- CPU stand-in of the host/device seam (b2_device.h) for host C tests.
+ *
+ * TEST INFRASTRUCTURE ONLY: linked into tests/c/host_test, never into the shipped library (which
+ * has no CPU compute path). It plays the role the reference's mock NPU plays for its host tests
+ * (research/custom-ops/tests/c/multitile_host_test.c:14-58): "device" memory is host memory and
+ * every operation completes immediately. Linear results come from the oracle's C restatement
+ * (oracle/linear_oracle.c): TILE16_EXACT (the reference's arithmetic, bit-identical to its file
+ * gate) for tile-16 operators and FP32ACC for FP32 operators, so a host test can check the host
+ * layer end to end (staging, descriptors, publish-on-success, error paths, fault seam) against the
+ * same oracle bit for bit.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "b2_device.h"
+#include "rocket_b200.h"
+
+int oracle_linear(int mode, unsigned m, unsigned k, unsigned n, const uint16_t *x, const uint16_t *w,
+                  const uint16_t *bias, int post, uint16_t *y16, double *act, double *raw, int threads);
+double oracle_f16_to_double(uint16_t h);
+uint16_t oracle_f16_from_double(double d);
+
+enum { ORACLE_TILE16_EXACT = 0, ORACLE_FP32ACC = 5 };
+
+struct b2_dev {
+    int ordinal;
+    void *stream;
+    uint32_t status;
+};
+
+static int mock_devices(void) {
+    const char *e = getenv("B2_MOCK_DEVICES");
+    return e ? atoi(e) : 1;
+}
+
+int b2d_device_count(void) { return mock_devices(); }
+
+int b2d_open(int ordinal, b2_dev **out) {
+    *out = NULL;
+    if (ordinal < 0 || ordinal >= mock_devices()) return ROCKET_E_DEVICE;
+    b2_dev *d = calloc(1, sizeof(*d));
+    if (!d) return ROCKET_E_NOMEM;
+    d->ordinal = ordinal;
+    *out = d;
+    return 0;
+}
+void b2d_close(b2_dev *d) { free(d); }
+int b2d_set_stream(b2_dev *d, void *stream) {
+    if (!d) return ROCKET_E_SHAPE;
+    d->stream = stream;
+    return 0;
+}
+void *b2d_stream(b2_dev *d) { return d ? d->stream : NULL; }
+int b2d_sm_count(b2_dev *d) { return d ? 148 : 0; }
+int b2d_ordinal(b2_dev *d) { return d ? d->ordinal : -1; }
+
+int b2d_malloc(b2_dev *d, size_t bytes, void **out) {
+    (void)d;
+    *out = calloc(1, bytes ? bytes : 1);
+    return *out ? 0 : ROCKET_E_NOMEM;
+}
+void b2d_free(b2_dev *d, void *ptr) {
+    (void)d;
+    free(ptr);
+}
+void *b2d_host_alloc(size_t bytes) { return malloc(bytes); }
+void b2d_host_free(void *ptr) { free(ptr); }
+
+int b2d_copy_2d(b2_dev *d, void *dst, size_t dpitch, const void *src, size_t spitch, size_t width, size_t rows,
+                int kind) {
+    (void)d;
+    (void)kind;
+    if ((!dst || !src) && rows && width) return ROCKET_E_SHAPE;
+    for (size_t r = 0; r < rows; r++) memcpy((char *)dst + r * dpitch, (const char *)src + r * spitch, width);
+    return 0;
+}
+int b2d_memset(b2_dev *d, void *ptr, int value, size_t bytes) {
+    (void)d;
+    memset(ptr, value, bytes);
+    return 0;
+}
+int b2d_sync(b2_dev *d) { return d ? 0 : ROCKET_E_DEVICE; }
+uint32_t b2d_status(b2_dev *d, int clear) {
+    uint32_t s = d->status;
+    if (clear) d->status = 0;
+    return s;
+}
+void b2d_status_merge(b2_dev *d, uint32_t bits) {
+    if (d) d->status |= bits;
+}
+
+/* ------------------------------------------------------------------------------ Linear */
+static int f16_nonfinite(uint16_t h) { return (h & 0x7c00u) == 0x7c00u; }
+
+/* Pitched FP16 [rows, ld] -> contiguous [rows, cols]. */
+static uint16_t *pack(const void *p, unsigned rows, unsigned cols, size_t ld) {
+    uint16_t *out = malloc((size_t)rows * cols * 2);
+    if (!out) return NULL;
+    for (unsigned r = 0; r < rows; r++) memcpy(out + (size_t)r * cols, (const uint16_t *)p + (size_t)r * ld, (size_t)cols * 2);
+    return out;
+}
+
+static float finish32(float acc, const uint16_t *bias, unsigned col, int post) {
+    float a = acc;
+    if (bias) a += (float)oracle_f16_to_double(bias[col]);
+    if (post) {
+        float t = a / 6.0f + 0.5f;
+        a = t < 0.0f ? 0.0f : (t > 1.0f ? 1.0f : t);
+    }
+    return a;
+}
+
+int b2d_linear(b2_dev *d, const b2k_linear *a, unsigned *launches) {
+    *launches = 0;
+    if (!d || !a || !a->m || !a->n || !a->k || !a->x || !a->w) return ROCKET_E_SHAPE;
+    uint16_t *x = pack(a->x, a->m, a->k, a->ldx), *w = pack(a->w, a->n, a->k, a->ldw);
+    uint16_t *y = malloc((size_t)a->m * a->n * 2);
+    double *raw = malloc((size_t)a->m * a->n * sizeof(double));
+    int rc = (x && w && y && raw) ? 0 : ROCKET_E_NOMEM;
+    const int mode = (a->acc == 0 && !a->raw_only) ? ORACLE_TILE16_EXACT : ORACLE_FP32ACC;
+    if (!rc && oracle_linear(mode, a->m, a->k, a->n, x, w, a->raw_only ? NULL : (const uint16_t *)a->bias,
+                             a->raw_only ? 0 : a->post, y, NULL, raw, 1))
+        rc = ROCKET_E_SHAPE;
+    if (!rc) {
+        if (a->raw_only) {
+            for (unsigned r = 0; r < a->m; r++)
+                for (unsigned c = 0; c < a->n; c++) a->partial[(size_t)r * a->ldp + c] = (float)raw[(size_t)r * a->n + c];
+        } else {
+            for (unsigned r = 0; r < a->m; r++)
+                for (unsigned c = 0; c < a->n; c++) {
+                    const uint16_t h = y[(size_t)r * a->n + c];
+                    if (f16_nonfinite(h)) d->status |= B2D_ST_NONFINITE_OUTPUT;
+                    ((uint16_t *)a->y)[(size_t)r * a->ldy + c] = h;
+                }
+            /* the unfused FP32 arm also leaves its raw accumulator in the workspace */
+            if (!a->fused && a->acc != 0 && a->partial)
+                for (unsigned r = 0; r < a->m; r++)
+                    for (unsigned c = 0; c < a->n; c++)
+                        a->partial[(size_t)r * a->ldp + c] = (float)raw[(size_t)r * a->n + c];
+        }
+        *launches = (a->fused || a->raw_only) ? 1 : 2;
+    }
+    free(x);
+    free(w);
+    free(y);
+    free(raw);
+    return rc;
+}
+
+int b2d_linear_config(b2_dev *d, const b2k_linear *a, b2k_config *cfg) {
+    if (!d || !a || !cfg) return ROCKET_E_SHAPE;
+    memset(cfg, 0, sizeof(*cfg));
+    cfg->kernel = a->m <= B2D_GEMV_MAX_M ? 1 : 0;
+    cfg->tile_m = cfg->kernel ? a->m : 256;
+    cfg->tile_n = cfg->kernel ? 8 : 256;
+    cfg->tile_k = cfg->kernel ? 256 : 64;
+    cfg->grid = 148;
+    return 0;
+}
+
+int b2d_linear_group(b2_dev *d, const b2k_linear *ops, unsigned count, unsigned *launches) {
+    *launches = 0;
+    if (!d || !ops || !count || count > B2D_GROUP_MAX) return ROCKET_E_SHAPE;
+    for (unsigned i = 0; i < count; i++) {
+        unsigned l = 0;
+        int rc = b2d_linear(d, &ops[i], &l);
+        if (rc) return rc;
+    }
+    *launches = 1;
+    return 0;
+}
+
+int b2d_epilogue(b2_dev *d, unsigned m, unsigned n, const float *partial, size_t ldp, const void *bias, int post,
+                 int acc, void *y, size_t ldy) {
+    if (!d || !m || !n || !partial || !y || ldp < n || ldy < n || acc != 1) return ROCKET_E_SHAPE;
+    for (unsigned r = 0; r < m; r++)
+        for (unsigned c = 0; c < n; c++) {
+            const uint16_t h = oracle_f16_from_double(finish32(partial[(size_t)r * ldp + c], bias, c, post));
+            if (f16_nonfinite(h)) d->status |= B2D_ST_NONFINITE_OUTPUT;
+            ((uint16_t *)y)[(size_t)r * ldy + c] = h;
+        }
+    return 0;
+}
+
+int b2d_scan_nonfinite(b2_dev *d, const void *p, size_t rows, size_t cols, size_t ld, uint32_t bit) {
+    if (!d || !p || ld % 8) return ROCKET_E_SHAPE;
+    for (size_t r = 0; r < rows; r++)
+        for (size_t c = 0; c < cols; c++)
+            if (f16_nonfinite(((const uint16_t *)p)[r * ld + c])) d->status |= bit;
+    return 0;
+}
+
+/* C2=8 cubes: atom (group g, row r) = 8 channels at ptr[(g * physical_rows + r) * 8]. */
+int b2d_cube_to_rowmajor(b2_dev *d, const b2k_cube_tile *tiles, unsigned count, void *dst, size_t ld) {
+    if (!d || !dst || ld % 8 || count > B2K_MAX_CUBE_TILES) return ROCKET_E_SHAPE;
+    for (unsigned t = 0; t < count; t++) {
+        const b2k_cube_tile *c = &tiles[t];
+        if (!c->ptr || c->physical_cols % 8 || c->rows > c->physical_rows || c->cols > c->physical_cols) return ROCKET_E_SHAPE;
+        for (unsigned g = 0; g < (c->cols + 7) / 8; g++)
+            for (unsigned r = 0; r < c->rows; r++)
+                memcpy((uint16_t *)dst + (size_t)(c->row0 + r) * ld + c->col0 + 8 * g,
+                       (const uint16_t *)c->ptr + ((size_t)g * c->physical_rows + r) * 8, 16);
+    }
+    return 0;
+}
+
+int b2d_rowmajor_to_cube(b2_dev *d, const void *src, size_t ld, const b2k_cube_tile *tiles, unsigned count) {
+    if (!d || !src || ld % 8 || count > B2K_MAX_CUBE_TILES) return ROCKET_E_SHAPE;
+    for (unsigned t = 0; t < count; t++) {
+        const b2k_cube_tile *c = &tiles[t];
+        if (!c->ptr || c->physical_cols % 8 || c->rows > c->physical_rows || c->cols > c->physical_cols) return ROCKET_E_SHAPE;
+        for (unsigned g = 0; g < c->physical_cols / 8; g++)
+            for (unsigned r = 0; r < c->physical_rows; r++) {
+                uint16_t v[8] = {0};
+                if (r < c->rows && 8 * g < c->cols) {
+                    memcpy(v, (const uint16_t *)src + (size_t)(c->row0 + r) * ld + c->col0 + 8 * g, 16);
+                    for (unsigned e = c->cols - 8 * g; e < 8; e++) v[e] = 0;
+                }
+                memcpy((uint16_t *)c->ptr + ((size_t)g * c->physical_rows + r) * 8, v, 16);
+            }
+    }
+    return 0;
+}
+
+static float noalloc_scratch[B2D_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+int b2d_noalloc_scratch(b2_dev *d, float **ptr, size_t *bytes) {
+    if (!d) return ROCKET_E_DEVICE;
+    *ptr = noalloc_scratch;
+    *bytes = B2D_NOALLOC_SCRATCH_BYTES;
+    return 0;
+}
+
+int b2d_guard_init(b2_dev *d, void *base, size_t payload, size_t slack, size_t guard) {
+    if (!d || !base) return ROCKET_E_SHAPE;
+    memset((char *)base + payload + slack, 0xa5, guard);
+    return 0;
+}
+
+int b2d_guard_check(b2_dev *d, void *const *bases, const size_t *payloads, unsigned count, size_t slack,
+                    size_t guard) {
+    if (!d || count > B2K_MAX_CUBE_TILES) return ROCKET_E_SHAPE;
+    for (unsigned i = 0; i < count; i++) {
+        const unsigned char *p = (const unsigned char *)bases[i] + payloads[i];
+        for (size_t j = 0; j < slack + guard; j++)
+            if (p[j] != (j < slack ? 0x00 : 0xa5)) d->status |= B2D_ST_GUARD;
+    }
+    return 0;
+}
+
+/* No peer memory in a single host process. */
+int b2d_ipc_export(b2_dev *d, const void *ptr, unsigned char out[B2D_IPC_HANDLE_BYTES]) {
+    (void)d;
+    (void)ptr;
+    (void)out;
+    return ROCKET_E_UNSUPPORTED;
+}
+int b2d_ipc_open(b2_dev *d, const unsigned char in[B2D_IPC_HANDLE_BYTES], void **ptr) {
+    (void)d;
+    (void)in;
+    *ptr = NULL;
+    return ROCKET_E_UNSUPPORTED;
+}
+int b2d_ipc_close(b2_dev *d, void *ptr) {
+    (void)d;
+    (void)ptr;
+    return ROCKET_E_UNSUPPORTED;
+}
+
+/* One-rank round: the FP32 partial, then the epilogue of the owned rows. */
+int b2d_ksplit_round(b2_dev *d, const b2k_linear *a, const b2k_ksplit *ks, unsigned *launches) {
+    *launches = 0;
+    if (!d || !a || !ks || ks->world != 1 || ks->rank != 0 || ks->rows_per_rank % 32) return ROCKET_E_SHAPE;
+    const size_t ldp = ks->ldp;
+    float *part = malloc((size_t)a->m * ldp * sizeof(float));
+    if (!part) return ROCKET_E_NOMEM;
+    b2k_linear raw = *a;
+    raw.partial = part;
+    raw.ldp = ldp;
+    raw.raw_only = 1;
+    unsigned l = 0;
+    int rc = b2d_linear(d, &raw, &l);
+    if (!rc && ks->own_rows) rc = b2d_epilogue(d, ks->own_rows, a->n, part, ldp, ks->bias, ks->post, 1, ks->y_own, ks->ldy);
+    free(part);
+    if (!rc) *launches = 3;
+    return rc;
+}
