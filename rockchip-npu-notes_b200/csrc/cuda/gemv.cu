@@ -269,7 +269,7 @@ __device__ __forceinline__ bool process_unit(const Problem &pr, int M, const __h
                     for (int i = 0; i < 4; ++i) acc[j][i] = 0.0f;
             }
             const int kend = min(K8, tile * 256 + 256);
-#pragma unroll 2
+#pragma unroll 4
             for (int kw = tile * 256; kw < kend; kw += 64) {
                 const int k0 = kw + t4 * 8, k1 = k0 + 32;
                 const bool l0 = k0 < K8, l1 = k1 < K8;
@@ -322,25 +322,27 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_stream_kernel(const __grid_
     __half *xtab = reinterpret_cast<__half *>(smem + S_X_OFFSET);
     const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S_STAGES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < S_STAGES; ++s) {
-            mbar_init(full0 + 8 * s, 1);
-            mbar_init(empty0 + 8 * s, 1);
+    if (warp == 0) {
+        // Warp 0 sets up the barriers and the problem table, hands both to the consumer warps with a
+        // non-blocking arrive on named barrier 2, and its producer lanes start streaming at once.
+        if (lane == 0) {
+            for (int s = 0; s < S_STAGES; ++s) {
+                mbar_init(full0 + 8 * s, 1);
+                mbar_init(empty0 + 8 * s, 1);
+            }
+            *abort_flag = 0;
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         }
-        *abort_flag = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    {
         const int words = g.count * (int)(sizeof(Problem) / 8);
         const unsigned long long *src = reinterpret_cast<const unsigned long long *>(g.prob);
         unsigned long long *dst = reinterpret_cast<unsigned long long *>(prob);
-        for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
-    }
-    __syncthreads();
-    if (warp == 0) {
+        for (int i = lane; i < words; i += 32) dst[i] = src[i];
+        __syncwarp();
+        asm volatile("bar.arrive 2, %0;" ::"r"(S_THREADS) : "memory");
         if (lane < S_STAGES) produce(g, prob, smem, meta, full0, empty0, abort_flag, lane);
         return;
     }
+    asm volatile("bar.sync 2, %0;" ::"r"(S_THREADS) : "memory");   // barriers and problem table ready
 
     // The consumer warps fill the x table (x rows, zero past K) while the producer streams W.
     {
