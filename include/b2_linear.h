@@ -9,6 +9,10 @@
  *   - asynchronous row-major device-pointer entries (inputs already resident in HBM);
  *   - raw FP32 partial accumulators and a separate bias/activation epilogue, used for K-split
  *     across GPUs (partials reduced with NCCL between the two calls);
+ *   - an allocation-free run of the unfused FP32 arm;
+ *   - a grouped small-M run (a decoder layer's decode projections in one launch);
+ *   - the per-GPU shard of N or K (b2_shard_range) and a fused K-split across GPUs whose GEMM
+ *     writes its partials straight into the owner's memory over NVLink (b2_ksplit_*);
  *   - a host-side fault-injection seam for failure-path tests.
  * An operator created here is the same object type as a co_linear and accepts every co_* run
  * entry whose shape limits it meets.
@@ -123,7 +127,8 @@ int b2_linear_group_run_device(b2_linear *const *ops, unsigned count, unsigned m
 typedef struct {
     unsigned m, k, n;
     unsigned kernel;             /* 0 = tcgen05 GEMM, 1 = GEMV (small M) */
-    unsigned tile_m, tile_n, tile_k, stages;
+    unsigned tile_m, tile_n, tile_k;
+    unsigned stages;             /* GEMM: TMA ring depth; streamed GEMV: 12 copy slots; else 0 */
     unsigned grid;               /* CTAs of the main kernel for the create-time m */
     unsigned launches_per_run;   /* CUDA launches of one co_linear_run */
     enum b2_accumulate acc;

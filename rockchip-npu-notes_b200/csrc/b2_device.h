@@ -79,7 +79,8 @@ typedef struct {
 int b2d_linear(b2_dev *, const b2k_linear *, unsigned *launches);
 int b2d_linear_config(b2_dev *, const b2k_linear *, b2k_config *);
 /* Runs `count` (<= B2D_GROUP_MAX) independent fused Linears with the same m. Those the streamed
- * small-M kernel serves (m <= 2, k <= 2048) share one launch; any other runs as b2d_linear.
+ * small-M kernel serves (m <= 8, k <= 2048) share one launch (or several when their distinct
+ * inputs exceed its shared x table); any other runs as b2d_linear.
  * Every op must have fused = 1 and raw_only = 0. */
 #define B2D_GROUP_MAX 16u
 int b2d_linear_group(b2_dev *, const b2k_linear *ops, unsigned count, unsigned *launches);
