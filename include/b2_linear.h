@@ -114,10 +114,10 @@ int b2_linear_run_device_noalloc(b2_linear *, unsigned m, const void *x, size_t 
  * as their distinct inputs (m x k each; members passing the same X share it) fit its 32 KB
  * shared-memory table; otherwise they are packed in order into consecutive launches that each
  * fit. Any other member runs as its own b2_linear_run_device launch. Each result is bit-identical
- * to that
- * operator's own b2_linear_run_device (CO_SEPARATE operators are finished in the same launch with
- * the same arithmetic as their separate epilogue). X_i and Y_i follow b2_linear_run_device's
- * rules; the X_i may alias (a shared input). Asynchronous on the handle's stream.
+ * to that operator's own b2_linear_run_device (CO_SEPARATE operators are finished in the same
+ * launch with the same arithmetic as their separate epilogue). X_i and Y_i follow
+ * b2_linear_run_device's rules; the X_i may alias (a shared input). Asynchronous on the handle's
+ * stream.
  * 1 <= count <= B2_GROUP_MAX, else ROCKET_E_SHAPE; operators on different handles: ROCKET_E_SHAPE. */
 #define B2_GROUP_MAX 16u
 int b2_linear_group_run_device(b2_linear *const *ops, unsigned count, unsigned m,
