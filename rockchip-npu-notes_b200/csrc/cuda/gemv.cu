@@ -153,6 +153,7 @@ __global__ void __launch_bounds__(D_THREADS) gemv_direct_kernel(const Params p) 
 }
 
 // ----------------------------------------------------------------------------- streamed kernel
+constexpr long long PDL_MAX_BYTES = 16ll << 20;      // weight bytes up to which launches start early
 constexpr int S_CONSUMERS = 12;                     // consumer warps
 constexpr int S_SLOTS_PER_CONSUMER = 1;             // a slot refills while its consumer works on the other
 constexpr int S_STAGES = S_CONSUMERS * S_SLOTS_PER_CONSUMER;   // one producer lane each: <= 32
@@ -322,6 +323,12 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_stream_kernel(const __grid_
     __half *xtab = reinterpret_cast<__half *>(smem + S_X_OFFSET);
     const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S_STAGES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Programmatic dependent launch (when the launch allows it): the next kernel on the stream may
+    // start as SMs free up. This kernel's producer only reads W, which no kernel writes; every read
+    // of x and every global write happens in the consumer warps after griddepcontrol.wait (the
+    // previous kernel has completed and its writes are visible), so neither a read-after-write nor
+    // a write-after-read crosses. Without the attribute both instructions have no effect.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (warp == 0) {
         // Warp 0 sets up the barriers and the problem table, hands both to the consumer warps with a
         // non-blocking arrive on named barrier 2, and its producer lanes start streaming at once.
@@ -343,6 +350,7 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_stream_kernel(const __grid_
         return;
     }
     asm volatile("bar.sync 2, %0;" ::"r"(S_THREADS) : "memory");   // barriers and problem table ready
+    asm volatile("griddepcontrol.wait;" ::: "memory");              // the previous kernel is done
 
     // The consumer warps fill the x table (x rows, zero past K) while the producer streams W.
     {
@@ -509,7 +517,23 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
         plan_units(g, sm_count);
         const unsigned grid = (unsigned)(g.units < sm_count ? g.units : sm_count);
         if (grid_out) *grid_out = grid;
-        gemv_stream_kernel<<<grid, S_THREADS, S_SMEM_BYTES, stream>>>(g);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(S_THREADS);
+        cfg.dynamicSmemBytes = S_SMEM_BYTES;
+        cfg.stream = stream;
+        // Early start of the next kernel pays off where the fixed per-launch cost dominates (it hid
+        // 0.6-0.7 us of a 1.8 MB projection) but slowed 56 MB launches with M >= 4 by ~10 %: only
+        // launches of at most PDL_MAX_BYTES of weights allow it.
+        long long wbytes = 0;
+        for (int i = 0; i < g.count; ++i) wbytes += (long long)g.prob[i].N * g.prob[i].ldw * 2;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = wbytes <= PDL_MAX_BYTES ? 1 : 0;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t le0 = cudaLaunchKernelEx(&cfg, gemv_stream_kernel, g);
+        if (le0 != cudaSuccess) return le0;
         const cudaError_t le = cudaGetLastError();
         if (le != cudaSuccess) return le;
         if (launches) ++*launches;
