@@ -164,7 +164,10 @@ int b2_shard_range(unsigned long long total, unsigned parts, unsigned index, uns
  * same number of rounds. m > 8 (the routed output is a GEMM epilogue), m <= m_max. All ranks must
  * use the same world, m_max and N: b2_ksplit_connect checks the declared layouts and returns
  * ROCKET_E_SHAPE on any mismatch. The first round after connecting is also when peer access is
- * enabled. world = 1 needs no connect (a local reduction). */
+ * enabled. world = 1 needs no connect (a local reduction). A rank that misses a round makes the
+ * others' round end with B2_STATUS_TIMEOUT after at most a second (their Y rows are not written);
+ * the ranks' round counters are then out of step, so every rank destroys and re-creates its
+ * b2_ksplit before the next round. */
 #define B2_KSPLIT_MAX_WORLD 8u
 #define B2_KSPLIT_BLOB_BYTES 96u
 typedef struct b2_ksplit b2_ksplit;

@@ -131,7 +131,9 @@ cudaError_t reduce(const ReduceParams &p, cudaStream_t stream, int sm_count) {
     if (p.rows == 0) return cudaSuccess;
     const long long work = (long long)((p.rows + 31) / 32) * ((p.n + 7) / 8) * 32;
     long long blocks = (work + THREADS - 1) / THREADS;
-    const long long cap = (long long)sm_count * 8;
+    // every block waits for the flags on its own: keep the grid resident in one wave, so a rank that
+    // never signals costs one wait limit, not one per wave
+    const long long cap = (long long)sm_count * 4;
     if (blocks > cap) blocks = cap;
     reduce_kernel<<<(unsigned)blocks, THREADS, 0, stream>>>(p);
     return cudaGetLastError();

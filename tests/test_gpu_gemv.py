@@ -177,3 +177,53 @@ def test_lm_head_sized_decode_against_oracle(b2, gpu_fd):
         ok, worst = oracle.tolerance_ok(y.cpu().numpy(), ref)
         assert ok, f"acc={acc}: worst {worst:.3f}"
         op.destroy()
+
+
+def test_dependent_chain_under_programmatic_launch(b2, gpu_fd):
+    """Back-to-back decode launches may overlap (programmatic dependent launch): a chain whose
+    input is the previous launch's output (ping-pong buffers, so each launch also overwrites the
+    buffer the launch before it read) gives the same bits with and without a sync after every
+    launch, eagerly and as a replayed CUDA graph."""
+    k = n = 576
+    rng = np.random.default_rng(21)
+    ws = [(rng.standard_normal((n, k)) * 0.03).astype(np.float16) for _ in range(3)]
+    ops = [b2.Linear(gpu_fd, 1, k, n, w, None, post=b2.CO_LINEAR_HSIG, acc=b2.ACC_FP32, compat=False) for w in ws]
+    x0 = torch.from_numpy(rng.standard_normal((1, k)).astype(np.float16)).cuda()
+    bufs = [torch.zeros(1, k, dtype=torch.float16, device="cuda") for _ in range(2)]
+    steps = 12
+
+    def chain(sync):
+        bufs[0].copy_(x0)
+        torch.cuda.synchronize()
+        for i in range(steps):
+            src, dst = bufs[i % 2], bufs[(i + 1) % 2]
+            ops[i % 3].run_device(1, src.data_ptr(), k, dst.data_ptr(), n)
+            if sync:
+                b2.sync(gpu_fd)
+        b2.sync(gpu_fd)
+        return bufs[steps % 2].clone()
+
+    ref = chain(True)
+    got = chain(False)
+    assert b2.status(gpu_fd) == 0
+    assert torch.equal(ref.view(torch.int16), got.view(torch.int16))
+    assert torch.isfinite(ref.float()).all() and ref.float().abs().sum() > 0
+    s = torch.cuda.Stream()
+    b2.set_stream(gpu_fd, s.cuda_stream)
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(steps):
+                src, dst = bufs[i % 2], bufs[(i + 1) % 2]
+                ops[i % 3].run_device(1, src.data_ptr(), k, dst.data_ptr(), n)
+        for _ in range(2):
+            with torch.cuda.stream(s):
+                bufs[0].copy_(x0)
+                g.replay()
+            s.synchronize()
+            assert torch.equal(ref.view(torch.int16), bufs[steps % 2].view(torch.int16))
+        del g
+    finally:
+        b2.set_stream(gpu_fd, None)
+    for op in ops:
+        op.destroy()

@@ -9,7 +9,9 @@ On one GPU (world = 1, the round signals itself):
   * argument errors: m <= 8, m > m_max, a tile-16 operator, world > 8, a peer blob declaring a
     different layout.
 On two GPUs (skipped with fewer): two spawned ranks, blobs exchanged over gloo, each rank's rows
-of Y within tolerance of the FP64 oracle over the full K.
+of Y within tolerance of the FP64 oracle over the full K; and failure detection: one rank never
+runs its round (a host-side failure), the other rank's round ends after its one-second wait limit
+with B2_STATUS_TIMEOUT instead of hanging, and its context keeps working.
 Tolerance: |y - ref| <= 2e-3 + 2e-3*|ref| element-wise.
 """
 import ctypes
@@ -179,3 +181,72 @@ def test_two_gpu_fused_ksplit(b2):
     for r in range(2):
         st, ok, worst = out[r]
         assert st == 0 and ok, (r, st, worst)
+
+
+def _lonely_rank(rank, world, port, out):
+    """Rank 1 never runs a round; rank 0's round must time out and report it."""
+    import importlib
+    import sys
+    import time
+    sys.path.insert(0, ROOT)
+    import torch as t
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        b2 = importlib.import_module("rockchip-npu-notes_b200")
+        sharded = importlib.import_module("rockchip-npu-notes_b200.sharded")
+        t.cuda.set_device(rank)
+        fd = b2.open_device(rank)
+        m, n, k = 256, 512, 1024
+        x, w, b = case(m, n, k, 13)
+        fk = sharded.FusedKSplit(fd, m, w, b, world, rank, t, dist)
+        dist.barrier()
+        result = None
+        if rank == 0:
+            xs = t.from_numpy(np.ascontiguousarray(x[:, fk.k0:fk.k1])).cuda()
+            y = t.zeros(m, n, dtype=t.float16, device="cuda")
+            t.cuda.synchronize()
+            t0 = time.time()
+            fk.run(m, xs.data_ptr(), fk.k1 - fk.k0, y.data_ptr(), n)
+            b2.sync(fd)
+            waited = time.time() - t0
+            st = b2.status(fd)
+            # the context still works: a plain run afterwards
+            op = b2.Linear(fd, 1, k, n, w, b, post=b2.CO_LINEAR_NONE, acc=b2.ACC_FP32, compat=False)
+            xf = t.from_numpy(x).cuda()
+            y2 = t.zeros(m, n, dtype=t.float16, device="cuda")
+            t.cuda.synchronize()
+            op.run_device(m, xf.data_ptr(), k, y2.data_ptr(), n)
+            b2.sync(fd)
+            st2 = b2.status(fd)
+            op.destroy()
+            result = (int(st), float(waited), int(st2), bool(t.isfinite(y2.float()).all()))
+        dist.barrier()                      # rank 1 keeps its buffer until rank 0 is done
+        fk.destroy()
+        b2.close(fd)
+        out[rank] = result
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gpu_missing_rank_times_out(b2):
+    if b2.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_lonely_rank, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    st, waited, st2, finite = out[0]
+    assert st & b2.STATUS_TIMEOUT, st
+    assert 0.5 < waited < 30, waited
+    assert st2 == 0 and finite
