@@ -13,6 +13,9 @@ Contents
 * ``XorShift``             the K-tiling probe generator and its ``dyadic`` / ``random_small``
                            draws (``research/custom-ops/tools/c/ktiling_probe.c:55-81``).
 * ``plan_tasks``           the task/submit accounting the file gate checks (``cli_gate.py:79-86``).
+* ``ew`` / ``rmsnorm`` / ``ffn``  ctypes front-end of ``graph_oracle.c``: the graph's elementwise
+                           nodes, RMSNorm (``research/custom-ops/src/co_row_ops.c:150-224``) and the
+                           SwiGLU FFN of the reference's graph gate (``tools/python/graph_gate.py``).
 
 Parity pins: ``tests/golden/`` holds outputs produced by importing the reference's own Python
 oracles; ``tests/test_oracle_golden.py`` checks this package against them bit for bit.
@@ -70,6 +73,12 @@ def lib():
         L.oracle_linear_pre.restype = ctypes.c_int
         L.oracle_f16_encode.argtypes = [dp, u16p, ctypes.c_size_t]
         L.oracle_f16_decode.argtypes = [u16p, dp, ctypes.c_size_t]
+        L.oracle_ew.argtypes = [ctypes.c_int, u16p, u16p, u16p, ctypes.c_size_t]
+        L.oracle_ew.restype = None
+        L.oracle_rmsnorm.argtypes = [ctypes.c_uint, ctypes.c_uint, u16p, u16p, ctypes.c_float, u16p]
+        L.oracle_rmsnorm.restype = ctypes.c_uint
+        L.oracle_gate16.argtypes = [ctypes.c_int, ctypes.c_uint16]
+        L.oracle_gate16.restype = ctypes.c_uint16
         _lib = L
     return _lib
 
@@ -173,6 +182,49 @@ def linear_py(m, k, n, x, w, bias, post=1):
                 affine = _f16(min(1.0, max(0.0, affine / 6.0 + 0.5)))
             out.append(affine)
     return out
+
+
+# ----------------------------------------------------------------------- graph nodes
+# graph_oracle.c: elementwise node kinds (co_graph.c:293-313) and RMSNorm (co_row_ops.c:150-224)
+EW_ADD, EW_MUL, EW_SILU, EW_GELU, EW_HSIG = 0, 1, 2, 3, 4
+GATE_SIGMOID, GATE_GELU = 1, 2
+
+
+def ew(op, a, b=None):
+    """One elementwise graph node over float16 arrays of one shape (b only for ADD/MUL)."""
+    a = _u16(a)
+    bb = _u16(b) if b is not None else None
+    y = np.empty(a.shape, np.uint16)
+    lib().oracle_ew(op, _ptr(a, ctypes.c_uint16), _ptr(bb, ctypes.c_uint16), _ptr(y, ctypes.c_uint16), a.size)
+    return y.view(np.float16)
+
+
+def rmsnorm(x, gamma, eps=1e-5):
+    """(y float16 [rows, cols], number of rejected rows) of the RMSNorm node; rejected rows are 0."""
+    x = _u16(x)
+    g = _u16(gamma)
+    rows, cols = x.shape
+    y = np.zeros((rows, cols), np.uint16)
+    bad = lib().oracle_rmsnorm(rows, cols, _ptr(x, ctypes.c_uint16), _ptr(g, ctypes.c_uint16), float(eps),
+                               _ptr(y, ctypes.c_uint16))
+    return y.view(np.float16), int(bad)
+
+
+def ffn(x, wg, wu, wd, bias=None, bias_up=None, gamma=None, eps=1e-5, act=EW_SILU):
+    """The graph FFN Y = X + Linear(act(Linear(Z, Wg, bias)) * Linear(Z, Wu, bias_up), Wd), Z = X or
+    RMSNorm(X): every node with the reference's arithmetic (Linear: TILE16_EXACT, the file gate's
+    per-256-K FP16 fold), bit-identical to research/custom-ops/tools/python/graph_gate.py:30-41
+    except for the RMSNorm coefficient (graph_oracle.c)."""
+    z = x
+    if gamma is not None:
+        z, bad = rmsnorm(x, gamma, eps)
+        if bad:
+            raise ValueError("RMSNorm rejected a row")
+    g = linear(TILE16_EXACT, z, wg, bias, post=0)["y16"]
+    u = linear(TILE16_EXACT, z, wu, bias_up, post=0)["y16"]
+    hidden = ew(EW_MUL, ew(act, g), u)
+    down = linear(TILE16_EXACT, hidden, wd, None, post=0)["y16"]
+    return ew(EW_ADD, down, x)
 
 
 # ----------------------------------------------------------------------- input generators

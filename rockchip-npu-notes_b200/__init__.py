@@ -87,6 +87,64 @@ class B2LinearInfo(ctypes.Structure):
                 ("device_bytes", ctypes.c_size_t)]
 
 
+# include/co_graph.h
+CO_GRAPH_MAX_NODES = 64
+(CO_GRAPH_INPUT, CO_GRAPH_LINEAR, CO_GRAPH_ADD, CO_GRAPH_MUL, CO_GRAPH_SILU, CO_GRAPH_GELU, CO_GRAPH_HSIG,
+ CO_GRAPH_RMSNORM, CO_GRAPH_SOFTMAX, CO_GRAPH_ROPE, CO_GRAPH_ATTENTION) = range(11)
+CO_GRAPH_ALLOW_NEG_INF = 1
+CO_ROPE_INTERLEAVED, CO_ROPE_SPLIT_HALF = 0, 1
+
+
+class CoGraphNode(ctypes.Structure):
+    _fields_ = [("op", ctypes.c_int), ("a", ctypes.c_uint), ("b", ctypes.c_uint), ("rows", ctypes.c_uint),
+                ("cols", ctypes.c_uint), ("c", ctypes.c_uint), ("mask_node", ctypes.c_uint),
+                ("has_mask", ctypes.c_uint), ("weights", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+                ("gamma", ctypes.c_void_p), ("epsilon", ctypes.c_float), ("flags", ctypes.c_uint),
+                ("heads", ctypes.c_uint), ("kv_heads", ctypes.c_uint), ("head_dim", ctypes.c_uint),
+                ("rotary_dim", ctypes.c_uint), ("theta", ctypes.c_float), ("scale", ctypes.c_float),
+                ("rope_style", ctypes.c_int), ("position_base", ctypes.c_uint32), ("causal", ctypes.c_int),
+                ("window", ctypes.c_uint)]
+
+
+class CoGraphDesc(ctypes.Structure):
+    _fields_ = [("nodes", ctypes.POINTER(CoGraphNode)), ("count", ctypes.c_uint), ("output", ctypes.c_uint),
+                ("device_budget", ctypes.c_size_t)]
+
+
+class CoGraphTensorPlan(ctypes.Structure):
+    _fields_ = [("rows", ctypes.c_uint), ("cols", ctypes.c_uint), ("tiles", ctypes.c_uint),
+                ("slot", ctypes.c_uint), ("first", ctypes.c_uint), ("last", ctypes.c_uint),
+                ("bytes", ctypes.c_size_t)]
+
+
+class CoGraphPlan(ctypes.Structure):
+    _fields_ = [("steps", ctypes.c_uint), ("inputs", ctypes.c_uint), ("slots", ctypes.c_uint),
+                ("order", ctypes.c_uint * 64), ("noutputs", ctypes.c_uint), ("outputs", ctypes.c_uint * 64),
+                ("tensors", CoGraphTensorPlan * 64), ("slot_bytes", ctypes.c_size_t * 64)] + \
+               [(f, ctypes.c_size_t) for f in ("tensor_bytes", "linear_bytes", "rowop_bytes", "rope_bytes",
+                                               "attention_bytes", "workspace_bytes", "device_bytes")] + \
+               [("hybrid_nodes", ctypes.c_uint)] + \
+               [(f, ctypes.c_ulonglong) for f in ("host_upload_calls", "statistic_download_calls",
+                                                  "activation_download_calls")] + \
+               [(f, ctypes.c_size_t) for f in ("host_activation_reads", "statistic_downloads",
+                                               "activation_downloads", "host_uploads")] + \
+               [("identity_mask", ctypes.c_uint), ("gate_bytes", ctypes.c_size_t),
+                ("tasks", ctypes.c_ulonglong), ("chain_submits", ctypes.c_ulonglong)]
+
+
+class CoGraphInput(ctypes.Structure):
+    _fields_ = [("node", ctypes.c_uint), ("data", ctypes.c_void_p)]
+
+
+class CoGraphOutput(ctypes.Structure):
+    _fields_ = [("node", ctypes.c_uint), ("data", ctypes.c_void_p)]
+
+
+class B2GraphInfo(ctypes.Structure):
+    _fields_ = [("gated", ctypes.c_uint), ("residual", ctypes.c_uint), ("kernels", ctypes.c_uint),
+                ("captured", ctypes.c_uint)]
+
+
 _P = ctypes.c_void_p
 _U = ctypes.c_uint
 _I = ctypes.c_int
@@ -171,6 +229,18 @@ SIGNATURES = {
     "b2_ksplit_rows": (_I, [_P, _U, ctypes.POINTER(_U), ctypes.POINTER(_U)]),
     "b2_ksplit_run": (_I, [_P, _U, _P, _Z, _P, _Z]),
     "b2_ksplit_destroy": (None, [_P]),
+    # co_graph.h
+    "co_graph_plan_init": (_I, [ctypes.POINTER(CoGraphDesc), ctypes.POINTER(CoGraphPlan)]),
+    "co_graph_plan_many": (_I, [ctypes.POINTER(CoGraphDesc), ctypes.POINTER(_U), _U, ctypes.POINTER(CoGraphPlan)]),
+    "co_graph_compile": (_I, [_I, ctypes.POINTER(CoGraphDesc), _I, ctypes.POINTER(_P)]),
+    "co_graph_compile_many": (_I, [_I, ctypes.POINTER(CoGraphDesc), ctypes.POINTER(_U), _U, _I, ctypes.POINTER(_P)]),
+    "co_graph_destroy": (None, [_P]),
+    "co_graph_run": (_I, [_P, ctypes.POINTER(CoGraphInput), _U, _P]),
+    "co_graph_run_many": (_I, [_P, ctypes.POINTER(CoGraphInput), _U, ctypes.POINTER(CoGraphOutput), _U]),
+    "b2_graph_tensor": (_I, [_P, _U, ctypes.POINTER(_P), ctypes.POINTER(_Z)]),
+    "b2_graph_launch": (_I, [_P]),
+    "b2_graph_status": (_I, [_P]),
+    "b2_graph_get_info": (_I, [_P, ctypes.POINTER(B2GraphInfo)]),
 }
 KSPLIT_BLOB_BYTES = 96
 

@@ -67,6 +67,20 @@ typedef struct {
     int acc;                        /* 0 per-256-K FP16 fold (reference), 1 FP32 */
     int fused;                      /* 1: epilogue in the GEMM; 0: raw to `partial`, then epilogue */
     int raw_only;                   /* 1: stop after writing the raw accumulator to `partial` */
+    /* Residual (graph ADD of this output): y = fp16(res + fp16(result)); FP16 [m, ldr], 16-byte
+     * aligned, ldr % 8 == 0; y must then be 16-byte aligned with ldy % 8 == 0. NULL for none. */
+    const void *res; size_t ldr;
+    /* Gated Linear (graph SiLU/GELU of one Linear times another Linear of the same input):
+     * gate = 1 SiLU, 2 GELU; w packed in 64-row blocks [32 gate rows | 32 up rows] with
+     * n = 2 * roundup(gate_n, 32); bias = gate bias [gate_n], bias2 = up bias [gate_n] (either
+     * NULL); y [m, ldy >= gate_n] receives fp16(fp16(g * fp16(gate(g))) * u). Requires acc = 0,
+     * post = 0, no residual. Where the GEMM cannot fuse it (m <= B2D_GEMV_MAX_M, or fused = 0)
+     * the folded sums go to tmp (FP16 [m, ldt >= n], 16-byte aligned, ldt % 8 == 0) and a
+     * second kernel combines them. */
+    int gate;
+    unsigned gate_n;
+    const void *bias2;
+    void *tmp; size_t ldt;
 } b2k_linear;
 
 typedef struct {
@@ -87,6 +101,30 @@ int b2d_linear_group(b2_dev *, const b2k_linear *ops, unsigned count, unsigned *
 /* y = act(partial + bias) with the same arithmetic as the fused epilogue of mode `acc`. */
 int b2d_epilogue(b2_dev *, unsigned m, unsigned n, const float *partial, size_t ldp,
                  const void *bias, int post, int acc, void *y, size_t ldy);
+
+/* ---------------------------------------------------------------------- graph node kernels
+ * FP16 row-major operands with 16-byte aligned bases and pitches (elements) that are multiples
+ * of 8; otherwise ROCKET_E_SHAPE. A result that overflows FP16 sets B2D_ST_NONFINITE_OUTPUT. */
+enum { B2D_EW_ADD = 0, B2D_EW_MUL = 1, B2D_EW_SILU = 2, B2D_EW_GELU = 3, B2D_EW_HSIG = 4 };
+/* y = fp16(a + b), fp16(a * b), fp16(a * fp16(sigmoid(a))), fp16(a * fp16(gelu_gate(a))) or
+ * fp16(hsig(a)); b only for ADD/MUL. y may be a or b (same pitch). */
+int b2d_elementwise(b2_dev *, int op, unsigned rows, unsigned cols, const void *a, size_t lda,
+                    const void *b, size_t ldb, void *y, size_t ldy);
+/* RMSNorm of each row with FP16 gamma [cols] and epsilon eps (> 0). A row whose 256-column
+ * square sum reaches 65504 or whose coefficient overflows FP16 sets B2D_ST_NONFINITE_INPUT. */
+int b2d_rmsnorm(b2_dev *, unsigned rows, unsigned cols, const void *x, size_t ldx,
+                const void *gamma, float eps, void *y, size_t ldy);
+
+/* ---------------------------------------------------------------------- CUDA graphs
+ * Launches issued between b2d_capture_begin and b2d_capture_end on this handle's stream are
+ * recorded (not run) into an executable graph; b2d_exec_launch replays it on the handle's
+ * stream. capture_begin returns ROCKET_E_UNSUPPORTED where capture is not available; after a
+ * failed launch inside the capture, capture_end still ends it and returns an error. */
+typedef struct b2_exec b2_exec;
+int b2d_capture_begin(b2_dev *);
+int b2d_capture_end(b2_dev *, b2_exec **out, unsigned *kernels);
+int b2d_exec_launch(b2_dev *, b2_exec *);
+void b2d_exec_destroy(b2_exec *);
 
 /* Sets status `bit` if any of rows x cols FP16 elements (row pitch ld elements) is not finite. */
 int b2d_scan_nonfinite(b2_dev *, const void *p, size_t rows, size_t cols, size_t ld, uint32_t bit);

@@ -71,4 +71,32 @@ __device__ __forceinline__ bool half_nonfinite(__half h) {
     return (__half_as_ushort(h) & 0x7c00u) == 0x7c00u;
 }
 
+// Activation gates of the graph's SiLU / GELU nodes (research/custom-ops/src/co_graph.c:303-307:
+// a LUT pass x -> gate, then an elementwise multiply x * gate). The reference's 513-entry LUTs
+// sample these functions (custom_ops.c:357-369); here each FP16 input gets the function itself,
+// evaluated in double and rounded once to FP16:
+//   GATE_SIGMOID  1 / (1 + exp(-a))
+//   GATE_GELU     0.5 * (1 + erf(a / sqrt 2))
+enum : int { GATE_SIGMOID = 1, GATE_GELU = 2 };
+
+__device__ __forceinline__ float round16_from_double(double g) {
+    unsigned short h;
+    asm("cvt.rn.f16.f64 %0, %1;" : "=h"(h) : "d"(g));
+    return __half2float(__ushort_as_half(h));
+}
+
+__device__ __forceinline__ float gate16(float a, int act) {
+    const double v = (double)a;
+    const double g = act == GATE_GELU ? 0.5 * (1.0 + erf(v / 1.4142135623730951)) : 1.0 / (1.0 + exp(-v));
+    return round16_from_double(g);
+}
+
+// SiLU / GELU node value of an FP16 a: fp16(a * fp16(gate(a))).
+__device__ __forceinline__ float gated_act16(float a, int act) { return round16(__fmul_rn(a, gate16(a, act))); }
+
+// The fused gate·up product: fp16(act16(g) * u) for FP16 g, u (the graph's MUL node).
+__device__ __forceinline__ float gated16(float g, float u, int act) {
+    return round16(__fmul_rn(gated_act16(g, act), u));
+}
+
 }  // namespace b2

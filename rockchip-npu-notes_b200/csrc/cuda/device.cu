@@ -16,6 +16,7 @@
 #include "common.cuh"
 #include "gemm_sm100.h"
 #include "gemv.h"
+#include "graph_kernels.h"
 #include "ksplit.h"
 #include "rocket_b200.h"
 
@@ -214,10 +215,81 @@ static bool linear_args_ok(const b2k_linear *a) {
            a->k <= (1u << 24);
 }
 
+// One launch of the weight-streaming GEMV (M <= 8) or the GEMM in output mode `out_mode`, writing
+// y/ldy (FP16 modes) or a->partial (OUT_RAW32). The bias is applied in OUT_FINAL only; the residual
+// and gate fields go to the GEMM's epilogue only with `extra`.
+static cudaError_t launch_core(b2_dev *d, const b2k_linear *a, int out_mode, bool fold, void *y, size_t ldy,
+                               bool extra) {
+    const __half *bias = static_cast<const __half *>(a->bias);
+    if (use_gemv(a)) {
+        b2::gemv::Params p = {};
+        p.M = (int)a->m; p.N = (int)a->n; p.K = (int)a->k;
+        p.x = static_cast<const __half *>(a->x); p.ldx = (long long)a->ldx;
+        p.w = static_cast<const __half *>(a->w); p.ldw = (long long)a->ldw;
+        p.bias = out_mode == b2::gemv::OUT_FINAL ? bias : nullptr;
+        p.y = static_cast<__half *>(y); p.ldy = (long long)ldy;
+        p.partial = a->partial; p.ldp = (long long)a->ldp;
+        p.out_mode = out_mode; p.post = a->post; p.fold = fold ? 1 : 0;
+        p.flags = d->flags_dev;
+        return b2::gemv::launch(p, d->stream, d->sm_count, nullptr);
+    }
+    b2::gemm::Params p = {};
+    p.M = (int)a->m; p.N = (int)a->n; p.K = (int)a->k;
+    p.bias = out_mode == b2::gemm::OUT_FINAL ? bias : nullptr;
+    p.y = static_cast<__half *>(y); p.ldy = (long long)ldy;
+    p.partial = a->partial; p.ldp = (long long)a->ldp;
+    p.out_mode = out_mode; p.post = a->post; p.fold = fold ? 1 : 0;
+    p.vec_y = y && aligned16(y) && ldy % 8 == 0;
+    p.vec_p = a->partial && aligned16(a->partial) && a->ldp % 4 == 0;
+    p.flags = d->flags_dev;
+    if (extra) {
+        p.res = static_cast<const __half *>(a->res); p.ldr = (long long)a->ldr;
+        p.vec_r = a->res && aligned16(a->res) && a->ldr % 8 == 0;
+        p.gate = a->gate; p.gate_n = (int)a->gate_n;
+        p.bias2 = static_cast<const __half *>(a->bias2);
+    }
+    b2::gemm::Shape s = {a->x, a->ldx, a->w, a->ldw};
+    return b2::gemm::launch(s, p, d->stream, d->ordinal, d->sm_count, nullptr);
+}
+
+static bool fp16_operand_ok(const void *p, size_t ld, size_t cols) {
+    return p && aligned16(p) && ld % 8 == 0 && ld >= cols;
+}
+
+// The packed gate|up Linear: fused in the GEMM's epilogue, else folded sums to tmp + combine.
+static int linear_gated(b2_dev *d, const b2k_linear *a, unsigned *launches) {
+    const size_t h32 = ((size_t)a->gate_n + 31) / 32 * 32;
+    if ((a->gate != b2::GATE_SIGMOID && a->gate != b2::GATE_GELU) || a->acc != 0 || a->post || a->res ||
+        a->raw_only || !a->gate_n || a->n != 2 * h32 || !a->y || a->ldy < a->gate_n)
+        return ROCKET_E_SHAPE;
+    if (a->fused && !use_gemv(a)) {
+        const cudaError_t e = launch_core(d, a, b2::gemm::OUT_FINAL, true, a->y, a->ldy, true);
+        if (e != cudaSuccess) return rc_of(e);
+        *launches = 1;
+        return 0;
+    }
+    if (!fp16_operand_ok(a->tmp, a->ldt, a->n) || !fp16_operand_ok(a->y, a->ldy, a->gate_n)) return ROCKET_E_SHAPE;
+    cudaError_t e = launch_core(d, a, b2::gemm::OUT_RAW16, true, a->tmp, a->ldt, false);
+    if (e != cudaSuccess) return rc_of(e);
+    *launches = 1;
+    b2::graph::GatedParams g = {};
+    g.rows = (int)a->m; g.gate_n = (int)a->gate_n; g.act = a->gate;
+    g.src = static_cast<const __half *>(a->tmp); g.lds = (long long)a->ldt;
+    g.bias_gate = static_cast<const __half *>(a->bias);
+    g.bias_up = static_cast<const __half *>(a->bias2);
+    g.y = static_cast<__half *>(a->y); g.ldy = (long long)a->ldy;
+    g.flags = d->flags_dev;
+    e = b2::graph::gated_combine(g, d->stream, d->sm_count);
+    if (e != cudaSuccess) return rc_of(e);
+    *launches = 2;
+    return 0;
+}
+
 int b2d_linear(b2_dev *d, const b2k_linear *a, unsigned *launches) {
     *launches = 0;
     if (!set_device(d)) return ROCKET_E_DEVICE;
     if (!linear_args_ok(a)) return ROCKET_E_SHAPE;
+    if (a->gate) return linear_gated(d, a, launches);
     const bool fold = a->acc == 0 && !a->raw_only;
     int out_mode;
     if (a->raw_only) out_mode = b2::gemm::OUT_RAW32;
@@ -225,47 +297,36 @@ int b2d_linear(b2_dev *d, const b2k_linear *a, unsigned *launches) {
     else out_mode = fold ? b2::gemm::OUT_RAW16 : b2::gemm::OUT_RAW32;
     if (out_mode == b2::gemm::OUT_RAW32 && (!a->partial || a->ldp < a->n)) return ROCKET_E_SHAPE;
     if (out_mode != b2::gemm::OUT_RAW32 && (!a->y || a->ldy < a->n)) return ROCKET_E_SHAPE;
-
-    const __half *bias = static_cast<const __half *>(a->bias);
-    cudaError_t e;
-    if (use_gemv(a)) {
-        b2::gemv::Params p = {};
-        p.M = (int)a->m; p.N = (int)a->n; p.K = (int)a->k;
-        p.x = static_cast<const __half *>(a->x); p.ldx = (long long)a->ldx;
-        p.w = static_cast<const __half *>(a->w); p.ldw = (long long)a->ldw;
-        p.bias = out_mode == b2::gemv::OUT_FINAL ? bias : nullptr;
-        p.y = static_cast<__half *>(a->y); p.ldy = (long long)a->ldy;
-        p.partial = a->partial; p.ldp = (long long)a->ldp;
-        p.out_mode = out_mode; p.post = a->post; p.fold = fold ? 1 : 0;
-        p.flags = d->flags_dev;
-        e = b2::gemv::launch(p, d->stream, d->sm_count, nullptr);
-    } else {
-        b2::gemm::Params p = {};
-        p.M = (int)a->m; p.N = (int)a->n; p.K = (int)a->k;
-        p.bias = out_mode == b2::gemm::OUT_FINAL ? bias : nullptr;
-        p.y = static_cast<__half *>(a->y); p.ldy = (long long)a->ldy;
-        p.partial = a->partial; p.ldp = (long long)a->ldp;
-        p.out_mode = out_mode; p.post = a->post; p.fold = fold ? 1 : 0;
-        p.vec_y = a->y && aligned16(a->y) && a->ldy % 8 == 0;
-        p.vec_p = a->partial && aligned16(a->partial) && a->ldp % 4 == 0;
-        p.flags = d->flags_dev;
-        b2::gemm::Shape s = {a->x, a->ldx, a->w, a->ldw};
-        e = b2::gemm::launch(s, p, d->stream, d->ordinal, d->sm_count, nullptr);
-    }
+    if (a->res && (a->raw_only || !fp16_operand_ok(a->res, a->ldr, a->n) || !fp16_operand_ok(a->y, a->ldy, a->n)))
+        return ROCKET_E_SHAPE;
+    const bool fuse_res = a->res && a->fused && !use_gemv(a);
+    cudaError_t e = launch_core(d, a, out_mode, fold, a->y, a->ldy, fuse_res);
     if (e != cudaSuccess) return rc_of(e);
     *launches = 1;
-    if (a->fused || a->raw_only) return 0;
-    // Separate epilogue: FP32 partial -> y, or the folded FP16 sum in y -> y in place.
-    b2::aux::EpilogueParams ep = {};
-    ep.M = (int)a->m; ep.N = (int)a->n;
-    ep.partial = fold ? nullptr : a->partial; ep.ldp = (long long)a->ldp;
-    ep.bias = bias;
-    ep.y = static_cast<__half *>(a->y); ep.ldy = (long long)a->ldy;
-    ep.post = a->post;
-    ep.flags = d->flags_dev;
-    e = b2::aux::epilogue(ep, d->stream, d->sm_count);
-    if (e != cudaSuccess) return rc_of(e);
-    *launches = 2;
+    if (!a->fused && !a->raw_only) {
+        // Separate epilogue: FP32 partial -> y, or the folded FP16 sum in y -> y in place.
+        b2::aux::EpilogueParams ep = {};
+        ep.M = (int)a->m; ep.N = (int)a->n;
+        ep.partial = fold ? nullptr : a->partial; ep.ldp = (long long)a->ldp;
+        ep.bias = static_cast<const __half *>(a->bias);
+        ep.y = static_cast<__half *>(a->y); ep.ldy = (long long)a->ldy;
+        ep.post = a->post;
+        ep.flags = d->flags_dev;
+        e = b2::aux::epilogue(ep, d->stream, d->sm_count);
+        if (e != cudaSuccess) return rc_of(e);
+        *launches = 2;
+    }
+    if (a->res && !fuse_res) {
+        b2::graph::EwParams ew = {};
+        ew.op = b2::graph::EW_ADD; ew.rows = (int)a->m; ew.cols = (int)a->n;
+        ew.a = static_cast<const __half *>(a->y); ew.lda = (long long)a->ldy;
+        ew.b = static_cast<const __half *>(a->res); ew.ldb = (long long)a->ldr;
+        ew.y = static_cast<__half *>(a->y); ew.ldy = (long long)a->ldy;
+        ew.flags = d->flags_dev;
+        e = b2::graph::elementwise(ew, d->stream, d->sm_count);
+        if (e != cudaSuccess) return rc_of(e);
+        *launches += 1;
+    }
     return 0;
 }
 
@@ -464,6 +525,107 @@ int b2d_guard_check(b2_dev *d, void *const *bases, const size_t *payloads, unsig
     }
     g.count = count;
     return rc_of(b2::aux::guard_check(g, slack, guard, d->flags_dev, d->stream));
+}
+
+// ----------------------------------------------------------------------------- graph node kernels
+int b2d_elementwise(b2_dev *d, int op, unsigned rows, unsigned cols, const void *a, size_t lda, const void *b,
+                    size_t ldb, void *y, size_t ldy) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    const bool binary = op == B2D_EW_ADD || op == B2D_EW_MUL;
+    if (op < B2D_EW_ADD || op > B2D_EW_HSIG || rows > (1u << 24) || cols > (1u << 24) ||
+        !fp16_operand_ok(a, lda, cols) || !fp16_operand_ok(y, ldy, cols) || (binary && !fp16_operand_ok(b, ldb, cols)))
+        return ROCKET_E_SHAPE;
+    b2::graph::EwParams p = {};
+    p.op = op; p.rows = (int)rows; p.cols = (int)cols;
+    p.a = static_cast<const __half *>(a); p.lda = (long long)lda;
+    p.b = static_cast<const __half *>(b); p.ldb = (long long)ldb;
+    p.y = static_cast<__half *>(y); p.ldy = (long long)ldy;
+    p.flags = d->flags_dev;
+    return rc_of(b2::graph::elementwise(p, d->stream, d->sm_count));
+}
+
+int b2d_rmsnorm(b2_dev *d, unsigned rows, unsigned cols, const void *x, size_t ldx, const void *gamma, float eps,
+                void *y, size_t ldy) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (rows > (1u << 24) || cols > (1u << 24) || !gamma || !(eps > 0.0f) || !fp16_operand_ok(x, ldx, cols) ||
+        !fp16_operand_ok(y, ldy, cols))
+        return ROCKET_E_SHAPE;
+    b2::graph::NormParams p = {};
+    p.rows = (int)rows; p.cols = (int)cols;
+    p.x = static_cast<const __half *>(x); p.ldx = (long long)ldx;
+    p.gamma = static_cast<const __half *>(gamma); p.eps = eps;
+    p.y = static_cast<__half *>(y); p.ldy = (long long)ldy;
+    p.flags = d->flags_dev;
+    return rc_of(b2::graph::rmsnorm(p, d->stream, d->sm_count));
+}
+
+// ----------------------------------------------------------------------------- CUDA graphs
+}  // extern "C"
+
+struct b2_exec {
+    cudaGraphExec_t exec;
+    int ordinal;
+};
+
+extern "C" {
+
+int b2d_capture_begin(b2_dev *d) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    // every launcher's one-time setup happens outside the capture
+    if (b2::gemm::prepare(d->ordinal, d->sm_count) != cudaSuccess || b2::gemv::prepare() != cudaSuccess) {
+        cudaGetLastError();
+        return ROCKET_E_UNSUPPORTED;
+    }
+    // thread-local: launches from other threads are neither recorded nor blocked
+    if (cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return ROCKET_E_UNSUPPORTED;
+    }
+    return 0;
+}
+
+int b2d_capture_end(b2_dev *d, b2_exec **out, unsigned *kernels) {
+    *out = nullptr;
+    if (kernels) *kernels = 0;
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    cudaGraph_t graph = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(d->stream, &graph);
+    if (e != cudaSuccess || !graph) {
+        cudaGetLastError();
+        if (graph) cudaGraphDestroy(graph);
+        return ROCKET_E_DEVICE;
+    }
+    size_t nodes = 0;
+    cudaGraphGetNodes(graph, nullptr, &nodes);
+    b2_exec *x = new (std::nothrow) b2_exec();
+    if (!x) {
+        cudaGraphDestroy(graph);
+        return ROCKET_E_NOMEM;
+    }
+    x->ordinal = d->ordinal;
+    const cudaError_t ie = cudaGraphInstantiate(&x->exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) {
+        cudaGetLastError();
+        delete x;
+        return rc_of(ie);
+    }
+    if (kernels) *kernels = (unsigned)nodes;
+    *out = x;
+    return 0;
+}
+
+int b2d_exec_launch(b2_dev *d, b2_exec *x) {
+    if (!set_device(d) || !x) return ROCKET_E_SHAPE;
+    if (x->ordinal != d->ordinal) return ROCKET_E_SHAPE;
+    return rc_of(cudaGraphLaunch(x->exec, d->stream));
+}
+
+void b2d_exec_destroy(b2_exec *x) {
+    if (!x) return;
+    cudaSetDevice(x->ordinal);
+    cudaGraphExecDestroy(x->exec);
+    delete x;
 }
 
 }  // extern "C"

@@ -227,6 +227,27 @@ __device__ __forceinline__ void load_bias32(const __half *bias, int cb, int n, f
     }
 }
 
+// 32 FP16 values of row `src` at columns [cb, cb+32) as floats (zero past n).
+__device__ __forceinline__ void load_half32(const __half *src, int cb, int n, bool vec, float (&r)[32]) {
+    if (vec && cb + 32 <= n) {
+        const uint4 *sp = reinterpret_cast<const uint4 *>(src + cb);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint4 u = __ldg(sp + q);
+            const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(h[e]);
+                r[8 * q + 2 * e] = f.x;
+                r[8 * q + 2 * e + 1] = f.y;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = cb + i < n ? __half2float(src[cb + i]) : 0.0f;
+    }
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t *>(&h);
@@ -261,6 +282,20 @@ __device__ __forceinline__ void store32f(float *dst, int cb, int n, bool vec, co
     }
 }
 
+// Residual add of the graph's ADD node fused into the store: pk[i] = fp16(res + pk[i]) for the 32
+// results of row `row` at columns [cb, cb+32) (the FP32 sum of two FP16 values, rounded once).
+__device__ __forceinline__ void add_residual32(const Params &p, int row, int cb, uint32_t (&pk)[16], bool &bad) {
+    float rv[32];
+    load_half32(p.res + (size_t)row * p.ldr, cb, p.N, p.vec_r, rv);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float2 y = __half22float2(*reinterpret_cast<const __half2 *>(&pk[i]));
+        const float s0 = __fadd_rn(rv[2 * i], y.x), s1 = __fadd_rn(rv[2 * i + 1], y.y);
+        bad |= f16_overflows(s0) | f16_overflows(s1);
+        pk[i] = pack_half2(s0, s1);
+    }
+}
+
 // Output tile -> (m block, n block). With group_m > 0, tiles are walked in bands of group_m
 // m-blocks so that the clusters running at the same time share X and W blocks in L2.
 __device__ __forceinline__ void tile_coords(int tile, const Params &p, int &mb, int &nb) {
@@ -278,7 +313,8 @@ __device__ __forceinline__ void tile_coords(int tile, const Params &p, int &mb, 
 }
 
 // Epilogue modes (one kernel instantiation each, so no mode branches in the hot code).
-enum : int { EPI_FP32 = 0, EPI_TILE16 = 1, EPI_RAW16 = 2, EPI_RAW32 = 3 };
+// EPI_GATED is the tile-16 fold with the gate·up product of a packed gate|up weight.
+enum : int { EPI_FP32 = 0, EPI_TILE16 = 1, EPI_RAW16 = 2, EPI_RAW32 = 3, EPI_GATED = 4 };
 
 // Epilogue warps: drain the TMEM accumulator of each finished tile (or 256-K chunk) in four
 // 32-column pieces, hand the accumulator back after the last piece is in registers, finish and
@@ -361,7 +397,48 @@ __device__ __forceinline__ void epilogue_role(const Params &p, int warp, int lan
                         bad |= f16_overflows(y0) | f16_overflows(y1);
                         pk[i] = pack_half2(y0, y1);
                     }
+                    if (p.res != nullptr && row_ok) add_residual32(p, row, cb, pk, bad);
                     if (row_ok) store32(p.y + (size_t)row * p.ldy, cb, p.N, p.vec_y, pk);
+                } else if constexpr (MODE == EPI_GATED) {
+                    // pieces 2t and 2t+1 of this half are the gate and up sums of 32 hidden columns
+                    __half2 *r = run + 16 * j;
+                    const int hb = (col0 + 32 * (j & ~1)) >> 1;   // first hidden column of the pair
+                    if (!last) {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const float2 o = first ? make_float2(0.0f, 0.0f) : __half22float2(r[i]);
+                            r[i] = __floats2half2_rn(fold16(o.x, v[2 * i], first), fold16(o.y, v[2 * i + 1], first));
+                        }
+                    } else {
+                        const __half *bsrc = (j & 1) ? p.bias2 : p.bias;
+                        float b[32];
+                        load_bias32(bsrc, hb, p.gate_n, b);
+                        const bool hasb = bsrc != nullptr;
+                        if (!(j & 1)) {
+                            // gate: finished FP16 values wait in `run` for the up piece
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const float2 o = first ? make_float2(0.0f, 0.0f) : __half22float2(r[i]);
+                                const float g0 = finish_tile16(fold16(o.x, v[2 * i], first), b[2 * i], hasb, false);
+                                const float g1 = finish_tile16(fold16(o.y, v[2 * i + 1], first), b[2 * i + 1], hasb, false);
+                                r[i] = __floats2half2_rn(g0, g1);
+                            }
+                        } else {
+                            const __half2 *g = run + 16 * (j - 1);
+                            uint32_t pk[16];
+#pragma unroll 4
+                            for (int i = 0; i < 16; ++i) {
+                                const float2 o = first ? make_float2(0.0f, 0.0f) : __half22float2(r[i]);
+                                const float u0 = finish_tile16(fold16(o.x, v[2 * i], first), b[2 * i], hasb, false);
+                                const float u1 = finish_tile16(fold16(o.y, v[2 * i + 1], first), b[2 * i + 1], hasb, false);
+                                const float2 gg = __half22float2(g[i]);
+                                const float y0 = gated16(gg.x, u0, p.gate), y1 = gated16(gg.y, u1, p.gate);
+                                bad |= f16_overflows(y0) | f16_overflows(y1);
+                                pk[i] = pack_half2(y0, y1);
+                            }
+                            if (row_ok) store32(p.y + (size_t)row * p.ldy, hb, p.gate_n, p.vec_y, pk);
+                        }
+                    }
                 } else {
                     __half2 *r = run + 16 * j;
                     if (!last) {
@@ -385,6 +462,8 @@ __device__ __forceinline__ void epilogue_role(const Params &p, int warp, int lan
                             }
                             pk[i] = pack_half2(s0, s1);
                         }
+                        if constexpr (MODE == EPI_TILE16)
+                            if (p.res != nullptr && row_ok) add_residual32(p, row, cb, pk, bad);
                         if (row_ok) store32(p.y + (size_t)row * p.ldy, cb, p.N, p.vec_y, pk);
                     }
                 }
@@ -635,14 +714,40 @@ void config_for(int M, int N, int sm_count, unsigned *tile_m, unsigned *tile_n, 
 }
 
 template <int CG, int TN, int MODE>
-static cudaError_t launch_mode(const CUtensorMap &ta, const CUtensorMap &tb, const Params &p, unsigned grid,
-                               cudaStream_t stream, int device) {
+static cudaError_t ensure_attr(int device) {
     static bool attr_done[64];
     if (!attr_done[device]) {
         const cudaError_t e = set_smem_attr<CG, TN, MODE>();
         if (e != cudaSuccess) return e;
         attr_done[device] = true;
     }
+    return cudaSuccess;
+}
+
+template <int CG, int TN>
+static cudaError_t prepare_variant(int device, int sm_count) {
+    resident_clusters<CG, TN>(sm_count);
+    cudaError_t e = cudaSuccess;
+    for (cudaError_t r : {ensure_attr<CG, TN, EPI_FP32>(device), ensure_attr<CG, TN, EPI_TILE16>(device),
+                          ensure_attr<CG, TN, EPI_RAW16>(device), ensure_attr<CG, TN, EPI_RAW32>(device),
+                          ensure_attr<CG, TN, EPI_GATED>(device)})
+        if (r != cudaSuccess) e = r;
+    return e;
+}
+
+cudaError_t prepare(int device, int sm_count) {
+    if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+    if (!encode_fn()) return cudaErrorNotSupported;
+    const cudaError_t e1 = prepare_variant<1, TILE_N>(device, sm_count);
+    const cudaError_t e2 = prepare_variant<2, TILE_N>(device, sm_count);
+    return e1 != cudaSuccess ? e1 : e2;
+}
+
+template <int CG, int TN, int MODE>
+static cudaError_t launch_mode(const CUtensorMap &ta, const CUtensorMap &tb, const Params &p, unsigned grid,
+                               cudaStream_t stream, int device) {
+    const cudaError_t e = ensure_attr<CG, TN, MODE>(device);
+    if (e != cudaSuccess) return e;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = cluster_config(CG, grid, Cfg<CG, TN>::SMEM_BYTES, stream, attr);
     return cudaLaunchKernelEx(&cfg, gemm_kernel<CG, TN, MODE>, ta, tb, p);
@@ -668,6 +773,10 @@ static cudaError_t launch_tile(const Shape &s, Params p, cudaStream_t stream, in
     if (grid_out) *grid_out = grid;
     if (p.out_mode == OUT_RAW32) return launch_mode<CG, TN, EPI_RAW32>(ta, tb, p, grid, stream, device);
     if (p.out_mode == OUT_RAW16) return launch_mode<CG, TN, EPI_RAW16>(ta, tb, p, grid, stream, device);
+    if (p.gate) {
+        if (!p.fold || p.res || p.post || p.N != 2 * ((p.gate_n + 31) / 32 * 32)) return cudaErrorInvalidValue;
+        return launch_mode<CG, TN, EPI_GATED>(ta, tb, p, grid, stream, device);
+    }
     if (p.fold) return launch_mode<CG, TN, EPI_TILE16>(ta, tb, p, grid, stream, device);
     return launch_mode<CG, TN, EPI_FP32>(ta, tb, p, grid, stream, device);
 }

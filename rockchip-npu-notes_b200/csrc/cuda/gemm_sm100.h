@@ -35,6 +35,17 @@ struct Params {
     long long route_plane;       // floats between the two parity planes
     const unsigned *route_seq;   // this rank's round counter, read by the epilogue
     int route_rows;
+    // Residual (OUT_FINAL): y = fp16(res + fp16(result)), res FP16 [M, ldr]; nullptr for none.
+    const __half *res;
+    long long ldr;
+    int vec_r;
+    // Gated output (OUT_FINAL with fold, gate != 0): W is packed in 64-row blocks, rows
+    // [64t, 64t+32) = gate rows [32t, 32t+32) and rows [64t+32, 64t+64) = up rows [32t, 32t+32),
+    // so N = 2 * roundup(gate_n, 32). Each FP16 sum is finished with its own bias (bias: gate,
+    // bias2: up; [gate_n] or nullptr) and y[r, j] = fp16(fp16(g * fp16(gate(g))) * u), j < gate_n.
+    int gate;                    // 0 none, GATE_SIGMOID (SiLU) or GATE_GELU (common.cuh)
+    int gate_n;
+    const __half *bias2;
 };
 
 struct Shape {
@@ -52,6 +63,10 @@ cudaError_t launch(const Shape &s, Params p, cudaStream_t stream, int device, in
 // A specific variant: cg CTAs per cluster (1 = 128x256 tiles, 2 = 256x256 tiles per CTA pair).
 cudaError_t launch_variant(int cg, const Shape &s, const Params &p, cudaStream_t stream, int device,
                            int sm_count, unsigned *grid_out);
+// Runs the launchers' one-time device setup (tensor-map encoder lookup, shared-memory limits,
+// co-resident cluster counts) now, so that a later launch issues no such call (a launch recorded
+// into a CUDA graph must not).
+cudaError_t prepare(int device, int sm_count);
 // Grid (CTAs) the launch would use, and its tile shape and ring depth (for reporting).
 unsigned grid_for(int M, int N, int sm_count);
 void config_for(int M, int N, int sm_count, unsigned *tile_m, unsigned *tile_n, unsigned *stages);

@@ -467,6 +467,11 @@ void plan_units(Group &g, int sm_count) {
 
 }  // namespace
 
+cudaError_t prepare() {
+    for (int m = 1; m <= MAX_M; m *= 2) direct_blocks(m);
+    return stream_attr();
+}
+
 bool streamed(int M, int K) { return M >= 1 && M <= STREAM_MAX_M && K >= 1 && K <= STREAM_MAX_K; }
 
 namespace {

@@ -58,6 +58,9 @@ bool streamed(int M, int K);
 
 // Picks the kernel for p (streamed when eligible, else the per-lane-load kernel) and launches it.
 cudaError_t launch(const Params &p, cudaStream_t stream, int sm_count, unsigned *grid_out);
+// Runs the launchers' one-time device setup (shared-memory limits, occupancy queries) now, so that
+// a later launch issues no such call (a launch recorded into a CUDA graph must not).
+cudaError_t prepare();
 // Launches the streamed kernel over g.count problems (each must satisfy streamed(g.M, K)): one
 // launch, or more when the problems' distinct x rows exceed the x table (*launches gets the count).
 cudaError_t launch_group(Group &g, cudaStream_t stream, int sm_count, unsigned *grid_out, unsigned *launches);

@@ -21,6 +21,10 @@ int oracle_linear(int mode, unsigned m, unsigned k, unsigned n, const uint16_t *
                   const uint16_t *bias, int post, uint16_t *y16, double *act, double *raw, int threads);
 double oracle_f16_to_double(uint16_t h);
 uint16_t oracle_f16_from_double(double d);
+uint16_t oracle_ew16(int op, uint16_t a, uint16_t b);
+uint16_t oracle_act16(int act, uint16_t a);
+unsigned oracle_rmsnorm(unsigned rows, unsigned cols, const uint16_t *x, const uint16_t *gamma, float eps,
+                        uint16_t *y);
 
 enum { ORACLE_TILE16_EXACT = 0, ORACLE_FP32ACC = 5 };
 
@@ -112,7 +116,58 @@ static float finish32(float acc, const uint16_t *bias, unsigned col, int post) {
     return a;
 }
 
+static int linear_plain(b2_dev *d, const b2k_linear *a, unsigned *launches);
+
+/* Gated pair: the folded FP16 sums of the packed gate|up weight, each finished with its half's
+ * bias, combined as fp16(fp16(g * fp16(gate(g))) * u) -- the arithmetic of the fused epilogue. */
+static int linear_gated(b2_dev *d, const b2k_linear *a, unsigned *launches) {
+    const unsigned h = a->gate_n, h32 = (h + 31) / 32 * 32;
+    if ((a->gate != 1 && a->gate != 2) || a->acc || a->post || a->res || a->raw_only || !h || a->n != 2 * h32 ||
+        !a->y || a->ldy < h)
+        return ROCKET_E_SHAPE;
+    uint16_t *sums = malloc((size_t)a->m * a->n * 2);
+    if (!sums) return ROCKET_E_NOMEM;
+    b2k_linear raw = *a;
+    raw.gate = 0;
+    raw.bias = NULL;
+    raw.fused = 1;
+    raw.y = sums;
+    raw.ldy = a->n;
+    int rc = linear_plain(d, &raw, launches);
+    const uint16_t *bg = a->bias, *bu = a->bias2;
+    for (unsigned r = 0; !rc && r < a->m; r++)
+        for (unsigned j = 0; j < h; j++) {
+            uint16_t g = sums[(size_t)r * a->n + 64 * (j / 32) + j % 32];
+            uint16_t u = sums[(size_t)r * a->n + 64 * (j / 32) + 32 + j % 32];
+            if (bg) g = oracle_ew16(0, g, bg[j]);
+            if (bu) u = oracle_ew16(0, u, bu[j]);
+            const uint16_t o = oracle_ew16(1, oracle_act16(a->gate, g), u);
+            if (f16_nonfinite(o)) d->status |= B2D_ST_NONFINITE_OUTPUT;
+            ((uint16_t *)a->y)[(size_t)r * a->ldy + j] = o;
+        }
+    free(sums);
+    if (!rc) *launches = (a->fused && a->m > B2D_GEMV_MAX_M) ? 1 : 2;
+    return rc;
+}
+
 int b2d_linear(b2_dev *d, const b2k_linear *a, unsigned *launches) {
+    *launches = 0;
+    if (!d || !a) return ROCKET_E_SHAPE;
+    if (a->gate) return linear_gated(d, a, launches);
+    int rc = linear_plain(d, a, launches);
+    if (!rc && a->res) {   /* y = fp16(res + y) */
+        for (unsigned r = 0; r < a->m; r++)
+            for (unsigned c = 0; c < a->n; c++) {
+                uint16_t *y = (uint16_t *)a->y + (size_t)r * a->ldy + c;
+                *y = oracle_ew16(0, *y, ((const uint16_t *)a->res)[(size_t)r * a->ldr + c]);
+                if (f16_nonfinite(*y)) d->status |= B2D_ST_NONFINITE_OUTPUT;
+            }
+        if (!(a->fused && a->m > B2D_GEMV_MAX_M)) *launches += 1;
+    }
+    return rc;
+}
+
+static int linear_plain(b2_dev *d, const b2k_linear *a, unsigned *launches) {
     *launches = 0;
     if (!d || !a || !a->m || !a->n || !a->k || !a->x || !a->w) return ROCKET_E_SHAPE;
     uint16_t *x = pack(a->x, a->m, a->k, a->ldx), *w = pack(a->w, a->n, a->k, a->ldw);
@@ -286,3 +341,49 @@ int b2d_ksplit_round(b2_dev *d, const b2k_linear *a, const b2k_ksplit *ks, unsig
     if (!rc) *launches = 3;
     return rc;
 }
+
+/* ---------------------------------------------------------------------- graph node kernels */
+int b2d_elementwise(b2_dev *d, int op, unsigned rows, unsigned cols, const void *a, size_t lda, const void *b,
+                    size_t ldb, void *y, size_t ldy) {
+    const int bin = op == B2D_EW_ADD || op == B2D_EW_MUL;
+    if (!d || op < B2D_EW_ADD || op > B2D_EW_HSIG || !a || !y || lda < cols || ldy < cols || (bin && (!b || ldb < cols)))
+        return ROCKET_E_SHAPE;
+    for (unsigned r = 0; r < rows; r++)
+        for (unsigned c = 0; c < cols; c++) {
+            const uint16_t av = ((const uint16_t *)a)[(size_t)r * lda + c];
+            const uint16_t bv = bin ? ((const uint16_t *)b)[(size_t)r * ldb + c] : 0;
+            const uint16_t o = oracle_ew16(op, av, bv);
+            if (f16_nonfinite(o)) d->status |= B2D_ST_NONFINITE_OUTPUT;
+            ((uint16_t *)y)[(size_t)r * ldy + c] = o;
+        }
+    return 0;
+}
+
+int b2d_rmsnorm(b2_dev *d, unsigned rows, unsigned cols, const void *x, size_t ldx, const void *gamma, float eps,
+                void *y, size_t ldy) {
+    if (!d || !x || !y || !gamma || !(eps > 0.0f) || ldx < cols || ldy < cols) return ROCKET_E_SHAPE;
+    uint16_t *in = pack(x, rows, cols, ldx), *out = malloc((size_t)rows * cols * 2 + 2);
+    if (!in || !out) {
+        free(in);
+        free(out);
+        return ROCKET_E_NOMEM;
+    }
+    memset(out, 0, (size_t)rows * cols * 2);
+    if (oracle_rmsnorm(rows, cols, in, gamma, eps, out)) d->status |= B2D_ST_NONFINITE_INPUT;
+    for (unsigned r = 0; r < rows; r++) memcpy((uint16_t *)y + (size_t)r * ldy, out + (size_t)r * cols, (size_t)cols * 2);
+    free(in);
+    free(out);
+    return 0;
+}
+
+/* ---------------------------------------------------------------------- CUDA graphs
+ * Every mock operation completes at once, so there is nothing to record: capture is reported
+ * unavailable and the host issues the launches directly. */
+int b2d_capture_begin(b2_dev *d) { return d ? ROCKET_E_UNSUPPORTED : ROCKET_E_DEVICE; }
+int b2d_capture_end(b2_dev *d, b2_exec **out, unsigned *kernels) {
+    *out = NULL;
+    if (kernels) *kernels = 0;
+    return ROCKET_E_DEVICE;
+}
+int b2d_exec_launch(b2_dev *d, b2_exec *x) { return ROCKET_E_SHAPE; }
+void b2d_exec_destroy(b2_exec *x) { (void)x; }
