@@ -20,6 +20,10 @@ scaling, one process per GPU).
             by NCCL all-reduce / reduce-scatter, then the epilogue).
   gemv      M=1 decode projections of a SmolLM-135M-shaped layer (HBM GB/s per launch, weights
             rotated over > 4x L2).
+  graph_ffn the SwiGLU FFN Y = X + Linear(SiLU(Linear(X, Wg, b)) * Linear(X, Wu), Wd) through the
+            static graph compiler (co_graph_*) at m = d = h = 4096 and at m = 8 / m = 1: CO_CHAIN
+            (fused gate·up GEMM + residual epilogue, one CUDA graph) against CO_SEPARATE, L2
+            flushed between steps, plus co_graph_run end to end.
   cpu_baseline  the oracle's restatement of the reference arithmetic (per-256-K FP16 running
             sum, tile16_fast) on a bounded row sample, all host threads.
 
@@ -187,6 +191,7 @@ def main():
     ap.add_argument("--no-gemv", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-sharded", action="store_true")
+    ap.add_argument("--no-graph", action="store_true")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
@@ -306,6 +311,11 @@ def main():
     if rank == 0 and world == 1 and not args.no_gemv:
         gemv = bench_gemv(b2, fd, torch, stream, peak_gbs)
 
+    # ---------------------------------------------------------------- graph FFN (rank 0, N=1 only)
+    graph = None
+    if rank == 0 and world == 1 and not args.no_graph:
+        graph = bench_graph(b2, fd, torch, stream, peak_tflops, peak_gbs)
+
     line = None
     if rank == 0:
         traffic = traffic_per_launch()
@@ -334,6 +344,8 @@ def main():
             line["sharded"] = shard
         if gemv:
             line["gemv"] = gemv
+        if graph:
+            line["graph_ffn"] = graph
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_sample()
     b2.close(fd)
@@ -356,7 +368,8 @@ def _timed_steps(torch, dist, world, stream, fn, warmup, steps, flush=None):
     with ClockSampler(torch.cuda.current_device()) as clocks:
         for _ in range(steps):
             if flush is not None:
-                flush.zero_()
+                with torch.cuda.stream(stream):   # on the launching stream: done before the start event
+                    flush.zero_()
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(stream)
             fn()
@@ -490,6 +503,91 @@ def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup,
     fk.destroy()
     del x, xs, y, flush
     torch.cuda.empty_cache()
+    return out
+
+
+def bench_graph(b2, fd, torch, stream, peak_tflops, peak_gbs):
+    """The SwiGLU FFN of the reference's graph CLI (research/custom-ops/tools/c/graph_cli.c:67-74),
+    Y = X + Linear(SiLU(Linear(X, Wg, b)) * Linear(X, Wu), Wd), through the static graph compiler
+    (co_graph_*) at the reference graph API's largest shape (m = d = h = 4096) and at decode (m = 8,
+    m = 1). Device-resident: b2_graph_launch timed with CUDA events per step, L2 flushed between steps,
+    in CO_CHAIN (gate·up pair as ONE tcgen05 GEMM with the SiLU product in its epilogue, the residual
+    in the down projection's epilogue, replayed as one CUDA graph) and CO_SEPARATE (one kernel per node,
+    Linear = GEMM + separate epilogue). End to end: co_graph_run with pinned host X / Y. Rows of Y are
+    checked against the oracle (every node with the reference's arithmetic)."""
+    import numpy as np
+    import oracle
+    G = importlib.import_module("rockchip-npu-notes_b200.graph")
+    l2 = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
+    flush = torch.empty(2 * l2, dtype=torch.uint8, device="cuda")
+    d = h = 4096
+    rng = np.random.default_rng(4096)
+    wg = (rng.standard_normal((h, d), np.float32) / 64).astype(np.float16)
+    wu = (rng.standard_normal((h, d), np.float32) / 64).astype(np.float16)
+    wd = (rng.standard_normal((d, h), np.float32) / 64).astype(np.float16)
+    bias = (rng.standard_normal(h, np.float32) * 0.1).astype(np.float16)
+    out = {"d": d, "h": h, "timing": "b2_graph_launch, CUDA events per step, L2 flushed between steps",
+           "cases": {}}
+    for m in (4096, 8, 1):
+        x = (np.random.default_rng(m).standard_normal((m, d), np.float32) * 0.7).astype(np.float16)
+        nodes, o = G.swiglu_ffn(m, d, h, wg, wu, wd, bias)
+        flops = 6 * m * d * h
+        wbytes = 3 * d * h * 2
+        case, ys = {"m": m, "flops": flops}, {}
+        for name, mode in (("chain", b2.CO_CHAIN), ("separate", b2.CO_SEPARATE)):
+            g = G.Graph(fd, nodes, o, mode, budget=4 << 30)
+            ys[name] = g.run({0: x})
+            steps = 30 if m > 8 else 200
+            ms, clocks = _timed_steps(torch, None, 1, stream, g.launch, 3, steps, flush)
+            b2.sync(fd)
+            if g.status():
+                raise RuntimeError(f"graph FFN m={m} {name}: device status raised")
+            info = g.info()
+            case[name] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "kernels": info["kernels"],
+                          "cuda_graph": bool(info["captured"]), "gated_fused": info["gated"],
+                          "residual_fused": info["residual"], "clocks": clocks}
+            if m <= 8:
+                case[name]["weight_gb_s"] = wbytes / (ms * 1e-3) / 1e9
+                case[name]["frac_of_hbm"] = wbytes / (ms * 1e-3) / 1e9 / peak_gbs
+            else:
+                case[name]["frac_of_peak"] = flops / (ms * 1e-3) / 1e12 / peak_tflops
+            if name == "chain":
+                hx = b2.lib().b2_host_alloc(m * d * 2)
+                hy = b2.lib().b2_host_alloc(m * d * 2)
+                xh = np.ctypeslib.as_array(ctypes.cast(hx, ctypes.POINTER(ctypes.c_uint16)), shape=(m, d))
+                yh = np.ctypeslib.as_array(ctypes.cast(hy, ctypes.POINTER(ctypes.c_uint16)), shape=(m, d))
+                xh[:] = x.view(np.uint16)
+                for _ in range(3):
+                    rc, _ = g.run_rc({0: xh.view(np.float16)}, {o: yh.view(np.float16)})
+                    b2.check("co_graph_run_many", rc)
+                reps = 10 if m > 8 else 100
+                es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                es.record(stream)
+                for _ in range(reps):
+                    g.run_rc({0: xh.view(np.float16)}, {o: yh.view(np.float16)})
+                ee.record(stream)
+                ee.synchronize()
+                e2e = es.elapsed_time(ee) / reps
+                case["e2e"] = {"ms": e2e, "tflops": flops / (e2e * 1e-3) / 1e12, "api": "co_graph_run (pinned host X/Y)",
+                               "h2d_bytes_per_step": m * d * 2, "d2h_bytes_per_step": m * d * 2}
+                b2.lib().b2_host_free(hx)
+                b2.lib().b2_host_free(hy)
+            g.destroy()
+        if not np.array_equal(ys["chain"].view(np.uint16), ys["separate"].view(np.uint16)):
+            raise RuntimeError(f"graph FFN m={m}: CO_CHAIN and CO_SEPARATE differ")
+        rows = np.arange(0, m, max(1, m // 4))[:4]
+        t0 = time.time()
+        ref = oracle.ffn(x[rows], wg, wu, wd, bias)
+        cpu_s = time.time() - t0
+        ok, worst = oracle.tolerance_ok(ys["chain"][rows], ref)
+        if not ok:
+            raise RuntimeError(f"graph FFN m={m} outside tolerance (worst err/tol {worst:.3f})")
+        case["spot_check"] = {"rows": int(rows.size), "worst_err_over_tol": worst,
+                              "chain_equals_separate": True}
+        case["cpu_oracle"] = {"rows": int(rows.size), "s": cpu_s, "kind": "port",
+                              "tflops": 6 * rows.size * d * h / cpu_s / 1e12, "cores": os.cpu_count()}
+        out["cases"][str(m)] = case
+    del flush
     return out
 
 

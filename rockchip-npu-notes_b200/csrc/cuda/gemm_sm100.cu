@@ -7,7 +7,7 @@
 // with one launch. Two variants share the code (template CG = CTA group):
 //   CG=2  a cluster of two CTAs on a TPC computes a 256x256 output tile with the 2-SM UMMA
 //         (tcgen05.mma.cta_group::2, M=256 N=256 K=16): each CTA stages its own 128 rows of X and
-//         128 rows of W per 64-wide K block (32 KB, 7-stage ring), so per SM the shared-memory
+//         128 rows of W per 64-wide K block (32 KB, 6-stage ring), so per SM the shared-memory
 //         and L2 traffic per FLOP is two thirds of the single-SM tile. Used for M > 128.
 //   CG=1  one CTA computes a 128x256 tile with tcgen05.mma.cta_group::1 (48 KB, 4-stage ring).
 // Roles per CTA (384 threads):
@@ -17,12 +17,18 @@
 //               256-column TMEM accumulators; tcgen05.commit (multicast to both CTAs of a pair)
 //               frees ring stages and publishes finished accumulators
 //   warp 2      TMEM allocator (512 columns)
-//   warps 4-11  epilogue: tcgen05.ld of their 32-lane quarter and 128-column half, then
-//                 - FP32 mode: y = fp16(act(acc + b)), or
-//                 - tile-16 mode (the reference's FP16-K-TILING numerics): the MMA warp closes an
-//                   accumulator every 256 K, the epilogue folds run = fp16(run + chunk) in
-//                   registers and finishes with affine = fp16(run + b), y = fp16(hsig(affine));
-//               16-byte stores to global.
+//   warps 4-11  epilogue, each on its 32-lane TMEM quarter and 128-column half:
+//                 - FP32 mode: tcgen05.ld, y = fp16(act(acc + b)) (+ residual);
+//                 - tile-16 modes (the reference's FP16-K-TILING numerics): the MMA warp closes an
+//                   accumulator every 256 K; the epilogue folds run = fp16(run + chunk) with packed
+//                   FP32 adds into 64 registers (unrolled, the TMEM loads software-pipelined) and
+//                   hands the accumulator straight back -- the last chunk's too -- then finishes
+//                   the tile from registers (affine = fp16(run + b), HardSigmoid, residual, or the
+//                   gate·up product of a packed gate|up weight) while the MMA warp starts the next
+//                   tile: with only two accumulators a finish that held one would stall the MMAs;
+//               FP16 results leave through one TMA tile store per warp and 32x32 box (staged in
+//               2 KB of shared memory per warp), or per-thread 16-byte stores where Y does not
+//               allow a tensor map.
 // Tiles are scheduled persistently (cluster c takes tiles c, c + clusters, ...) so the TMA/MMA of
 // the next tile overlaps the epilogue of the previous one through the two TMEM accumulators.
 //
@@ -32,6 +38,7 @@
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "gemm_sm100.h"
@@ -54,9 +61,11 @@ struct Cfg {
     static constexpr uint32_t A_BYTES = 128 * BK * 2;
     static constexpr uint32_t B_BYTES = B_ROWS * BK * 2;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (int)((SMEM_LIMIT - 1024 - 512) / STAGE_BYTES);
+    // output staging of the TMA tile stores: one 32 x 32 FP16 box (2 KB) per epilogue warp
+    static constexpr uint32_t OUT_BYTES = EPI_WARPS * 32 * 64;
+    static constexpr int STAGES = (int)((SMEM_LIMIT - 1024 - 512 - OUT_BYTES) / STAGE_BYTES);
     static constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1;
-    static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + NUM_BARS * 8 + 16;
+    static constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + 1024 + NUM_BARS * 8 + 16;
     static constexpr uint32_t TMEM_COLS = 2 * TN;       // two accumulators (power of two >= 32)
     // Instruction descriptor, kind::f16: D=F32 (bits 4-5 = 1), A=B=F16 (0), both K-major,
     // N>>3 at bits 17-22, M>>4 at bits 24-28.
@@ -282,6 +291,143 @@ __device__ __forceinline__ void store32f(float *dst, int cb, int n, bool vec, co
     }
 }
 
+// The tile-16 running sum of a thread's 128 columns is 64 half2 registers; piece j (a rolled loop)
+// owns [16j, 16j+16). Reading and writing a piece through these selects (static indices only)
+// keeps the array in registers -- indexed by j it would live in local memory, and with the ring
+// holding 227 KB of shared memory the L1 is too small to keep it: every 256-K chunk would move
+// 128 KB per CTA through L2.
+template <int N>
+__device__ __forceinline__ void run_get(const __half2 (&run)[N], int j, __half2 (&cur)[16]) {
+#pragma unroll
+    for (int q = 0; q < N / 16; ++q)
+        if (q == j) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) cur[i] = run[16 * q + i];
+        }
+}
+template <int N>
+__device__ __forceinline__ void run_put(__half2 (&run)[N], int j, const __half2 (&cur)[16]) {
+#pragma unroll
+    for (int q = 0; q < N / 16; ++q)
+        if (q == j) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) run[16 * q + i] = cur[i];
+        }
+}
+
+// Two FP32 adds in one instruction (sm_100 packed FP32), each rounded to nearest like __fadd_rn.
+__device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
+    uint64_t x, y, r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a.x), "f"(a.y));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b.x), "f"(b.y));
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+    float2 o;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(r));
+    return o;
+}
+
+// 16 FP32 columns of this thread's TMEM lane, issued without waiting: the registers are valid only
+// after tmem_wait16 on the same array (which names them as in/out operands, so no use of them can
+// be scheduled before the wait).
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait16(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                   "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                   "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+
+// Folds 16 columns (8 packed pairs) of a 256-K chunk into run[8j, 8j+8).
+template <int N>
+__device__ __forceinline__ void fold16x(__half2 (&run)[N], int j, const uint32_t (&r)[16], bool first) {
+    if (first) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            run[8 * j + i] = __floats2half2_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float2 s = fadd2_rn(__half22float2(run[8 * j + i]),
+                                      make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])));
+            run[8 * j + i] = __floats2half2_rn(s.x, s.y);
+        }
+    }
+}
+
+// One fold-only 256-K chunk of the tile-16 modes over this thread's HALF columns: run =
+// fp16(chunk) for the first chunk, else fp16(run + chunk) (fold16, two columns per packed add and
+// one packing conversion). Unrolled, so every index into `run` is static, and software-pipelined:
+// the TMEM load of the next 16 columns is in flight while the current ones are folded. The
+// accumulator is handed back (release) as soon as its last columns are in registers.
+template <int HALF, int N, typename Release>
+__device__ __forceinline__ void fold_chunk(__half2 (&run)[N], uint32_t taddr, bool first, Release release) {
+    constexpr int SUB = HALF / 16;
+    uint32_t a[16], b[16];
+    tmem_ld16_async(taddr, a);
+    tmem_wait16(a);
+#pragma unroll
+    for (int j = 0; j < SUB; ++j) {
+        uint32_t (&cur)[16] = (j & 1) ? b : a;
+        uint32_t (&nxt)[16] = (j & 1) ? a : b;
+        if (j + 1 < SUB) tmem_ld16_async(taddr + 16 * (j + 1), nxt);
+        else release();
+        fold16x(run, j, cur, first);
+        if (j + 1 < SUB) tmem_wait16(nxt);
+    }
+}
+
+// Hands a drained TMEM accumulator back to the MMA warp (the leader CTA's barrier for a pair).
+template <int CG>
+__device__ __forceinline__ void release_acc(int lane, uint32_t tempty_leader, uint32_t tempty0, uint32_t acc) {
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+        if constexpr (CG == 2) mbar_arrive_cluster(tempty_leader + 8 * acc);
+        else mbar_arrive(tempty0 + 8 * acc);
+    }
+}
+
+// 32 FP16 results of this thread's row at output columns [x, x+32) (n_out columns in all). With
+// p.tma_y the warp writes its 32 rows into its 2 KB staging box (64-byte swizzle: 16-byte chunk q of
+// row r at chunk q ^ ((r >> 1) & 3), so the eight rows of each store phase hit distinct banks) and
+// one lane issues a TMA tile store of the box (coalesced 64-byte row writes, asynchronous; rows past
+// M and columns past n_out are clipped by the tensor map). Otherwise each thread stores its row.
+__device__ __forceinline__ void store_out(const Params &p, const CUtensorMap *tmap_y, uint32_t stage, int lane,
+                                          int row, bool row_ok, int x, int n_out, const uint32_t (&pk)[16]) {
+    if (p.tma_y) {
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // box free again
+        __syncwarp();
+        const uint32_t base = stage + (uint32_t)lane * 64;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(base + ((q ^ ((lane >> 1) & 3)) << 4)),
+                         "r"(pk[4 * q]), "r"(pk[4 * q + 1]), "r"(pk[4 * q + 2]), "r"(pk[4 * q + 3])
+                         : "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        const int row0 = row - lane;
+        if (lane == 0 && row0 < p.M && x < n_out) {
+            asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                             reinterpret_cast<uint64_t>(tmap_y)),
+                         "r"(x), "r"(row0), "r"(stage)
+                         : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+    } else if (row_ok) {
+        store32(p.y + (size_t)row * p.ldy, x, n_out, p.vec_y, pk);
+    }
+}
+
 // Residual add of the graph's ADD node fused into the store: pk[i] = fp16(res + pk[i]) for the 32
 // results of row `row` at columns [cb, cb+32) (the FP32 sum of two FP16 values, rounded once).
 __device__ __forceinline__ void add_residual32(const Params &p, int row, int cb, uint32_t (&pk)[16], bool &bad) {
@@ -316,18 +462,156 @@ __device__ __forceinline__ void tile_coords(int tile, const Params &p, int &mb, 
 // EPI_GATED is the tile-16 fold with the gate·up product of a packed gate|up weight.
 enum : int { EPI_FP32 = 0, EPI_TILE16 = 1, EPI_RAW16 = 2, EPI_RAW32 = 3, EPI_GATED = 4 };
 
+// 16 bias values as packed pairs for columns [cb, cb+32) (zero past n or without bias).
+__device__ __forceinline__ void load_bias_pairs(const __half *bias, int cb, int n, __half2 (&b)[16]) {
+    if (bias && cb + 32 <= n) {
+        const uint4 *bp = reinterpret_cast<const uint4 *>(bias + cb);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint4 u = __ldg(bp + q);
+            const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) b[4 * q + e] = h[e];
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const __half lo = (bias && cb + 2 * i < n) ? bias[cb + 2 * i] : __float2half(0.0f);
+            const __half hi = (bias && cb + 2 * i + 1 < n) ? bias[cb + 2 * i + 1] : __float2half(0.0f);
+            b[i] = __halves2half2(lo, hi);
+        }
+    }
+}
+
+// FP32-mode finish of 32 accumulators: y = fp16(POST ? hsig(acc + b) : acc + b) (finish_fp32),
+// specialised on POST for the same reason as finish_piece16.
+template <bool POST>
+__device__ __forceinline__ void finish_piece32(const float (&v)[32], const float (&b)[32], uint32_t (&pk)[16],
+                                               bool &bad) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        float y0 = __fadd_rn(v[2 * i], b[2 * i]), y1 = __fadd_rn(v[2 * i + 1], b[2 * i + 1]);
+        if constexpr (POST) {
+            y0 = hsig(y0);
+            y1 = hsig(y1);
+        }
+        bad |= f16_overflows(y0) | f16_overflows(y1);
+        pk[i] = pack_half2(y0, y1);
+    }
+}
+
+// Finish of 32 columns from their folded FP16 sums r, specialised on the operator's uniform choices
+// so that no element evaluates a bias add or HardSigmoid it does not use (a per-element branch on
+// them is if-converted into computing both sides): affine = BIAS ? fp16(run + b) : run, then
+// POST ? fp16(hsig(affine)) : affine -- finish_tile16 of common.cuh.
+template <bool BIAS, bool POST>
+__device__ __forceinline__ void finish_piece16(const __half2 (&r)[16], const __half2 (&b)[16], uint32_t (&pk)[16],
+                                               bool &bad) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        if constexpr (!BIAS && !POST) {
+            pk[i] = *reinterpret_cast<const uint32_t *>(&r[i]);
+            bad |= half_nonfinite(__low2half(r[i])) | half_nonfinite(__high2half(r[i]));
+        } else {
+            float2 s = __half22float2(r[i]);
+            if constexpr (BIAS) {
+                const float2 bb = __half22float2(b[i]);
+                s = make_float2(round16(__fadd_rn(s.x, bb.x)), round16(__fadd_rn(s.y, bb.y)));
+            }
+            if constexpr (POST) s = make_float2(hsig(s.x), hsig(s.y));
+            bad |= f16_overflows(s.x) | f16_overflows(s.y);
+            pk[i] = pack_half2(s.x, s.y);
+        }
+    }
+}
+
+// The gate·up product of 32 hidden columns from their folded gate sums g and up sums u, each finished
+// with its bias when it has one.
+template <bool BG, bool BU>
+__device__ __forceinline__ void gated_piece(const __half2 (&g)[16], const __half2 (&u)[16], const __half2 (&bg)[16],
+                                            const __half2 (&bu)[16], int act, uint32_t (&pk)[16], bool &bad) {
+#pragma unroll 4
+    for (int i = 0; i < 16; ++i) {
+        float2 gs = __half22float2(g[i]), us = __half22float2(u[i]);
+        if constexpr (BG) {
+            const float2 b = __half22float2(bg[i]);
+            gs = make_float2(round16(__fadd_rn(gs.x, b.x)), round16(__fadd_rn(gs.y, b.y)));
+        }
+        if constexpr (BU) {
+            const float2 b = __half22float2(bu[i]);
+            us = make_float2(round16(__fadd_rn(us.x, b.x)), round16(__fadd_rn(us.y, b.y)));
+        }
+        const float y0 = gated16(gs.x, us.x, act), y1 = gated16(gs.y, us.y, act);
+        bad |= f16_overflows(y0) | f16_overflows(y1);
+        pk[i] = pack_half2(y0, y1);
+    }
+}
+
+// The finish of a tile-16 tile from its folded FP16 sums in `run` (this thread's row, HALF columns
+// from col0), after the last chunk's accumulator was handed back:
+//   EPI_TILE16  y = fp16(hsig?(fp16(run + b))) (+ residual), the reference's EW bias then LUT
+//   EPI_RAW16   y = run (the separate epilogue kernel finishes it)
+//   EPI_GATED   pieces 2t / 2t+1 are the gate / up sums of 32 hidden columns:
+//               y[hb + i] = fp16(fp16(g * fp16(gate(g))) * u), g and u finished with their biases
+template <int MODE, int N>
+__device__ __forceinline__ void finish_tile(const Params &p, const __half2 (&run)[N], int row, bool row_ok, int col0,
+                                            bool &bad, const CUtensorMap *tmap_y, uint32_t stage, int lane) {
+    constexpr int PIECES = N / 16;
+#pragma unroll 1
+    for (int j = 0; j < PIECES; ++j) {
+        if constexpr (MODE == EPI_GATED)
+            if (!(j & 1)) continue;   // each gate piece is finished together with its up piece
+        __half2 r[16];
+        run_get(run, j, r);
+        uint32_t pk[16];
+        if constexpr (MODE == EPI_GATED) {
+            __half2 g[16], bg[16], bu[16];
+            run_get(run, j - 1, g);
+            const int hb = (col0 + 32 * (j - 1)) >> 1;
+            load_bias_pairs(p.bias, hb, p.gate_n, bg);
+            load_bias_pairs(p.bias2, hb, p.gate_n, bu);
+            if (p.bias) {
+                if (p.bias2) gated_piece<true, true>(g, r, bg, bu, p.gate, pk, bad);
+                else gated_piece<true, false>(g, r, bg, bu, p.gate, pk, bad);
+            } else {
+                if (p.bias2) gated_piece<false, true>(g, r, bg, bu, p.gate, pk, bad);
+                else gated_piece<false, false>(g, r, bg, bu, p.gate, pk, bad);
+            }
+            store_out(p, tmap_y, stage, lane, row, row_ok, hb, p.gate_n, pk);
+        } else {
+            const int cb = col0 + 32 * j;
+            if constexpr (MODE == EPI_TILE16) {
+                __half2 b[16];
+                if (p.bias) {
+                    load_bias_pairs(p.bias, cb, p.N, b);
+                    if (p.post) finish_piece16<true, true>(r, b, pk, bad);
+                    else finish_piece16<true, false>(r, b, pk, bad);
+                } else {
+                    if (p.post) finish_piece16<false, true>(r, b, pk, bad);
+                    else finish_piece16<false, false>(r, b, pk, bad);
+                }
+                if (p.res != nullptr && row_ok) add_residual32(p, row, cb, pk, bad);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) pk[i] = *reinterpret_cast<const uint32_t *>(&r[i]);
+            }
+            store_out(p, tmap_y, stage, lane, row, row_ok, cb, p.N, pk);
+        }
+    }
+}
+
 // Epilogue warps: drain the TMEM accumulator of each finished tile (or 256-K chunk) in four
 // 32-column pieces, hand the accumulator back after the last piece is in registers, finish and
 // store. The loops stay rolled so the code of the persistent kernel fits the instruction cache.
 template <int CG, int TN, int MODE>
 __device__ __forceinline__ void epilogue_role(const Params &p, int warp, int lane, uint32_t rank, int cluster_id,
                                               int num_clusters, int nchunks, uint32_t tmem_base, uint32_t tfull0,
-                                              uint32_t tempty0, volatile int *abort_flag) {
+                                              uint32_t tempty0, volatile int *abort_flag,
+                                              const CUtensorMap *tmap_y, uint32_t stage) {
     using C = Cfg<CG, TN>;
     constexpr int HALF = TN / 2, PIECES = HALF / 32;
     const int quarter = warp & 3;          // TMEM lanes [32*quarter, 32*quarter + 32)
     const int half = (warp - 4) >> 2;      // columns [HALF*half, HALF*half + HALF) of the tile
-    const bool has_bias = p.bias != nullptr;
     const uint32_t tempty_leader = CG == 2 ? map_to_rank(tempty0, 0) : tempty0;
     uint32_t acc_used = 0;
     bool ok = true, bad = false;
@@ -351,18 +635,18 @@ __device__ __forceinline__ void epilogue_role(const Params &p, int warp, int lan
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * TN + half * HALF;
             const bool first = c == 0, last = c == nchunks - 1;
+            if constexpr (MODE == EPI_TILE16 || MODE == EPI_RAW16 || MODE == EPI_GATED) {
+                // Every 256-K chunk, the last included, is folded into `run` and its accumulator handed
+                // back at once; the tile's finish then runs from registers while the MMA warp already
+                // works on the next tile (with two accumulators it needs this one back within a chunk).
+                fold_chunk<HALF>(run, taddr, first, [&] { release_acc<CG>(lane, tempty_leader, tempty0, acc); });
+                if (last) finish_tile<MODE>(p, run, row, row_ok, col0, bad, tmap_y, stage, lane);
+            } else {
 #pragma unroll 1
             for (int j = 0; j < PIECES; ++j) {
                 float v[32];
                 tmem_ld32(taddr + j * 32, v);
-                if (j == PIECES - 1) {   // accumulator drained into registers: hand it back
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) {
-                        if constexpr (CG == 2) mbar_arrive_cluster(tempty_leader + 8 * acc);
-                        else mbar_arrive(tempty0 + 8 * acc);
-                    }
-                }
+                if (j == PIECES - 1) release_acc<CG>(lane, tempty_leader, tempty0, acc);   // drained into registers
                 const int cb = col0 + 32 * j;
                 if constexpr (MODE == EPI_RAW32) {
                     if (p.route_rows > 0) {
@@ -386,91 +670,21 @@ __device__ __forceinline__ void epilogue_role(const Params &p, int warp, int lan
                     } else if (row_ok) {
                         store32f(p.partial + (size_t)row * p.ldp, cb, p.N, p.vec_p, v);
                     }
-                } else if constexpr (MODE == EPI_FP32) {
+                } else {
                     float b[32];
                     load_bias32(p.bias, cb, p.N, b);
                     uint32_t pk[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float y0 = finish_fp32(v[2 * i], b[2 * i], p.post);
-                        const float y1 = finish_fp32(v[2 * i + 1], b[2 * i + 1], p.post);
-                        bad |= f16_overflows(y0) | f16_overflows(y1);
-                        pk[i] = pack_half2(y0, y1);
-                    }
+                    if (p.post) finish_piece32<true>(v, b, pk, bad);
+                    else finish_piece32<false>(v, b, pk, bad);
                     if (p.res != nullptr && row_ok) add_residual32(p, row, cb, pk, bad);
-                    if (row_ok) store32(p.y + (size_t)row * p.ldy, cb, p.N, p.vec_y, pk);
-                } else if constexpr (MODE == EPI_GATED) {
-                    // pieces 2t and 2t+1 of this half are the gate and up sums of 32 hidden columns
-                    __half2 *r = run + 16 * j;
-                    const int hb = (col0 + 32 * (j & ~1)) >> 1;   // first hidden column of the pair
-                    if (!last) {
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const float2 o = first ? make_float2(0.0f, 0.0f) : __half22float2(r[i]);
-                            r[i] = __floats2half2_rn(fold16(o.x, v[2 * i], first), fold16(o.y, v[2 * i + 1], first));
-                        }
-                    } else {
-                        const __half *bsrc = (j & 1) ? p.bias2 : p.bias;
-                        float b[32];
-                        load_bias32(bsrc, hb, p.gate_n, b);
-                        const bool hasb = bsrc != nullptr;
-                        if (!(j & 1)) {
-                            // gate: finished FP16 values wait in `run` for the up piece
-#pragma unroll
-                            for (int i = 0; i < 16; ++i) {
-                                const float2 o = first ? make_float2(0.0f, 0.0f) : __half22float2(r[i]);
-                                const float g0 = finish_tile16(fold16(o.x, v[2 * i], first), b[2 * i], hasb, false);
-                                const float g1 = finish_tile16(fold16(o.y, v[2 * i + 1], first), b[2 * i + 1], hasb, false);
-                                r[i] = __floats2half2_rn(g0, g1);
-                            }
-                        } else {
-                            const __half2 *g = run + 16 * (j - 1);
-                            uint32_t pk[16];
-#pragma unroll 4
-                            for (int i = 0; i < 16; ++i) {
-                                const float2 o = first ? make_float2(0.0f, 0.0f) : __half22float2(r[i]);
-                                const float u0 = finish_tile16(fold16(o.x, v[2 * i], first), b[2 * i], hasb, false);
-                                const float u1 = finish_tile16(fold16(o.y, v[2 * i + 1], first), b[2 * i + 1], hasb, false);
-                                const float2 gg = __half22float2(g[i]);
-                                const float y0 = gated16(gg.x, u0, p.gate), y1 = gated16(gg.y, u1, p.gate);
-                                bad |= f16_overflows(y0) | f16_overflows(y1);
-                                pk[i] = pack_half2(y0, y1);
-                            }
-                            if (row_ok) store32(p.y + (size_t)row * p.ldy, hb, p.gate_n, p.vec_y, pk);
-                        }
-                    }
-                } else {
-                    __half2 *r = run + 16 * j;
-                    if (!last) {
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const float2 o = first ? make_float2(0.0f, 0.0f) : __half22float2(r[i]);
-                            r[i] = __floats2half2_rn(fold16(o.x, v[2 * i], first), fold16(o.y, v[2 * i + 1], first));
-                        }
-                    } else {
-                        float b[32];
-                        if constexpr (MODE == EPI_TILE16) load_bias32(p.bias, cb, p.N, b);
-                        uint32_t pk[16];
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const float2 o = first ? make_float2(0.0f, 0.0f) : __half22float2(r[i]);
-                            float s0 = fold16(o.x, v[2 * i], first), s1 = fold16(o.y, v[2 * i + 1], first);
-                            if constexpr (MODE == EPI_TILE16) {
-                                s0 = finish_tile16(s0, b[2 * i], has_bias, p.post);
-                                s1 = finish_tile16(s1, b[2 * i + 1], has_bias, p.post);
-                                bad |= f16_overflows(s0) | f16_overflows(s1);
-                            }
-                            pk[i] = pack_half2(s0, s1);
-                        }
-                        if constexpr (MODE == EPI_TILE16)
-                            if (p.res != nullptr && row_ok) add_residual32(p, row, cb, pk, bad);
-                        if (row_ok) store32(p.y + (size_t)row * p.ldy, cb, p.N, p.vec_y, pk);
-                    }
+                    store_out(p, tmap_y, stage, lane, row, row_ok, cb, p.N, pk);
                 }
+            }
             }
             ++acc_used;
         }
     }
+    if (p.tma_y && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");   // stores done
     if constexpr (MODE == EPI_RAW32)
         if (p.route_rows > 0) __threadfence_system();   // peer stores before the round's signal
     if (__any_sync(0xffffffffu, bad) && lane == 0) raise_flag(p.flags, FLAG_NONFINITE_OUTPUT);
@@ -480,14 +694,15 @@ __device__ __forceinline__ void epilogue_role(const Params &p, int warp, int lan
 template <int CG, int TN, int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                const Params p) {
+                const __grid_constant__ CUtensorMap tmap_y, const Params p) {
     using C = Cfg<CG, TN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~static_cast<uintptr_t>(1023));
     uint8_t *sA = smem;
     uint8_t *sB = smem + C::STAGES * C::A_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+    uint8_t *sOut = smem + C::STAGES * C::STAGE_BYTES;   // 1024-byte aligned
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sOut + C::OUT_BYTES);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + C::NUM_BARS);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -511,6 +726,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
+        if (p.tma_y) prefetch_tmap(&tmap_y);
     }
     if (warp == 2) {
         tmem_alloc<CG>(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -589,7 +805,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else if (warp >= 4) {
         epilogue_role<CG, TN, MODE>(p, warp, lane, rank, cluster_id, num_clusters, nchunks, tmem_base, tfull0,
-                                tempty0, abort_flag);
+                                tempty0, abort_flag, &tmap_y, smem_u32(sOut + (warp - 4) * 2048));
     }
 
     tc_fence_before();
@@ -743,14 +959,40 @@ cudaError_t prepare(int device, int sm_count) {
     return e1 != cudaSuccess ? e1 : e2;
 }
 
+// Output tensor map of the TMA tile stores: FP16 [rows, ld] of which `cols` are valid, 32 x 32 boxes,
+// 64-byte swizzle (the layout store_out writes into the staging box).
+static bool make_store_map(CUtensorMap *map, const void *ptr, uint64_t cols, uint64_t rows, uint64_t ld) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * 2};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int CG, int TN, int MODE>
-static cudaError_t launch_mode(const CUtensorMap &ta, const CUtensorMap &tb, const Params &p, unsigned grid,
+static cudaError_t launch_mode(const CUtensorMap &ta, const CUtensorMap &tb, Params p, unsigned grid,
                                cudaStream_t stream, int device) {
     const cudaError_t e = ensure_attr<CG, TN, MODE>(device);
     if (e != cudaSuccess) return e;
+    // FP16 outputs leave through TMA tile stores when Y allows a tensor map (16-byte aligned base and
+    // pitch, at least one 32 x 32 box) whose row ends on a 16-byte boundary: a box crossing a ragged
+    // row end was seen to write the rest of that row's last 16 bytes, i.e. into the pitch padding.
+    // Otherwise each epilogue thread stores its row directly, clipped at the last column.
+    CUtensorMap ty;
+    memset(&ty, 0, sizeof(ty));
+    const uint64_t n_out = MODE == EPI_GATED ? (uint64_t)p.gate_n : (uint64_t)p.N;
+    p.tma_y = 0;
+    if constexpr (MODE != EPI_RAW32)
+        if (p.vec_y && n_out % 8 == 0 && n_out >= 32 && p.M >= 32 &&
+            make_store_map(&ty, p.y, n_out, (uint64_t)p.M, (uint64_t)p.ldy))
+            p.tma_y = 1;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = cluster_config(CG, grid, Cfg<CG, TN>::SMEM_BYTES, stream, attr);
-    return cudaLaunchKernelEx(&cfg, gemm_kernel<CG, TN, MODE>, ta, tb, p);
+    return cudaLaunchKernelEx(&cfg, gemm_kernel<CG, TN, MODE>, ta, tb, ty, p);
 }
 
 template <int CG, int TN>
