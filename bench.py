@@ -368,8 +368,12 @@ def _timed_steps(torch, dist, world, stream, fn, warmup, steps, flush=None):
     with ClockSampler(torch.cuda.current_device()) as clocks:
         for _ in range(steps):
             if flush is not None:
-                with torch.cuda.stream(stream):   # on the launching stream: done before the start event
+                # on the launching stream, before the start event: write a buffer larger than L2, then
+                # read one (so the timed launch starts with a cold L2 that holds no dirty lines whose
+                # write-back it would pay for)
+                with torch.cuda.stream(stream):
                     flush.zero_()
+                    flush.view(torch.float32).sum()
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(stream)
             fn()

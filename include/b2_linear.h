@@ -110,10 +110,10 @@ int b2_linear_run_device_noalloc(b2_linear *, unsigned m, const void *x, size_t 
  * decode time. It replaces the projection step of the reference's multi-output graph call
  * (research/custom-ops/src/co_decoder.c:128-129, co_graph_run_many in
  * research/custom-ops/include/co_graph.h:77), which produces Q, K and V from one input.
- * Operators with m <= 8 and k <= 2048 share ONE kernel launch (the weight-streaming GEMV) as long
- * as their distinct inputs (m x k each; members passing the same X share it) fit its 32 KB
- * shared-memory table; otherwise they are packed in order into consecutive launches that each
- * fit. Any other member runs as its own b2_linear_run_device launch. Each result is bit-identical
+ * Operators with m <= 8 whose m x k input fits the weight-streaming GEMV's 32 KB shared-memory
+ * table (m * roundup(k, 8) * 2 bytes; k <= 8192 at m <= 2, 4096 at m = 4, 2048 at m = 8) share ONE
+ * kernel launch as long as their distinct inputs (members passing the same X share it) fit the
+ * table together; otherwise they are packed in order into consecutive launches that each fit. Any other member runs as its own b2_linear_run_device launch. Each result is bit-identical
  * to that operator's own b2_linear_run_device (CO_SEPARATE operators are finished in the same
  * launch with the same arithmetic as their separate epilogue). X_i and Y_i follow
  * b2_linear_run_device's rules; the X_i may alias (a shared input). Asynchronous on the handle's

@@ -27,6 +27,7 @@ struct b2_dev {
     cudaStream_t stream;
     unsigned *flags;        // host pointer of the mapped status words
     unsigned *flags_dev;    // the same words as seen by kernels
+    b2::gemv::Scratch gemv; // tile sums and block counters of long-K small-M launches
 };
 
 namespace {
@@ -86,6 +87,22 @@ int b2d_open(int ordinal, b2_dev **out) {
         return ROCKET_E_DEVICE;
     }
     memset(d->flags, 0, b2::FLAG_COUNT * sizeof(unsigned));
+    // long-K small-M scratch: allocated once per handle (a launch recorded into a CUDA graph keeps
+    // its address); the counters start at zero and every launch leaves them at zero
+    void *ts = nullptr, *tc = nullptr;
+    if (cudaMalloc(&ts, (size_t)b2::gemv::TSUM_FLOATS * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&tc, (size_t)b2::gemv::TCOUNT_WORDS * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(tc, 0, (size_t)b2::gemv::TCOUNT_WORDS * sizeof(unsigned)) != cudaSuccess) {
+        cudaGetLastError();
+        if (ts) cudaFree(ts);
+        if (tc) cudaFree(tc);
+        cudaFreeHost(d->flags);
+        cudaStreamDestroy(d->own);
+        delete d;
+        return ROCKET_E_NOMEM;
+    }
+    d->gemv.tsum = static_cast<float *>(ts);
+    d->gemv.tcount = static_cast<unsigned *>(tc);
     *out = d;
     return 0;
 }
@@ -96,6 +113,8 @@ void b2d_close(b2_dev *d) {
     cudaStreamSynchronize(d->stream);
     cudaStreamDestroy(d->own);
     cudaFreeHost(d->flags);
+    cudaFree(d->gemv.tsum);
+    cudaFree(d->gemv.tcount);
     delete d;
 }
 
@@ -199,7 +218,7 @@ int b2d_linear_config(b2_dev *d, const b2k_linear *a, b2k_config *cfg) {
         cfg->tile_n = 8;
         cfg->tile_k = 256;
         cfg->grid = b2::gemv::grid_for((int)a->m, (int)a->n, (int)a->k, (long long)a->ldw, d->sm_count);
-        cfg->stages = b2::gemv::streamed((int)a->m, (int)a->k) ? 12 : 0;
+        cfg->stages = b2::gemv::stream_launches((int)a->m, (int)a->n, (int)a->k, (long long)a->ldw) ? 12 : 0;
     } else {
         cfg->kernel = 0;
         b2::gemm::config_for((int)a->m, (int)a->n, d->sm_count, &cfg->tile_m, &cfg->tile_n, &cfg->stages);
@@ -231,6 +250,7 @@ static cudaError_t launch_core(b2_dev *d, const b2k_linear *a, int out_mode, boo
         p.partial = a->partial; p.ldp = (long long)a->ldp;
         p.out_mode = out_mode; p.post = a->post; p.fold = fold ? 1 : 0;
         p.flags = d->flags_dev;
+        p.scratch = d->gemv;
         return b2::gemv::launch(p, d->stream, d->sm_count, nullptr);
     }
     b2::gemm::Params p = {};
@@ -252,6 +272,14 @@ static cudaError_t launch_core(b2_dev *d, const b2k_linear *a, int out_mode, boo
     return b2::gemm::launch(s, p, d->stream, d->ordinal, d->sm_count, nullptr);
 }
 
+// Kernels launch_core issues for `a`: one GEMM, or the small-M launches (row groups when the x rows
+// exceed the streamed kernel's table).
+static unsigned core_launches(const b2k_linear *a) {
+    if (!use_gemv(a)) return 1;
+    const int n = b2::gemv::stream_launches((int)a->m, (int)a->n, (int)a->k, (long long)a->ldw);
+    return n > 0 ? (unsigned)n : 1u;
+}
+
 static bool fp16_operand_ok(const void *p, size_t ld, size_t cols) {
     return p && aligned16(p) && ld % 8 == 0 && ld >= cols;
 }
@@ -271,7 +299,7 @@ static int linear_gated(b2_dev *d, const b2k_linear *a, unsigned *launches) {
     if (!fp16_operand_ok(a->tmp, a->ldt, a->n) || !fp16_operand_ok(a->y, a->ldy, a->gate_n)) return ROCKET_E_SHAPE;
     cudaError_t e = launch_core(d, a, b2::gemm::OUT_RAW16, true, a->tmp, a->ldt, false);
     if (e != cudaSuccess) return rc_of(e);
-    *launches = 1;
+    *launches = core_launches(a);
     b2::graph::GatedParams g = {};
     g.rows = (int)a->m; g.gate_n = (int)a->gate_n; g.act = a->gate;
     g.src = static_cast<const __half *>(a->tmp); g.lds = (long long)a->ldt;
@@ -281,7 +309,7 @@ static int linear_gated(b2_dev *d, const b2k_linear *a, unsigned *launches) {
     g.flags = d->flags_dev;
     e = b2::graph::gated_combine(g, d->stream, d->sm_count);
     if (e != cudaSuccess) return rc_of(e);
-    *launches = 2;
+    *launches += 1;
     return 0;
 }
 
@@ -302,7 +330,7 @@ int b2d_linear(b2_dev *d, const b2k_linear *a, unsigned *launches) {
     const bool fuse_res = a->res && a->fused && !use_gemv(a);
     cudaError_t e = launch_core(d, a, out_mode, fold, a->y, a->ldy, fuse_res);
     if (e != cudaSuccess) return rc_of(e);
-    *launches = 1;
+    *launches = core_launches(a);
     if (!a->fused && !a->raw_only) {
         // Separate epilogue: FP32 partial -> y, or the folded FP16 sum in y -> y in place.
         b2::aux::EpilogueParams ep = {};
@@ -314,7 +342,7 @@ int b2d_linear(b2_dev *d, const b2k_linear *a, unsigned *launches) {
         ep.flags = d->flags_dev;
         e = b2::aux::epilogue(ep, d->stream, d->sm_count);
         if (e != cudaSuccess) return rc_of(e);
-        *launches = 2;
+        *launches += 1;
     }
     if (a->res && !fuse_res) {
         b2::graph::EwParams ew = {};
@@ -342,9 +370,10 @@ int b2d_linear_group(b2_dev *d, const b2k_linear *ops, unsigned count, unsigned 
     b2::gemv::Group g = {};
     g.M = (int)ops[0].m;
     g.flags = d->flags_dev;
+    g.scratch = d->gemv;
     for (unsigned i = 0; i < count; ++i) {
         const b2k_linear *a = &ops[i];
-        if (!b2::gemv::streamed((int)a->m, (int)a->k)) continue;
+        if (!b2::gemv::streamed((int)a->m, (int)a->n, (int)a->k, (long long)a->ldw)) continue;
         g.prob[g.count++] = b2::gemv::Problem{static_cast<const __half *>(a->x), (long long)a->ldx,
                                               static_cast<const __half *>(a->w), (long long)a->ldw,
                                               static_cast<const __half *>(a->bias), static_cast<__half *>(a->y),
@@ -358,7 +387,7 @@ int b2d_linear_group(b2_dev *d, const b2k_linear *ops, unsigned count, unsigned 
         if (e != cudaSuccess) return rc_of(e);
     }
     for (unsigned i = 0; i < count; ++i) {
-        if (b2::gemv::streamed((int)ops[i].m, (int)ops[i].k)) continue;
+        if (b2::gemv::streamed((int)ops[i].m, (int)ops[i].n, (int)ops[i].k, (long long)ops[i].ldw)) continue;
         unsigned l = 0;
         const int rc = b2d_linear(d, &ops[i], &l);
         *launches += l;

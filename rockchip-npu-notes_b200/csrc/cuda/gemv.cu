@@ -29,6 +29,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "gemv.h"
@@ -159,9 +160,11 @@ constexpr int S_SLOTS_PER_CONSUMER = 1;             // a slot refills while its 
 constexpr int S_STAGES = S_CONSUMERS * S_SLOTS_PER_CONSUMER;   // one producer lane each: <= 32
 constexpr int S_THREADS = 32 * (1 + S_CONSUMERS);
 constexpr uint32_t S_STAGE_BYTES = (196608u / S_STAGES) & ~127u;
+static_assert(S_STAGE_BYTES == (uint32_t)STREAM_ROW_BYTES, "copy slot size");
+static_assert(16 * STREAM_SLICE * 2 <= STREAM_ROW_BYTES && STREAM_SLICE % 256 == 0, "a 16-row slice fills one slot");
 static_assert(S_STAGES <= 32, "one producer lane per slot");
 struct Meta {
-    int prob, row0, rows, pad;   // prob < 0: no more units
+    int prob, row0, rows, slice;   // prob < 0: no more units; slice: K slice of a sliced unit
 };
 // ring | x table | meta | full and empty barriers | abort flag | the group's problems (copied
 // from the kernel parameter once per CTA: dynamically indexed parameter reads are slow)
@@ -180,6 +183,13 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
                  : "memory");
 }
 
+// One 2-D box of a tensor map into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_box(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+                 ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+                 : "memory");
+}
+
 // D += A * B, m16n8k16, FP16 inputs, FP32 accumulation.
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -191,9 +201,11 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
 }
 
 // Lane `slot` of warp 0 feeds ring slot `slot`: it streams this CTA's units q = slot, slot +
-// S_STAGES, ... (unit u = blockIdx.x + q * gridDim.x) into that slot, then an end marker. The
-// slots' producers run side by side, so the latency of the barrier and bulk-copy instructions of
-// one slot overlaps the others'. On abort a lane waits (bounded) for its own copy in flight.
+// S_STAGES, ... (unit u = blockIdx.x + q * gridDim.x) into that slot, then an end marker. A
+// whole-row unit is one bulk copy of its rows; a sliced unit (one K slice of a 16-row block of a
+// long-K problem, unit = block * slices + slice) is one bulk copy per row onto the slot's barrier.
+// The slots' producers run side by side, so the latency of the barrier and bulk-copy instructions
+// of one slot overlaps the others'. On abort a lane waits (bounded) for its own copy in flight.
 __device__ __forceinline__ void produce(const Group &g, const Problem *prob, uint8_t *smem, Meta *meta, uint32_t full0,
                                         uint32_t empty0, volatile int *abort_flag, int slot) {
     const int count = g.count, units = g.units;
@@ -204,7 +216,8 @@ __device__ __forceinline__ void produce(const Group &g, const Problem *prob, uin
     int pi = 0;
     // the current problem's fields, reloaded only when the unit index crosses into the next one
     int next_begin = count > 1 ? prob[1].unit_begin : units;
-    int begin = prob[0].unit_begin, R = prob[0].rows_per_unit, N = prob[0].N;
+    int begin = prob[0].unit_begin, R = prob[0].rows_per_unit, N = prob[0].N, K8 = (prob[0].K + 7) & ~7;
+    int kslice = prob[0].kslice, slices = prob[0].slices;
     long long ldw = prob[0].ldw;
     const __half *w = prob[0].w;
     for (int u = blockIdx.x + slot * gridDim.x; u < units; u += S_STAGES * gridDim.x) {
@@ -214,19 +227,32 @@ __device__ __forceinline__ void produce(const Group &g, const Problem *prob, uin
             begin = prob[pi].unit_begin;
             R = prob[pi].rows_per_unit;
             N = prob[pi].N;
+            K8 = (prob[pi].K + 7) & ~7;
+            kslice = prob[pi].kslice;
+            slices = prob[pi].slices;
             ldw = prob[pi].ldw;
             w = prob[pi].w;
         }
-        const int row0 = (u - begin) * R;
+        const int q = u - begin;
+        const int blk = kslice ? q / slices : q, sl = kslice ? q - blk * slices : 0;
+        const int row0 = blk * R;
         const int rows = min(R, N - row0);
         if (!wait_phase(empty, ph ^ 1u, abort_flag, g.flags)) {
             ok = false;
             break;
         }
-        meta[slot] = Meta{pi, row0, rows, 0};
-        const uint32_t bytes = (uint32_t)rows * (uint32_t)ldw * 2u;
-        mbar_arrive_expect_tx(full, bytes);
-        bulk_g2s(dst, w + (size_t)row0 * ldw, bytes, full);
+        meta[slot] = Meta{pi, row0, rows, sl};
+        if (kslice) {
+            // one 2-D tensor copy per 256-wide half of the slice (rows past N and K past the end
+            // arrive as zeros); box b holds rows [row0, row0+16) x K [k0 + 256b, k0 + 256b + 256)
+            const int k0 = sl * kslice, boxes = min(kslice / 256, (K8 - k0 + 255) / 256);
+            mbar_arrive_expect_tx(full, (uint32_t)boxes * 16u * 256u * 2u);
+            for (int b = 0; b < boxes; ++b) tma_box(dst + (uint32_t)b * 16u * 256u * 2u, &g.wmap, full, k0 + 256 * b, row0);
+        } else {
+            const uint32_t bytes = (uint32_t)rows * (uint32_t)ldw * 2u;
+            mbar_arrive_expect_tx(full, bytes);
+            bulk_g2s(dst, w + (size_t)row0 * ldw, bytes, full);
+        }
         armed = true;
         ph ^= 1u;
     }
@@ -238,79 +264,195 @@ __device__ __forceinline__ void produce(const Group &g, const Problem *prob, uin
     if (armed) drain_phase(full, ph ^ 1u);   // the last copy this lane issued
 }
 
-// Rows [0, rows) of a unit staged at `stage` (row pitch ldw), x rows (pitch round8(K), zero past
-// K) from the shared x table: 16-row blocks, one m16n8k16 MMA per 16 K with the W rows as A
-// (row-major) and up to 8 x rows as B. Lane (g = lane/4, t = lane%4) supplies, per 32-wide K
-// window, the 8 consecutive elements at window + 8t of W rows g and g+8 and of x row g; those 8
-// elements are the k-slots {2t, 2t+1, 2t+8, 2t+9} of two consecutive MMAs. The dot product only
-// needs A and B to use the same k order, and this order depends on t alone. Four accumulators
-// (one per 16-wide slice of a 64-wide step) keep consecutive MMAs independent; their sum is the
-// tile sum (tile-16) or the row total (FP32). The accumulator of lane (g, t) holds rows g and g+8
-// for x rows 2t and 2t+1.
+// One 16-row block of W against up to 8 x rows, with the m16n8k16 MMA: the W rows as A (row-major)
+// and the x rows (from the shared x table, zero past K) as B. Lane (g = lane/4, t = lane%4) supplies,
+// per 32-wide K window, the 8 consecutive elements at window + 8t of W rows g and g+8 and of x row
+// g; those 8 elements are the k-slots {2t, 2t+1, 2t+8, 2t+9} of two consecutive MMAs. The dot
+// product only needs A and B to use the same k order, and this order depends on t alone. Four
+// accumulators (one per 16-wide slice of a 64-wide step) keep consecutive MMAs independent; their
+// sum is the tile sum (tile-16) or the row total (FP32). The accumulator of lane (g, t) holds rows
+// g and g+8 for x rows 2t and 2t+1. The state lives across the K slices of a sliced unit.
+struct BlockAcc {
+    float acc[4][4];
+    float run[4];
+};
+
+__device__ __forceinline__ void block_reset(BlockAcc &s) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s.acc[j][i] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) s.run[i] = 0.0f;
+}
+
+// Accumulates K positions [kb, ke) (ke <= roundup(K, 8); kb and, except at the end, ke multiples of
+// 256) of W rows wa / wc (element 0 of each is K position kb; va / vc: the row exists) against x row
+// xrow (nullptr past M). Tile-16 folds run = fp16(run + tile) at every 256-K tile (the first tile
+// of the row starts the running sum); FP32 keeps summing.
+__device__ __forceinline__ void block_accumulate(const __half *wa, const __half *wc, bool va, bool vc,
+                                                 const __half *xrow, int kb, int ke, int K8, bool fold, int lane,
+                                                 BlockAcc &s) {
+    const int t4 = lane & 3;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    for (int t0 = kb; t0 < ke; t0 += 256) {
+        if (fold) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) s.acc[j][i] = 0.0f;
+        }
+        const int kend = min(ke, t0 + 256);
+#pragma unroll 4
+        for (int kw = t0; kw < kend; kw += 64) {
+            const int k0 = kw + t4 * 8, k1 = k0 + 32;
+            const bool l0 = k0 < K8, l1 = k1 < K8;
+            const uint4 a0 = (va && l0) ? *reinterpret_cast<const uint4 *>(wa + (k0 - kb)) : z;
+            const uint4 a1 = (va && l1) ? *reinterpret_cast<const uint4 *>(wa + (k1 - kb)) : z;
+            const uint4 b0 = (vc && l0) ? *reinterpret_cast<const uint4 *>(wc + (k0 - kb)) : z;
+            const uint4 b1 = (vc && l1) ? *reinterpret_cast<const uint4 *>(wc + (k1 - kb)) : z;
+            const uint4 x0 = (xrow && l0) ? *reinterpret_cast<const uint4 *>(xrow + k0) : z;
+            const uint4 x1 = (xrow && l1) ? *reinterpret_cast<const uint4 *>(xrow + k1) : z;
+            mma16816(s.acc[0], a0.x, b0.x, a0.y, b0.y, x0.x, x0.y);
+            mma16816(s.acc[1], a0.z, b0.z, a0.w, b0.w, x0.z, x0.w);
+            mma16816(s.acc[2], a1.x, b1.x, a1.y, b1.y, x1.x, x1.y);
+            mma16816(s.acc[3], a1.z, b1.z, a1.w, b1.w, x1.z, x1.w);
+        }
+        if (fold) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                s.run[i] = fold16(s.run[i], (s.acc[0][i] + s.acc[1][i]) + (s.acc[2][i] + s.acc[3][i]), t0 == 0);
+        }
+    }
+}
+
+// Writes the block's results: lane (g, t4) element 0 is row g / x row 2t4, 1 row g / x row 2t4+1,
+// 2 and 3 the same for row g+8 (rows relative to the block's first row `n0`). Returns true if a
+// final FP16 output is not finite.
+__device__ __forceinline__ bool block_finish(const Problem &pr, int M, int n0, int ra, int rc, int rows, int lane,
+                                             const BlockAcc &s) {
+    const int t4 = lane & 3;
+    const bool fold = pr.fold != 0, has_bias = pr.bias != nullptr;
+    bool bad = false;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = (i < 2 ? ra : rc), xr = 2 * t4 + (i & 1);
+        if (r >= rows || xr >= M) continue;
+        const int n = n0 + r;
+        const float total = fold ? s.run[i] : (s.acc[0][i] + s.acc[1][i]) + (s.acc[2][i] + s.acc[3][i]);
+        if (pr.out_mode == OUT_RAW32) {
+            pr.partial[(size_t)xr * pr.ldp + n] = total;
+        } else if (pr.out_mode == OUT_RAW16) {
+            pr.y[(size_t)xr * pr.ldy + n] = __float2half_rn(total);
+        } else {
+            const float b = has_bias ? __half2float(pr.bias[n]) : 0.0f;
+            const float v = fold ? finish_tile16(total, b, has_bias, pr.post) : finish_fp32(total, b, pr.post);
+            const __half h = __float2half_rn(v);
+            bad |= half_nonfinite(h);
+            pr.y[(size_t)xr * pr.ldy + n] = h;
+        }
+    }
+    return bad;
+}
+
+// A whole-row unit: rows [0, rows) staged at `stage` (pitch ldw), all of K, in 16-row blocks.
 __device__ __forceinline__ bool process_unit(const Problem &pr, int M, const __half *stage, const __half *xtab,
                                              int row0, int rows, int lane) {
-    const int g = lane >> 2, t4 = lane & 3;
-    const long long ldw = pr.ldw;
-    const int K = pr.K, K8 = (K + 7) & ~7, tiles = (K + 255) >> 8;
-    const bool fold = pr.fold != 0;
-    const __half *xrow = g < M ? xtab + pr.x_off + (size_t)g * K8 : nullptr;   // zero past K
-    const bool has_bias = pr.bias != nullptr;
-    const uint4 z = make_uint4(0, 0, 0, 0);
+    const int g = lane >> 2;
+    const int K8 = (pr.K + 7) & ~7;
+    const __half *xrow = g < M ? xtab + pr.x_off + (size_t)g * K8 : nullptr;
     bool bad = false;
     for (int rb = 0; rb < rows; rb += 16) {
         const int ra = rb + g, rc = rb + g + 8;
-        const bool va = ra < rows, vc = rc < rows;
-        const __half *wa = stage + (size_t)ra * ldw, *wc = stage + (size_t)rc * ldw;
-        float acc[4][4] = {}, run[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int tile = 0; tile < tiles; ++tile) {
-            if (fold) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) acc[j][i] = 0.0f;
-            }
-            const int kend = min(K8, tile * 256 + 256);
+        BlockAcc s;
+        block_reset(s);
+        block_accumulate(stage + (size_t)ra * pr.ldw, stage + (size_t)rc * pr.ldw, ra < rows, rc < rows, xrow, 0, K8,
+                         K8, pr.fold != 0, lane, s);
+        bad |= block_finish(pr, M, row0, ra, rc, rows, lane, s);
+    }
+    return bad;
+}
+
+// Slice `sl` of a sliced unit: rows [0, rows <= 16) of the block at row0, staged with pitch kslice,
+// K positions [sl * kslice, ...). Each 256-K tile's FP32 sum goes to the scratch (row, x row, tile);
+// the unit that completes the block's last slice (arrival counter) reads the block's tile sums back
+// in K order and finishes them exactly as the whole-row path does: fp16 fold over the tiles
+// (tile-16) or their FP32 sum, then bias / HardSigmoid. It resets the counter for the next launch.
+template <typename Release>
+__device__ __forceinline__ bool process_slice(const Group &grp, const Problem &pr, int M, const __half *stage,
+                                              const __half *xtab, int row0, int rows, int sl, int lane,
+                                              Release release) {
+    const int g = lane >> 2, t4 = lane & 3;
+    const int K8 = (pr.K + 7) & ~7, T = (K8 + 255) >> 8, kb = sl * pr.kslice, ke = min(K8, kb + pr.kslice);
+    const __half *xrow = g < M ? xtab + pr.x_off + (size_t)g * K8 : nullptr;
+    float *ts = grp.scratch.tsum + (size_t)row0 * M * T;   // this block's tile sums
+    const bool va = g < rows, vc = g + 8 < rows;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    for (int t0 = kb; t0 < ke; t0 += 256) {
+        // the tile's box: 16 rows of 256 (rows past N are zeros, never written)
+        const __half *box = stage + (size_t)((t0 - kb) >> 8) * 16 * 256;
+        const __half *wa = box + (size_t)g * 256, *wc = box + (size_t)(g + 8) * 256;
+        float acc[4][4] = {};
+        const int kend = min(ke, t0 + 256);
 #pragma unroll 4
-            for (int kw = tile * 256; kw < kend; kw += 64) {
-                const int k0 = kw + t4 * 8, k1 = k0 + 32;
-                const bool l0 = k0 < K8, l1 = k1 < K8;
-                const uint4 a0 = (va && l0) ? *reinterpret_cast<const uint4 *>(wa + k0) : z;
-                const uint4 a1 = (va && l1) ? *reinterpret_cast<const uint4 *>(wa + k1) : z;
-                const uint4 b0 = (vc && l0) ? *reinterpret_cast<const uint4 *>(wc + k0) : z;
-                const uint4 b1 = (vc && l1) ? *reinterpret_cast<const uint4 *>(wc + k1) : z;
-                const uint4 x0 = (xrow && l0) ? *reinterpret_cast<const uint4 *>(xrow + k0) : z;
-                const uint4 x1 = (xrow && l1) ? *reinterpret_cast<const uint4 *>(xrow + k1) : z;
-                mma16816(acc[0], a0.x, b0.x, a0.y, b0.y, x0.x, x0.y);
-                mma16816(acc[1], a0.z, b0.z, a0.w, b0.w, x0.z, x0.w);
-                mma16816(acc[2], a1.x, b1.x, a1.y, b1.y, x1.x, x1.y);
-                mma16816(acc[3], a1.z, b1.z, a1.w, b1.w, x1.z, x1.w);
-            }
-            if (fold) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    run[i] = fold16(run[i], (acc[0][i] + acc[1][i]) + (acc[2][i] + acc[3][i]), tile == 0);
-            }
+        for (int kw = t0; kw < kend; kw += 64) {
+            const int k0 = kw + t4 * 8, k1 = k0 + 32;
+            const bool l0 = k0 < K8, l1 = k1 < K8;
+            const uint4 a0 = (va && l0) ? *reinterpret_cast<const uint4 *>(wa + (k0 - t0)) : z;
+            const uint4 a1 = (va && l1) ? *reinterpret_cast<const uint4 *>(wa + (k1 - t0)) : z;
+            const uint4 b0 = (vc && l0) ? *reinterpret_cast<const uint4 *>(wc + (k0 - t0)) : z;
+            const uint4 b1 = (vc && l1) ? *reinterpret_cast<const uint4 *>(wc + (k1 - t0)) : z;
+            const uint4 x0 = (xrow && l0) ? *reinterpret_cast<const uint4 *>(xrow + k0) : z;
+            const uint4 x1 = (xrow && l1) ? *reinterpret_cast<const uint4 *>(xrow + k1) : z;
+            mma16816(acc[0], a0.x, b0.x, a0.y, b0.y, x0.x, x0.y);
+            mma16816(acc[1], a0.z, b0.z, a0.w, b0.w, x0.z, x0.w);
+            mma16816(acc[2], a1.x, b1.x, a1.y, b1.y, x1.x, x1.y);
+            mma16816(acc[3], a1.z, b1.z, a1.w, b1.w, x1.z, x1.w);
         }
-        // lane (g, t4): element 0 row g / x row 2t4, 1 row g / x row 2t4+1, 2 and 3 the same for row g+8
+        const int t = t0 >> 8;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const int r = (i < 2 ? ra : rc), xr = 2 * t4 + (i & 1);
-            if (r >= rows || xr >= M) continue;
-            const int n = row0 + r;
-            const float total = fold ? run[i] : (acc[0][i] + acc[1][i]) + (acc[2][i] + acc[3][i]);
-            if (pr.out_mode == OUT_RAW32) {
-                pr.partial[(size_t)xr * pr.ldp + n] = total;
-            } else if (pr.out_mode == OUT_RAW16) {
-                pr.y[(size_t)xr * pr.ldy + n] = __float2half_rn(total);
-            } else {
-                const float b = has_bias ? __half2float(pr.bias[n]) : 0.0f;
-                const float v = fold ? finish_tile16(total, b, has_bias, pr.post) : finish_fp32(total, b, pr.post);
-                const __half h = __float2half_rn(v);
-                bad |= half_nonfinite(h);
-                pr.y[(size_t)xr * pr.ldy + n] = h;
-            }
+            const int r = i < 2 ? g : g + 8, xr = 2 * t4 + (i & 1);
+            if (r < rows && xr < M) ts[((size_t)r * M + xr) * T + t] = (acc[0][i] + acc[1][i]) + (acc[2][i] + acc[3][i]);
         }
     }
+    // the slot's data is consumed: the producer may refill it while the tile sums are published
+    __syncwarp();
+    release();
+    // arrival: the warp's tile sums (ordered before lane 0's fence by the warp barrier) are visible
+    // device-wide before the block counter moves
+    unsigned *cnt = grp.scratch.tcount + row0 / 16;
+    int last = 0;
+    if (lane == 0) {
+        __threadfence();
+        last = atomicAdd(cnt, 1u) == (unsigned)(pr.slices - 1);
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return false;
+    __threadfence();   // the other units' tile sums, written before their arrivals
+    const bool fold = pr.fold != 0, has_bias = pr.bias != nullptr;
+    bool bad = false;
+    for (int o = lane; o < rows * M; o += 32) {
+        const int r = o / M, xr = o - r * M, n = row0 + r;
+        const float *p = ts + ((size_t)r * M + xr) * T;
+        float total = 0.0f;
+        for (int t = 0; t < T; ++t) {
+            const float v = __ldcg(p + t);
+            total = fold ? fold16(total, v, t == 0) : (t == 0 ? v : total + v);
+        }
+        if (pr.out_mode == OUT_RAW32) {
+            pr.partial[(size_t)xr * pr.ldp + n] = total;
+        } else if (pr.out_mode == OUT_RAW16) {
+            pr.y[(size_t)xr * pr.ldy + n] = __float2half_rn(total);
+        } else {
+            const float b = has_bias ? __half2float(pr.bias[n]) : 0.0f;
+            const float v = fold ? finish_tile16(total, b, has_bias, pr.post) : finish_fp32(total, b, pr.post);
+            const __half h = __float2half_rn(v);
+            bad |= half_nonfinite(h);
+            pr.y[(size_t)xr * pr.ldy + n] = h;
+        }
+    }
+    if (lane == 0) *cnt = 0u;   // every unit of this block has arrived: ready for the next launch
     return bad;
 }
 
@@ -388,9 +530,17 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_stream_kernel(const __grid_
         const Meta mt = meta[slot];
         if (mt.prob < 0) break;
         const __half *stage = reinterpret_cast<const __half *>(smem + (size_t)slot * S_STAGE_BYTES);
-        bad |= process_unit(prob[mt.prob], g.M, stage, xtab, mt.row0, mt.rows, lane);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty0 + 8 * slot);
+        const Problem &pr = prob[mt.prob];
+        const uint32_t empty = empty0 + 8 * slot;
+        if (pr.kslice) {
+            bad |= process_slice(g, pr, g.M, stage, xtab, mt.row0, mt.rows, mt.slice, lane, [&] {
+                if (lane == 0) mbar_arrive(empty);
+            });
+        } else {
+            bad |= process_unit(pr, g.M, stage, xtab, mt.row0, mt.rows, lane);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty);
+        }
         if (++j == S_SLOTS_PER_CONSUMER) {
             j = 0;
             ph ^= 1u;
@@ -444,7 +594,8 @@ unsigned direct_grid(int M, int N, int sm_count) {
     return (unsigned)(need < cap ? need : cap);
 }
 
-// Rows per unit: spread the group's weight bytes over about two units per SM, one stage at most.
+// Whole-row problems: rows per unit spread the group's weight bytes over about two units per SM, one
+// slot at most. Long-K problems (or rows wider than a slot): 16-row units streamed in K slices.
 void plan_units(Group &g, int sm_count) {
     long long total = 0;
     for (int i = 0; i < g.count; ++i) total += (long long)g.prob[i].N * g.prob[i].ldw * 2;
@@ -453,6 +604,17 @@ void plan_units(Group &g, int sm_count) {
     int units = 0;
     for (int i = 0; i < g.count; ++i) {
         Problem &p = g.prob[i];
+        const int k8 = (p.K + 7) & ~7;
+        if (k8 > STREAM_WHOLE_K || p.ldw * 2 > (long long)S_STAGE_BYTES) {
+            p.kslice = STREAM_SLICE;
+            p.slices = (k8 + STREAM_SLICE - 1) / STREAM_SLICE;
+            p.rows_per_unit = 16;
+            p.unit_begin = units;
+            units += (p.N + 15) / 16 * p.slices;
+            continue;
+        }
+        p.kslice = 0;
+        p.slices = 1;
         const long long row_bytes = p.ldw * 2;
         long long r = target / row_bytes;
         const long long rmax = (long long)S_STAGE_BYTES / row_bytes;
@@ -467,12 +629,69 @@ void plan_units(Group &g, int sm_count) {
 
 }  // namespace
 
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    }
+    return fn;
+}
+
+// W [N, ldw] of which K columns are valid, as 256 (K) x 16 (rows) boxes, unswizzled: the layout
+// process_slice reads. Columns >= K and rows >= N arrive as zeros.
+static bool make_wmap(CUtensorMap *map, const __half *w, int K, int N, long long ldw) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+    cuuint64_t strides[1] = {(cuuint64_t)ldw * 2};
+    cuuint32_t box[2] = {256, 16};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(w), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 cudaError_t prepare() {
     for (int m = 1; m <= MAX_M; m *= 2) direct_blocks(m);
+    if (!encode_fn()) return cudaErrorNotSupported;
     return stream_attr();
 }
 
-bool streamed(int M, int K) { return M >= 1 && M <= STREAM_MAX_M && K >= 1 && K <= STREAM_MAX_K; }
+bool sliced(int K, long long ldw) {
+    const long long k8 = ((long long)K + 7) & ~7ll;
+    return k8 > STREAM_WHOLE_K || ldw * 2 > (long long)S_STAGE_BYTES;
+}
+
+// x rows of one launch: as many as the x table holds (and, for a sliced problem, as many as the
+// scratch holds the tile sums of); 0 when not even one fits.
+static long long rows_that_fit(int N, int K, long long ldw) {
+    const long long k8 = ((long long)K + 7) & ~7ll;
+    long long fit = (long long)STREAM_X_BYTES / (k8 * 2);
+    if (sliced(K, ldw)) {
+        if ((N + 15) / 16 > TCOUNT_WORDS) return 0;
+        const long long per_row = ((long long)N + 15) / 16 * 16 * ((k8 + 255) / 256);
+        const long long fs = TSUM_FLOATS / per_row;
+        if (fs < fit) fit = fs;
+    }
+    return fit;
+}
+
+int stream_launches(int M, int N, int K, long long ldw) {
+    if (M < 1 || M > STREAM_MAX_M || K < 1 || N < 1 || ldw < K) return 0;
+    const long long fit = rows_that_fit(N, K, ldw);
+    if (fit < 1) return 0;
+    return (int)((M + fit - 1) / fit);
+}
+
+bool streamed(int M, int N, int K, long long ldw) { return stream_launches(M, N, K, ldw) == 1; }
 
 namespace {
 
@@ -483,10 +702,14 @@ int pack_group(const Group &all, int first, Group &g) {
     g.nx = 0;
     g.M = all.M;
     g.flags = all.flags;
+    g.scratch = all.scratch;
     int used = 0;
     int i = first;
     for (; i < all.count; ++i) {
         Problem p = all.prob[i];
+        // a sliced problem uses the whole tile-sum scratch: it runs in a launch of its own
+        if (sliced(p.K, p.ldw) && g.count > 0) break;
+        if (g.count == 1 && sliced(g.prob[0].K, g.prob[0].ldw)) break;
         int e = 0;
         while (e < g.nx && !(g.xsrc[e].x == p.x && g.xsrc[e].ldx == p.ldx && g.xsrc[e].K == p.K)) ++e;
         if (e == g.nx) {
@@ -508,7 +731,7 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
     if (all.count < 1 || all.count > GROUP_MAX || all.M < 1 || all.M > STREAM_MAX_M) return cudaErrorInvalidValue;
     for (int i = 0; i < all.count; ++i) {
         const Problem &p = all.prob[i];
-        if (!streamed(all.M, p.K) || p.N < 1 || p.ldw < p.K || p.ldw % 8 || p.ldw * 2 > (long long)S_STAGE_BYTES ||
+        if (!streamed(all.M, p.N, p.K, p.ldw) || p.ldw % 8 ||
             p.ldx < p.K || p.ldx % 8 || (reinterpret_cast<uintptr_t>(p.w) & 15) ||
             (reinterpret_cast<uintptr_t>(p.x) & 15))
             return cudaErrorInvalidValue;
@@ -520,6 +743,8 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
         const int next = pack_group(all, first, g);
         if (next == first) return cudaErrorInvalidValue;   // one problem always fits the table
         plan_units(g, sm_count);
+        if (g.prob[0].kslice && !make_wmap(&g.wmap, g.prob[0].w, g.prob[0].K, g.prob[0].N, g.prob[0].ldw))
+            return cudaErrorInvalidValue;
         const unsigned grid = (unsigned)(g.units < sm_count ? g.units : sm_count);
         if (grid_out) *grid_out = grid;
         cudaLaunchConfig_t cfg = {};
@@ -548,10 +773,10 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
 }
 
 unsigned grid_for(int M, int N, int K, long long ldw, int sm_count) {
-    if (!streamed(M, K)) return direct_grid(M, N, sm_count);
+    if (!stream_launches(M, N, K, ldw)) return direct_grid(M, N, sm_count);
     Group g = {};
     g.count = 1;
-    g.M = M;
+    g.M = 1;
     g.prob[0].N = N;
     g.prob[0].K = K;
     g.prob[0].ldw = ldw;
@@ -561,14 +786,23 @@ unsigned grid_for(int M, int N, int K, long long ldw, int sm_count) {
 
 cudaError_t launch(const Params &p, cudaStream_t stream, int sm_count, unsigned *grid_out) {
     if (p.M < 1 || p.M > MAX_M) return cudaErrorInvalidValue;
-    if (streamed(p.M, p.K)) {
-        Group g = {};
-        g.count = 1;
-        g.M = p.M;
-        g.flags = p.flags;
-        g.prob[0] = Problem{p.x, p.ldx, p.w, p.ldw, p.bias, p.y, p.ldy, p.partial, p.ldp,
-                            p.N, p.K, p.out_mode, p.post, p.fold, 0, 0, 0, 0};
-        return launch_group(g, stream, sm_count, grid_out, nullptr);
+    const int nl = stream_launches(p.M, p.N, p.K, p.ldw);
+    if (nl > 0) {
+        const int per = (p.M + nl - 1) / nl;   // x rows per launch, balanced
+        for (int r0 = 0; r0 < p.M; r0 += per) {
+            Group g = {};
+            g.count = 1;
+            g.M = p.M - r0 < per ? p.M - r0 : per;
+            g.flags = p.flags;
+            g.scratch = p.scratch;
+            g.prob[0] = Problem{p.x + (size_t)r0 * p.ldx, p.ldx, p.w, p.ldw, p.bias,
+                                p.y ? p.y + (size_t)r0 * p.ldy : nullptr, p.ldy,
+                                p.partial ? p.partial + (size_t)r0 * p.ldp : nullptr, p.ldp,
+                                p.N, p.K, p.out_mode, p.post, p.fold, 0, 0, 0, 0, 0, 0};
+            const cudaError_t e = launch_group(g, stream, sm_count, grid_out, nullptr);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
     }
     const unsigned grid = direct_grid(p.M, p.N, sm_count);
     if (grid_out) *grid_out = grid;

@@ -1,5 +1,6 @@
 // gemv.h -- parameters and launchers of the small-M kernels (gemv.cu).
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -8,6 +9,16 @@ namespace gemv {
 
 constexpr int MAX_M = 8;
 enum OutMode : int { OUT_FINAL = 0, OUT_RAW16 = 1, OUT_RAW32 = 2 };
+
+// Per-handle device scratch of the long-K (sliced) streamed launches: FP32 sums of every 256-K tile
+// of every (W row, x row), and one arrival counter per 16-row block (zero between launches: the
+// unit that completes a block resets it).
+constexpr long long TSUM_FLOATS = 2ll << 20;   // 8 MB
+constexpr int TCOUNT_WORDS = 1 << 16;
+struct Scratch {
+    float *tsum;
+    unsigned *tcount;
+};
 
 struct Params {
     int M, N, K;
@@ -18,14 +29,20 @@ struct Params {
     float *partial; long long ldp;
     int out_mode, post, fold;
     unsigned *flags;
+    Scratch scratch;                    // tile sums of long-K problems (from the device handle)
 };
 
 // Bulk-copy streamed kernel: one launch serves up to GROUP_MAX independent projections that share
 // the row count M (for example the Q/K/V or gate/up projections of one decoder layer).
 constexpr int GROUP_MAX = 16;
 constexpr int STREAM_MAX_M = 8;         // x rows: the n8 dimension of the m16n8k16 MMA
-constexpr int STREAM_MAX_K = 2048;      // 8 x rows of 2048 fill the 32 KB x table
 constexpr int STREAM_X_BYTES = 32768;   // shared-memory table of the launch's distinct x rows
+constexpr int STREAM_ROW_BYTES = 16384; // one copy slot
+// A unit of a problem with K <= STREAM_WHOLE_K is whole W rows (as many as fill a slot); above it a
+// unit is a 16-row block whose K is streamed in slices of STREAM_SLICE through the same slot, so the
+// 16 W rows of every m16n8k16 MMA are real rows however long K is.
+constexpr int STREAM_WHOLE_K = 2048;
+constexpr int STREAM_SLICE = 512;       // 16 rows x 512 FP16 = one slot; a multiple of the 256-K tile
 
 struct Problem {
     const __half *x; long long ldx;
@@ -36,6 +53,8 @@ struct Problem {
     int N, K, out_mode, post, fold;
     int rows_per_unit, unit_begin;      // filled in by launch_group
     int x_off;                          // element offset of this problem's x rows in the x table
+    int kslice;                         // 0: whole-row units; else K slice of the 16-row units
+    int slices;                         // K slices of a sliced problem (units = blocks x slices)
     int pad;
 };
 
@@ -47,24 +66,34 @@ struct XSource {
 };
 
 struct Group {
+    CUtensorMap wmap;                   // W of a sliced problem (alone in its launch): 256 x 16 boxes
     Problem prob[GROUP_MAX];
     XSource xsrc[GROUP_MAX];
     int count, M, units, nx;
     unsigned *flags;
+    Scratch scratch;
 };
 
-// True when the streamed kernel serves this shape (M <= 8, K <= 2048).
-bool streamed(int M, int K);
+// The streamed kernel serves M <= 8 when the M x rows fit the x table (M * roundup(K, 8) FP16):
+// K <= 16384 for M = 1, 8192 for M = 2, 4096 for M = 4, 2048 for M = 8; a long-K problem also needs
+// its tile sums (N * M * K/256 floats) and block counters (N / 16) to fit the scratch.
+bool streamed(int M, int N, int K, long long ldw);
+// Streamed launches that serve a single problem in `launch`: 1 when streamed(), else M is split into
+// row groups whose x rows fit the table (each group streams all of W; every row's result is the same
+// as in a one-launch run); 0 when no row group fits: the per-lane kernel serves it.
+int stream_launches(int M, int N, int K, long long ldw);
 
 // Picks the kernel for p (streamed when eligible, else the per-lane-load kernel) and launches it.
 cudaError_t launch(const Params &p, cudaStream_t stream, int sm_count, unsigned *grid_out);
 // Runs the launchers' one-time device setup (shared-memory limits, occupancy queries) now, so that
 // a later launch issues no such call (a launch recorded into a CUDA graph must not).
 cudaError_t prepare();
-// Launches the streamed kernel over g.count problems (each must satisfy streamed(g.M, K)): one
+// Launches the streamed kernel over g.count problems (each must satisfy streamed(g.M, K, ldw)): one
 // launch, or more when the problems' distinct x rows exceed the x table (*launches gets the count).
 cudaError_t launch_group(Group &g, cudaStream_t stream, int sm_count, unsigned *grid_out, unsigned *launches);
 unsigned grid_for(int M, int N, int K, long long ldw, int sm_count);
+// True when a problem of this K streams in K slices (16-row units).
+bool sliced(int K, long long ldw);
 
 }  // namespace gemv
 }  // namespace b2

@@ -1,12 +1,13 @@
 """Small-M (decode) kernels and the grouped projection launch, through the C-ABI library.
 
-* Both small-M kernels (streamed tensor-core kernel for K <= 2048, per-lane-load kernel above)
-  compute each x row independently of the rest of the batch: rows of M=1, 2, 3, 8 runs agree bit
-  for bit, both accumulation modes, with and without bias and HardSigmoid, ragged K, NaN in the
-  x pitch padding; all within tolerance of the oracle.
+* The streamed tensor-core kernel (K <= 8192; M split into row groups whose x rows fit its 32 KB
+  table) computes each x row independently of the rest of the batch: rows of M=1, 2, 3, 8 runs
+  agree bit for bit, both accumulation modes, with and without bias and HardSigmoid, ragged K, NaN
+  in the x pitch padding; all within tolerance of the oracle.
 * b2_linear_group_run_device: every member's output equals that operator's own
   b2_linear_run_device bit for bit (shared and separate inputs, CO_SEPARATE and tile-16 members,
-  a member outside the streamed range), and a group whose members all stream is one launch.
+  a K=4096 member that joins the shared launch at m <= 2 and runs on its own at m = 8), and a
+  group whose members all stream is one launch.
   The group replaces the Q/K/V projection step of research/custom-ops/src/co_decoder.c:128-129.
 * An LM-head-sized M=1 run (N=49152, K=576) against the oracle (tile-16) and FP64 (FP32 mode).
 Tolerance: |y - ref| <= 2e-3 + 2e-3*|ref| element-wise.
@@ -43,11 +44,12 @@ def bits(t, cols):
     return t[:, :cols].cpu().numpy().view(np.uint16)
 
 
-@pytest.mark.parametrize("k", [1, 17, 576, 1000, 1536, 2048, 2056, 4096])
+@pytest.mark.parametrize("k", [1, 17, 576, 1000, 1536, 2048, 2056, 4096, 8192])
 def test_small_m_rows_are_batch_independent_and_within_tolerance(b2, gpu_fd, k):
     """Rows of M=1, 2, 3 and 8 runs agree bit for bit (each x row's result does not depend on the
-    rest of the batch), for the streamed kernel (K <= 2048) and the per-lane-load kernel (K > 2048),
-    in both accumulation modes, with and without bias and HardSigmoid; all rows within tolerance."""
+    rest of the batch, also where M=8 is split into two streamed launches of 4 rows because 8 x rows
+    of K > 2048 exceed the kernel's 32 KB x table), in both accumulation modes, with and without
+    bias and HardSigmoid; all rows within tolerance."""
     n = 300
     x, w, b = uniform_case(8, n, k, 7000 + k)
     ldx, ldy = r8(k), r8(n)
@@ -57,7 +59,7 @@ def test_small_m_rows_are_batch_independent_and_within_tolerance(b2, gpu_fd, k):
             for bias in (b, None):
                 op = b2.Linear(gpu_fd, 1, k, n, w, bias, post=post, mode=b2.CO_CHAIN, acc=acc, compat=False)
                 info = op.info()
-                assert info.kernel == 1 and info.stages == (12 if k <= 2048 else 0)
+                assert info.kernel == 1 and info.stages == 12
                 ys = {m: torch.zeros((m, ldy), dtype=torch.float16, device="cuda") for m in (1, 2, 3, 8)}
                 torch.cuda.synchronize()
                 for m, y in ys.items():
