@@ -25,6 +25,7 @@ enum {
     B2D_ST_NONFINITE_OUTPUT = 2u,
     B2D_ST_NONFINITE_INPUT = 4u,
     B2D_ST_GUARD = 8u,
+    B2D_ST_SCAN_OUTPUT = 16u,       /* internal: a graph output scan found a non-finite value */
 };
 
 /* Largest M served by the weight-streaming small-M kernel; larger M uses the tcgen05 GEMM. */
@@ -93,8 +94,9 @@ typedef struct {
 int b2d_linear(b2_dev *, const b2k_linear *, unsigned *launches);
 int b2d_linear_config(b2_dev *, const b2k_linear *, b2k_config *);
 /* Runs `count` (<= B2D_GROUP_MAX) independent fused Linears with the same m. Those the streamed
- * small-M kernel serves (m <= 8, k <= 2048) share one launch (or several when their distinct
- * inputs exceed its shared x table); any other runs as b2d_linear.
+ * small-M kernel serves in one launch (m <= 8, m x k input within its 32 KB x table, k <= 2048 to
+ * share a launch with others) share one launch (or several when their distinct inputs exceed the
+ * table); any other runs as b2d_linear.
  * Every op must have fused = 1 and raw_only = 0. */
 #define B2D_GROUP_MAX 16u
 int b2d_linear_group(b2_dev *, const b2k_linear *ops, unsigned count, unsigned *launches);

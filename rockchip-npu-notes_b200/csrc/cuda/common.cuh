@@ -21,8 +21,10 @@ namespace b2 {
 
 // Status flag slots (host-mapped pinned memory; one word per kind, written with plain stores so
 // no system-scope atomics are needed). Host side maps them to the B2_STATUS_* bits.
+// FLAG_SCAN_OUTPUT: a finiteness scan of a caller-visible result (the graph's outputs) found a
+// non-finite value; kept apart from FLAG_NONFINITE_OUTPUT, which any kernel raises on an overflow.
 enum : int { FLAG_TIMEOUT = 0, FLAG_NONFINITE_OUTPUT = 1, FLAG_NONFINITE_INPUT = 2, FLAG_GUARD = 3,
-             FLAG_COUNT = 4 };
+             FLAG_SCAN_OUTPUT = 4, FLAG_COUNT = 5 };
 
 __device__ __forceinline__ void raise_flag(unsigned *flags, int idx) {
     volatile unsigned *p = flags + idx;
@@ -91,12 +93,24 @@ __device__ __forceinline__ float gate16(float a, int act) {
     return round16_from_double(g);
 }
 
+// The kernels read the gate of an FP16 input from a table of all 65536 inputs, one per activation
+// (GATE_SIGMOID at [0, 65536), GATE_GELU at [65536, 131072)), filled once per device handle with
+// gate16 itself: the same bits as evaluating it, without double-precision math per element.
+constexpr int GATE_TABLE_ENTRIES = 2 * 65536;
+
+__device__ __forceinline__ float gate16_lut(const __half *table, float a, int act) {
+    const unsigned idx = (unsigned)__half_as_ushort(__float2half_rn(a)) + (act == GATE_GELU ? 65536u : 0u);
+    return __half2float(__ldg(table + idx));
+}
+
 // SiLU / GELU node value of an FP16 a: fp16(a * fp16(gate(a))).
-__device__ __forceinline__ float gated_act16(float a, int act) { return round16(__fmul_rn(a, gate16(a, act))); }
+__device__ __forceinline__ float gated_act16(const __half *table, float a, int act) {
+    return round16(__fmul_rn(a, gate16_lut(table, a, act)));
+}
 
 // The fused gate·up product: fp16(act16(g) * u) for FP16 g, u (the graph's MUL node).
-__device__ __forceinline__ float gated16(float g, float u, int act) {
-    return round16(__fmul_rn(gated_act16(g, act), u));
+__device__ __forceinline__ float gated16(const __half *table, float g, float u, int act) {
+    return round16(__fmul_rn(gated_act16(table, g, act), u));
 }
 
 }  // namespace b2

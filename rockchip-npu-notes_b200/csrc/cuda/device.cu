@@ -28,6 +28,7 @@ struct b2_dev {
     unsigned *flags;        // host pointer of the mapped status words
     unsigned *flags_dev;    // the same words as seen by kernels
     b2::gemv::Scratch gemv; // tile sums and block counters of long-K small-M launches
+    __half *gate_table;     // SiLU / GELU gates of every FP16 input (common.cuh)
 };
 
 namespace {
@@ -46,6 +47,7 @@ inline int flag_of_bit(uint32_t bit) {
         case B2D_ST_NONFINITE_OUTPUT: return b2::FLAG_NONFINITE_OUTPUT;
         case B2D_ST_NONFINITE_INPUT: return b2::FLAG_NONFINITE_INPUT;
         case B2D_ST_GUARD: return b2::FLAG_GUARD;
+        case B2D_ST_SCAN_OUTPUT: return b2::FLAG_SCAN_OUTPUT;
         default: return -1;
     }
 }
@@ -103,6 +105,20 @@ int b2d_open(int ordinal, b2_dev **out) {
     }
     d->gemv.tsum = static_cast<float *>(ts);
     d->gemv.tcount = static_cast<unsigned *>(tc);
+    void *gt = nullptr;
+    if (cudaMalloc(&gt, (size_t)b2::GATE_TABLE_ENTRIES * sizeof(__half)) != cudaSuccess ||
+        b2::graph::fill_gate_table(static_cast<__half *>(gt), d->stream) != cudaSuccess ||
+        cudaStreamSynchronize(d->stream) != cudaSuccess) {
+        cudaGetLastError();
+        if (gt) cudaFree(gt);
+        cudaFree(ts);
+        cudaFree(tc);
+        cudaFreeHost(d->flags);
+        cudaStreamDestroy(d->own);
+        delete d;
+        return ROCKET_E_NOMEM;
+    }
+    d->gate_table = static_cast<__half *>(gt);
     *out = d;
     return 0;
 }
@@ -115,6 +131,7 @@ void b2d_close(b2_dev *d) {
     cudaFreeHost(d->flags);
     cudaFree(d->gemv.tsum);
     cudaFree(d->gemv.tcount);
+    cudaFree(d->gate_table);
     delete d;
 }
 
@@ -194,6 +211,7 @@ uint32_t b2d_status(b2_dev *d, int clear) {
     if (f[b2::FLAG_NONFINITE_OUTPUT]) bits |= B2D_ST_NONFINITE_OUTPUT;
     if (f[b2::FLAG_NONFINITE_INPUT]) bits |= B2D_ST_NONFINITE_INPUT;
     if (f[b2::FLAG_GUARD]) bits |= B2D_ST_GUARD;
+    if (f[b2::FLAG_SCAN_OUTPUT]) bits |= B2D_ST_SCAN_OUTPUT;
     if (clear)
         for (int i = 0; i < b2::FLAG_COUNT; ++i) f[i] = 0;
     return bits;
@@ -202,7 +220,7 @@ uint32_t b2d_status(b2_dev *d, int clear) {
 void b2d_status_merge(b2_dev *d, uint32_t bits) {
     if (!d) return;
     volatile unsigned *f = d->flags;
-    for (uint32_t b = 1; b <= B2D_ST_GUARD; b <<= 1)
+    for (uint32_t b = 1; b <= B2D_ST_SCAN_OUTPUT; b <<= 1)
         if (bits & b) f[flag_of_bit(b)] = 1;
 }
 
@@ -267,6 +285,7 @@ static cudaError_t launch_core(b2_dev *d, const b2k_linear *a, int out_mode, boo
         p.vec_r = a->res && aligned16(a->res) && a->ldr % 8 == 0;
         p.gate = a->gate; p.gate_n = (int)a->gate_n;
         p.bias2 = static_cast<const __half *>(a->bias2);
+        p.gate_table = d->gate_table;
     }
     b2::gemm::Shape s = {a->x, a->ldx, a->w, a->ldw};
     return b2::gemm::launch(s, p, d->stream, d->ordinal, d->sm_count, nullptr);
@@ -306,6 +325,7 @@ static int linear_gated(b2_dev *d, const b2k_linear *a, unsigned *launches) {
     g.bias_gate = static_cast<const __half *>(a->bias);
     g.bias_up = static_cast<const __half *>(a->bias2);
     g.y = static_cast<__half *>(a->y); g.ldy = (long long)a->ldy;
+    g.gate_table = d->gate_table;
     g.flags = d->flags_dev;
     e = b2::graph::gated_combine(g, d->stream, d->sm_count);
     if (e != cudaSuccess) return rc_of(e);
@@ -569,6 +589,7 @@ int b2d_elementwise(b2_dev *d, int op, unsigned rows, unsigned cols, const void 
     p.a = static_cast<const __half *>(a); p.lda = (long long)lda;
     p.b = static_cast<const __half *>(b); p.ldb = (long long)ldb;
     p.y = static_cast<__half *>(y); p.ldy = (long long)ldy;
+    p.gate_table = d->gate_table;
     p.flags = d->flags_dev;
     return rc_of(b2::graph::elementwise(p, d->stream, d->sm_count));
 }

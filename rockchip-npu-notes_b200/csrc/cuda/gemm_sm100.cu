@@ -529,7 +529,8 @@ __device__ __forceinline__ void finish_piece16(const __half2 (&r)[16], const __h
 // with its bias when it has one.
 template <bool BG, bool BU>
 __device__ __forceinline__ void gated_piece(const __half2 (&g)[16], const __half2 (&u)[16], const __half2 (&bg)[16],
-                                            const __half2 (&bu)[16], int act, uint32_t (&pk)[16], bool &bad) {
+                                            const __half2 (&bu)[16], const __half *table, int act, uint32_t (&pk)[16],
+                                            bool &bad) {
 #pragma unroll 4
     for (int i = 0; i < 16; ++i) {
         float2 gs = __half22float2(g[i]), us = __half22float2(u[i]);
@@ -541,7 +542,7 @@ __device__ __forceinline__ void gated_piece(const __half2 (&g)[16], const __half
             const float2 b = __half22float2(bu[i]);
             us = make_float2(round16(__fadd_rn(us.x, b.x)), round16(__fadd_rn(us.y, b.y)));
         }
-        const float y0 = gated16(gs.x, us.x, act), y1 = gated16(gs.y, us.y, act);
+        const float y0 = gated16(table, gs.x, us.x, act), y1 = gated16(table, gs.y, us.y, act);
         bad |= f16_overflows(y0) | f16_overflows(y1);
         pk[i] = pack_half2(y0, y1);
     }
@@ -571,11 +572,11 @@ __device__ __forceinline__ void finish_tile(const Params &p, const __half2 (&run
             load_bias_pairs(p.bias, hb, p.gate_n, bg);
             load_bias_pairs(p.bias2, hb, p.gate_n, bu);
             if (p.bias) {
-                if (p.bias2) gated_piece<true, true>(g, r, bg, bu, p.gate, pk, bad);
-                else gated_piece<true, false>(g, r, bg, bu, p.gate, pk, bad);
+                if (p.bias2) gated_piece<true, true>(g, r, bg, bu, p.gate_table, p.gate, pk, bad);
+                else gated_piece<true, false>(g, r, bg, bu, p.gate_table, p.gate, pk, bad);
             } else {
-                if (p.bias2) gated_piece<false, true>(g, r, bg, bu, p.gate, pk, bad);
-                else gated_piece<false, false>(g, r, bg, bu, p.gate, pk, bad);
+                if (p.bias2) gated_piece<false, true>(g, r, bg, bu, p.gate_table, p.gate, pk, bad);
+                else gated_piece<false, false>(g, r, bg, bu, p.gate_table, p.gate, pk, bad);
             }
             store_out(p, tmap_y, stage, lane, row, row_ok, hb, p.gate_n, pk);
         } else {

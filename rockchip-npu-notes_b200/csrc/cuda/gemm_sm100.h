@@ -46,6 +46,7 @@ struct Params {
     int gate;                    // 0 none, GATE_SIGMOID (SiLU) or GATE_GELU (common.cuh)
     int gate_n;
     const __half *bias2;
+    const __half *gate_table;    // the gate of every FP16 input (common.cuh GATE_TABLE_ENTRIES)
     int tma_y;                   // FP16 output stored through TMA tile stores (set by the launcher)
 };
 

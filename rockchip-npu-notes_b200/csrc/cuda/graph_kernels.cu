@@ -4,7 +4,9 @@
 // tile and the hybrid row operator of co_row_ops.c:150-224:
 //   elementwise    ADD / MUL: y = fp16(a op b) (co_emit_ew); HSIG: fp16(hsig(a)) (co_emit_lut);
 //                  SILU / GELU: y = fp16(a * fp16(gate(a))) (a LUT pass into a gate buffer, then
-//                  co_emit_ew multiply). One FP32 operation on two FP16 values rounded once to FP16
+//                  co_emit_ew multiply), the gate read from the handle's table of every FP16 input
+//                  (fill_gate_table: common.cuh's double-precision gate16, once per handle). One
+//                  FP32 operation on two FP16 values rounded once to FP16
 //                  is the correctly rounded FP16 result (24 >= 2*11 + 2 bits), so these match the
 //                  reference's double-precision restatement bit for bit.
 //   rmsnorm        per row: each 256-column tile's sum of FP16 squares fp16(x*x), summed exactly
@@ -88,7 +90,7 @@ __global__ void __launch_bounds__(THREADS) ew_kernel(EwParams p) {
             for (int e = 0; e < 8; ++e) y[e] = hsig(a[e]);
         } else {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) y[e] = gated_act16(a[e], OP == EW_GELU ? GATE_GELU : GATE_SIGMOID);
+            for (int e = 0; e < 8; ++e) y[e] = gated_act16(p.gate_table, a[e], OP == EW_GELU ? GATE_GELU : GATE_SIGMOID);
         }
 #pragma unroll
         for (int e = 0; e < 8; ++e)
@@ -133,7 +135,7 @@ __global__ void __launch_bounds__(THREADS) gated_kernel(GatedParams p) {
             const float bu = (p.bias_up && in) ? __half2float(p.bias_up[j + e]) : 0.0f;
             const float gv = finish_tile16(g[e], bg, p.bias_gate != nullptr, false);
             const float uv = finish_tile16(u[e], bu, p.bias_up != nullptr, false);
-            y[e] = gated16(gv, uv, p.act);
+            y[e] = gated16(p.gate_table, gv, uv, p.act);
             if (in) bad |= f16_overflows(y[e]);
         }
         store8(p.y + (size_t)r * p.ldy, j, p.gate_n, y);
@@ -145,6 +147,19 @@ cudaError_t gated_combine(const GatedParams &p, cudaStream_t s, int sm_count) {
     if (p.rows <= 0 || p.gate_n <= 0) return cudaSuccess;
     if (p.act != GATE_SIGMOID && p.act != GATE_GELU) return cudaErrorInvalidValue;
     gated_kernel<<<grid_cap((size_t)p.rows * ((p.gate_n + 7) / 8), sm_count, 8), THREADS, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
+// ----------------------------------------------------------------------------- gate table
+__global__ void __launch_bounds__(THREADS) gate_table_kernel(__half *table) {
+    const int i = blockIdx.x * THREADS + threadIdx.x;
+    if (i >= GATE_TABLE_ENTRIES) return;
+    const float a = __half2float(__ushort_as_half((unsigned short)(i & 0xffff)));
+    table[i] = __float2half_rn(gate16(a, i < 65536 ? GATE_SIGMOID : GATE_GELU));   // exact: already FP16
+}
+
+cudaError_t fill_gate_table(__half *table, cudaStream_t s) {
+    gate_table_kernel<<<(GATE_TABLE_ENTRIES + THREADS - 1) / THREADS, THREADS, 0, s>>>(table);
     return cudaGetLastError();
 }
 

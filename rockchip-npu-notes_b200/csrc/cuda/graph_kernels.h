@@ -16,6 +16,7 @@ struct EwParams {
     const __half *a; long long lda;
     const __half *b; long long ldb;      // ADD / MUL only
     __half *y; long long ldy;
+    const __half *gate_table;            // SILU / GELU: the gate of every FP16 input
     unsigned *flags;
 };
 
@@ -33,12 +34,15 @@ struct GatedParams {
     const __half *src; long long lds;    // folded FP16 sums, packed gate|up 64-column blocks
     const __half *bias_gate, *bias_up;   // [gate_n] or nullptr
     __half *y; long long ldy;
+    const __half *gate_table;
     unsigned *flags;
 };
 
 cudaError_t elementwise(const EwParams &p, cudaStream_t s, int sm_count);
 cudaError_t rmsnorm(const NormParams &p, cudaStream_t s, int sm_count);
 cudaError_t gated_combine(const GatedParams &p, cudaStream_t s, int sm_count);
+// Fills table[GATE_TABLE_ENTRIES] (common.cuh) with gate16 of every FP16 input, both activations.
+cudaError_t fill_gate_table(__half *table, cudaStream_t s);
 
 }  // namespace graph
 }  // namespace b2

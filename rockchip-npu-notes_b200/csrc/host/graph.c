@@ -59,7 +59,6 @@ struct co_graph {
     void *gamma[MAXN];
     size_t gamma_bytes[MAXN];
     void *tmp; size_t tmp_bytes;     /* FP16 sums of a gated pair served by the small-M kernel */
-    _Float16 *staging; size_t staging_bytes;   /* pinned host copy of the outputs */
     b2_exec *exec;
     int no_capture;
     unsigned kernels;
@@ -289,8 +288,8 @@ static int analyze(const co_graph_desc *d, const unsigned *outputs, unsigned nou
     }
     for (unsigned s = 0; s < p.slots; s++) p.tensor_bytes += p.slot_bytes[s] + CO_SLACK + CO_GUARD;
     p.workspace_bytes = tmp_bytes;
-    p.tasks += 1;            /* the guard check of every slot */
-    p.chain_submits += 1;
+    p.tasks += 1 + p.noutputs;           /* the guard check of every slot, a scan of each output */
+    p.chain_submits += 1 + p.noutputs;
     p.device_bytes = p.tensor_bytes + p.linear_bytes + p.rowop_bytes + p.workspace_bytes;
     if (p.device_bytes > (d->device_budget ? d->device_budget : CO_LINEAR_DEVICE_BUDGET)) return ROCKET_E_TILING;
     *out = p;
@@ -306,9 +305,19 @@ int co_graph_plan_init(const co_graph_desc *d, co_graph_plan *out) {
     return co_graph_plan_many(d, d ? &d->output : NULL, 1, out);
 }
 
+/* 1 if no FP16 value of v[0, n) is infinite or NaN: four values per 64-bit word at a time (an
+ * exponent field of all ones plus one carries into the lane's sign bit). */
 static int finite16(const _Float16 *v, size_t n) {
     const uint16_t *b = (const uint16_t *)v;
-    for (size_t i = 0; i < n; i++)
+    size_t i = 0;
+    if (((uintptr_t)b & 7u) == 0) {
+        const uint64_t *w = (const uint64_t *)b;
+        uint64_t any = 0;
+        for (size_t j = 0; j < n / 4; j++) any |= ((w[j] & 0x7c007c007c007c00ull) + 0x0400040004000400ull);
+        if (any & 0x8000800080008000ull) return 0;
+        i = n / 4 * 4;
+    }
+    for (; i < n; i++)
         if ((b[i] & 0x7c00u) == 0x7c00u) return 0;
     return 1;
 }
@@ -325,7 +334,6 @@ void co_graph_destroy(co_graph *g) {
         b2h_free(g->fd, g->gamma[i], g->gamma_bytes[i]);
     }
     b2h_free(g->fd, g->tmp, g->tmp_bytes);
-    b2d_host_free(g->staging);
     free(g);
 }
 
@@ -438,13 +446,7 @@ int co_graph_compile_many(int fd, const co_graph_desc *desc, const unsigned *out
     g->plan = plan;
     g->f = f;
     memcpy(g->nodes, desc->nodes, desc->count * sizeof(*desc->nodes));
-    for (unsigned i = 0; i < plan.noutputs; i++) {
-        const co_graph_tensor_plan *t = &plan.tensors[plan.outputs[i]];
-        g->staging_bytes += (size_t)t->rows * t->cols * 2;
-    }
-    if (b2h_fault(B2_FAULT_ALLOC)) rc = ROCKET_E_NOMEM;
-    else if (!(g->staging = b2d_host_alloc(g->staging_bytes))) rc = ROCKET_E_NOMEM;
-    if (!rc) rc = compile_nodes(g, desc);
+    rc = compile_nodes(g, desc);
     if (rc) {
         co_graph_destroy(g);
         return rc;
@@ -559,8 +561,18 @@ static int exec_program(co_graph *g, unsigned *launches) {
     for (unsigned s = 0; s < g->plan.slots; s++) payload[s] = g->plan.slot_bytes[s];
     if (b2h_fault(B2_FAULT_LAUNCH)) return ROCKET_E_DEVICE;
     int rc = b2d_guard_check(b2h_dev(g->fd), g->slot, payload, g->plan.slots, CO_SLACK, CO_GUARD);
-    if (!rc) *launches += 1;
-    return rc;
+    if (rc) return rc;
+    *launches += 1;
+    /* every output must be finite before any is published (co_graph.c:366-367) */
+    for (unsigned i = 0; i < g->plan.noutputs; i++) {
+        unsigned id = g->plan.outputs[i];
+        const co_graph_tensor_plan *t = &g->plan.tensors[id];
+        if (b2h_fault(B2_FAULT_LAUNCH)) return ROCKET_E_DEVICE;
+        rc = b2d_scan_nonfinite(b2h_dev(g->fd), tensor_ptr(g, id), t->rows, t->cols, g->ld[id], B2D_ST_SCAN_OUTPUT);
+        if (rc) return rc;
+        *launches += 1;
+    }
+    return 0;
 }
 
 /* One run of the program on the handle's stream: the recorded CUDA graph in CO_CHAIN (recorded at
@@ -599,7 +611,8 @@ static int launch_program(co_graph *g, unsigned *launches) {
 static int status_rc(uint32_t st) {
     if (st & (B2_STATUS_TIMEOUT | B2_STATUS_GUARD)) return ROCKET_E_DEVICE;
     if (st & B2_STATUS_NONFINITE_INPUT) return ROCKET_E_SHAPE;
-    return 0;   /* an FP16 overflow inside the graph shows in the outputs' finiteness check */
+    if (st & B2D_ST_SCAN_OUTPUT) return ROCKET_E_DEVICE;
+    return 0;   /* an FP16 overflow inside the graph matters only where it reaches an output */
 }
 
 static void count_run(const co_graph *g, unsigned launches) {
@@ -649,30 +662,20 @@ int co_graph_run_many(co_graph *g, const co_graph_input *inputs, unsigned count,
     }
     unsigned launches = 0;
     if (!rc) rc = launch_program(g, &launches);
-    size_t offset = 0;
-    for (unsigned i = 0; i < g->plan.noutputs && !rc; i++) {
-        unsigned id = g->plan.outputs[i];
-        const co_graph_tensor_plan *t = &g->plan.tensors[id];
-        rc = b2d_copy_2d(d, g->staging + offset, (size_t)t->cols * 2, tensor_ptr(g, id), g->ld[id] * 2,
-                         (size_t)t->cols * 2, t->rows, B2D_D2H);
-        offset += (size_t)t->rows * t->cols;
-    }
     int sync_rc = b2d_sync(d);
     if (!rc) rc = sync_rc;
     uint32_t st = b2d_status(d, 1);
     b2d_status_merge(d, prior);
+    if (!rc && b2h_fault(B2_FAULT_NAN_OUTPUT)) st |= B2D_ST_SCAN_OUTPUT;
     if (!rc) rc = status_rc(st);
-    if (!rc && b2h_fault(B2_FAULT_NAN_OUTPUT)) g->staging[0] = (_Float16)NAN;
-    if (!rc && !finite16(g->staging, g->staging_bytes / 2)) rc = ROCKET_E_DEVICE;
-    if (!rc) {
-        offset = 0;
-        for (unsigned i = 0; i < g->plan.noutputs; i++) {
-            unsigned id = g->plan.outputs[i];
-            size_t elements = (size_t)g->plan.tensors[id].rows * g->plan.tensors[id].cols;
-            memcpy(targets[id], g->staging + offset, elements * 2);
-            offset += elements;
-        }
+    /* the run succeeded and every output is finite: publish them */
+    for (unsigned i = 0; i < g->plan.noutputs && !rc; i++) {
+        unsigned id = g->plan.outputs[i];
+        const co_graph_tensor_plan *t = &g->plan.tensors[id];
+        rc = b2d_copy_2d(d, targets[id], (size_t)t->cols * 2, tensor_ptr(g, id), g->ld[id] * 2, (size_t)t->cols * 2,
+                         t->rows, B2D_D2H);
     }
+    if (!rc) rc = b2d_sync(d);
     if (launches) count_run(g, launches);
     return rc;
 }

@@ -173,4 +173,4 @@ def test_device_resident_launch(b2, G, gpu_fd):
     assert g.status() == 0
     got = yout[:, :d].cpu().numpy()
     assert np.array_equal(bits(got), bits(want))
-    assert g.info()["kernels"] == 3       # gated GEMM, residual GEMM, guard check
+    assert g.info()["kernels"] == 4       # gated GEMM, residual GEMM, guard check, output scan
