@@ -20,6 +20,8 @@ scaling, one process per GPU).
             by NCCL all-reduce / reduce-scatter, then the epilogue).
   gemv      M=1 decode projections of a SmolLM-135M-shaped layer (HBM GB/s per launch, weights
             rotated over > 4x L2).
+  gemm_tile16  the same 4096^3 Linear with the reference's per-256-K FP16 running sum (the
+            co_linear_* default numerics), device-resident like `value`.
   graph_ffn the SwiGLU FFN Y = X + Linear(SiLU(Linear(X, Wg, b)) * Linear(X, Wu), Wd) through the
             static graph compiler (co_graph_*) at m = d = h = 4096 and at m = 8 / m = 1: CO_CHAIN
             (fused gate·up GEMM + residual epilogue, one CUDA graph) against CO_SEPARATE, L2
@@ -192,6 +194,11 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-sharded", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--graph-only", action="store_true", help="only the graph FFN section (diagnostics)")
+    ap.add_argument("--graph-m", type=int, nargs="*", default=[4096, 8, 1], help="graph FFN row counts")
+    ap.add_argument("--tile16-only", action="store_true", help="only the tile-16 GEMM section (diagnostics)")
+    ap.add_argument("--linear-shape", type=int, nargs=3, metavar=("M", "N", "K"),
+                    help="time one tile-16 Linear of this shape only (diagnostics)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
@@ -214,6 +221,21 @@ def main():
     fd = b2.open_device(local)
     stream = torch.cuda.ExternalStream(b2.lib().b2_get_stream(fd))
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    if args.linear_shape:   # diagnostics: one Linear shape, no headline line
+        m_, n_, k_ = args.linear_shape
+        print(json.dumps({"linear_shape": bench_linear_shape(b2, fd, torch, stream, peak_tflops, peak_gbs, m_, n_, k_,
+                                                             args.steps)}), flush=True)
+        b2.close(fd)
+        return
+    if args.tile16_only:   # diagnostics (profiling the tile-16 GEMM): no headline line
+        print(json.dumps({"gemm_tile16": bench_tile16(b2, fd, torch, stream, peak_tflops, args.steps)}), flush=True)
+        b2.close(fd)
+        return
+    if args.graph_only:   # diagnostics (profiling the graph section): no headline line
+        print(json.dumps({"graph_ffn": bench_graph(b2, fd, torch, stream, peak_tflops, peak_gbs, args.graph_m)}),
+              flush=True)
+        b2.close(fd)
+        return
 
     # ---------------------------------------------------------------- device-resident timing
     sets = []
@@ -311,10 +333,15 @@ def main():
     if rank == 0 and world == 1 and not args.no_gemv:
         gemv = bench_gemv(b2, fd, torch, stream, peak_gbs)
 
+    # ---------------------------------------------------------------- tile-16 GEMM (rank 0, N=1 only)
+    tile16 = None
+    if rank == 0 and world == 1:
+        tile16 = bench_tile16(b2, fd, torch, stream, peak_tflops, min(steps, 400))
+
     # ---------------------------------------------------------------- graph FFN (rank 0, N=1 only)
     graph = None
     if rank == 0 and world == 1 and not args.no_graph:
-        graph = bench_graph(b2, fd, torch, stream, peak_tflops, peak_gbs)
+        graph = bench_graph(b2, fd, torch, stream, peak_tflops, peak_gbs, args.graph_m)
 
     line = None
     if rank == 0:
@@ -344,6 +371,8 @@ def main():
             line["sharded"] = shard
         if gemv:
             line["gemv"] = gemv
+        if tile16:
+            line["gemm_tile16"] = tile16
         if graph:
             line["graph_ffn"] = graph
         if world == 1 and not args.no_cpu:
@@ -510,7 +539,80 @@ def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup,
     return out
 
 
-def bench_graph(b2, fd, torch, stream, peak_tflops, peak_gbs):
+def bench_tile16(b2, fd, torch, stream, peak_tflops, steps):
+    """The same 4096^3 Linear with the reference's own numerics (per-256-K FP16 running sum,
+    co_linear_create's default; the headline uses FP32 accumulation): 4 rotating X/W/Y sets,
+    back-to-back b2_linear_run_device launches timed with CUDA events on the launching stream."""
+    import numpy as np
+    gen = torch.Generator(device="cuda").manual_seed(77)
+    sets = []
+    for _ in range(4):
+        x = torch.randn(M, K, device="cuda", generator=gen).half()
+        w = (torch.randn(N_PER_GPU, K, device="cuda", generator=gen) / K ** 0.5).half()
+        y = torch.empty(M, N_PER_GPU, device="cuda", dtype=torch.float16)
+        op = b2.Linear(fd, M, K, N_PER_GPU, w.cpu().numpy(), np.zeros(N_PER_GPU, np.float16),
+                       post=b2.CO_LINEAR_NONE, mode=b2.CO_CHAIN, acc=b2.ACC_TILE16, compat=False)
+        sets.append((x, y, op))
+    torch.cuda.synchronize()
+
+    def step(i):
+        x, y, op = sets[i % 4]
+        op.run_device(M, x.data_ptr(), K, y.data_ptr(), N_PER_GPU)
+
+    for i in range(5):
+        step(i)
+    b2.sync(fd)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        s.record(stream)
+        for i in range(steps):
+            step(i)
+        e.record(stream)
+        e.synchronize()
+    if b2.status(fd):
+        raise RuntimeError("device status raised in the tile-16 GEMM")
+    ms = s.elapsed_time(e) / steps
+    tflops = FLOPS_PER_GPU / (ms * 1e-3) / 1e12
+    for _, _, op in sets:
+        op.destroy()
+    return {"ms": ms, "tflops": tflops, "frac": tflops / peak_tflops, "steps": steps,
+            "numerics": "per-256-K FP16 running sum (co_linear_create default)", "clocks": clocks.summary()}
+
+
+def bench_linear_shape(b2, fd, torch, stream, peak_tflops, peak_gbs, m, n, k, steps):
+    """Diagnostics: one tile-16 Linear [m, k] x [n, k]^T through b2_linear_run_device, weights
+    rotated over >= 4x L2 (so every launch streams W from HBM), back-to-back launches timed with
+    CUDA events on the launching stream."""
+    import numpy as np
+    l2 = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
+    wbytes = 2 * n * k
+    copies = max(2, min(64, -(-4 * l2 // wbytes)))
+    w = (np.random.default_rng(n + k).standard_normal((n, k), np.float32) / np.sqrt(k)).astype(np.float16)
+    ops = [b2.Linear(fd, m, k, n, w, None, post=b2.CO_LINEAR_NONE, mode=b2.CO_CHAIN, acc=b2.ACC_TILE16, compat=False)
+           for _ in range(copies)]
+    x = torch.randn(m, k, device="cuda").half()
+    y = torch.empty(m, n, device="cuda", dtype=torch.float16)
+    for op in ops:
+        op.run_device(m, x.data_ptr(), k, y.data_ptr(), n)
+    b2.sync(fd)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for i in range(steps):
+        ops[i % copies].run_device(m, x.data_ptr(), k, y.data_ptr(), n)
+    e.record(stream)
+    e.synchronize()
+    if b2.status(fd):
+        raise RuntimeError("device status raised in the linear-shape run")
+    ms = s.elapsed_time(e) / steps
+    info = ops[0].info()
+    for op in ops:
+        op.destroy()
+    return {"m": m, "n": n, "k": k, "us": ms * 1e3, "tflops": 2 * m * n * k / (ms * 1e-3) / 1e12,
+            "weight_gb_s": wbytes / (ms * 1e-3) / 1e9, "frac_of_hbm": wbytes / (ms * 1e-3) / 1e9 / peak_gbs,
+            "kernel": "gemv" if info.kernel == 1 else "gemm", "weight_copies": copies}
+
+
+def bench_graph(b2, fd, torch, stream, peak_tflops, peak_gbs, rows=(4096, 8, 1)):
     """The SwiGLU FFN of the reference's graph CLI (research/custom-ops/tools/c/graph_cli.c:67-74),
     Y = X + Linear(SiLU(Linear(X, Wg, b)) * Linear(X, Wu), Wd), through the static graph compiler
     (co_graph_*) at the reference graph API's largest shape (m = d = h = 4096) and at decode (m = 8,
@@ -532,7 +634,7 @@ def bench_graph(b2, fd, torch, stream, peak_tflops, peak_gbs):
     bias = (rng.standard_normal(h, np.float32) * 0.1).astype(np.float16)
     out = {"d": d, "h": h, "timing": "b2_graph_launch, CUDA events per step, L2 flushed between steps",
            "cases": {}}
-    for m in (4096, 8, 1):
+    for m in rows:
         x = (np.random.default_rng(m).standard_normal((m, d), np.float32) * 0.7).astype(np.float16)
         nodes, o = G.swiglu_ffn(m, d, h, wg, wu, wd, bias)
         flops = 6 * m * d * h

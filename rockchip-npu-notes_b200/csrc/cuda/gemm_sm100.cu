@@ -531,7 +531,9 @@ template <bool BG, bool BU>
 __device__ __forceinline__ void gated_piece(const __half2 (&g)[16], const __half2 (&u)[16], const __half2 (&bg)[16],
                                             const __half2 (&bu)[16], const __half *table, int act, uint32_t (&pk)[16],
                                             bool &bad) {
-#pragma unroll 4
+    // the 32 gate-table reads of the piece are independent: all in flight at once (the table is an
+    // L2 read: the shared-memory ring leaves little L1)
+#pragma unroll
     for (int i = 0; i < 16; ++i) {
         float2 gs = __half22float2(g[i]), us = __half22float2(u[i]);
         if constexpr (BG) {
