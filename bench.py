@@ -197,8 +197,8 @@ def main():
     ap.add_argument("--graph-only", action="store_true", help="only the graph FFN section (diagnostics)")
     ap.add_argument("--graph-m", type=int, nargs="*", default=[4096, 8, 1], help="graph FFN row counts")
     ap.add_argument("--tile16-only", action="store_true", help="only the tile-16 GEMM section (diagnostics)")
-    ap.add_argument("--linear-shape", type=int, nargs=3, metavar=("M", "N", "K"),
-                    help="time one tile-16 Linear of this shape only (diagnostics)")
+    ap.add_argument("--linear-shape", type=int, nargs="+", metavar="M N K",
+                    help="time tile-16 Linears of these shapes only, given as M N K triples (diagnostics)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
@@ -221,10 +221,13 @@ def main():
     fd = b2.open_device(local)
     stream = torch.cuda.ExternalStream(b2.lib().b2_get_stream(fd))
     gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
-    if args.linear_shape:   # diagnostics: one Linear shape, no headline line
-        m_, n_, k_ = args.linear_shape
-        print(json.dumps({"linear_shape": bench_linear_shape(b2, fd, torch, stream, peak_tflops, peak_gbs, m_, n_, k_,
-                                                             args.steps)}), flush=True)
+    if args.linear_shape:   # diagnostics: Linear shapes (M N K triples), no headline line
+        if len(args.linear_shape) % 3:
+            raise SystemExit("--linear-shape takes M N K triples")
+        for i in range(0, len(args.linear_shape), 3):
+            m_, n_, k_ = args.linear_shape[i:i + 3]
+            print(json.dumps({"linear_shape": bench_linear_shape(b2, fd, torch, stream, peak_tflops, peak_gbs, m_, n_,
+                                                                 k_, args.steps)}), flush=True)
         b2.close(fd)
         return
     if args.tile16_only:   # diagnostics (profiling the tile-16 GEMM): no headline line

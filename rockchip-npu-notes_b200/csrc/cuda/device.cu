@@ -212,8 +212,15 @@ uint32_t b2d_status(b2_dev *d, int clear) {
     if (f[b2::FLAG_NONFINITE_INPUT]) bits |= B2D_ST_NONFINITE_INPUT;
     if (f[b2::FLAG_GUARD]) bits |= B2D_ST_GUARD;
     if (f[b2::FLAG_SCAN_OUTPUT]) bits |= B2D_ST_SCAN_OUTPUT;
-    if (clear)
+    if (clear) {
         for (int i = 0; i < b2::FLAG_COUNT; ++i) f[i] = 0;
+        // A launch that timed out may have left long-K block counters raised: the next launch on
+        // the stream must find them at zero.
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if ((bits & B2D_ST_TIMEOUT) && set_device(d) && cudaStreamIsCapturing(d->stream, &cs) == cudaSuccess &&
+            cs == cudaStreamCaptureStatusNone)
+            cudaMemsetAsync(d->gemv.tcount, 0, (size_t)b2::gemv::TCOUNT_WORDS * sizeof(unsigned), d->stream);
+    }
     return bits;
 }
 
@@ -236,7 +243,7 @@ int b2d_linear_config(b2_dev *d, const b2k_linear *a, b2k_config *cfg) {
         cfg->tile_n = 8;
         cfg->tile_k = 256;
         cfg->grid = b2::gemv::grid_for((int)a->m, (int)a->n, (int)a->k, (long long)a->ldw, d->sm_count);
-        cfg->stages = b2::gemv::stream_launches((int)a->m, (int)a->n, (int)a->k, (long long)a->ldw) ? 12 : 0;
+        cfg->stages = b2::gemv::stream_stages((int)a->m, (int)a->n, (int)a->k, (long long)a->ldw);
     } else {
         cfg->kernel = 0;
         b2::gemm::config_for((int)a->m, (int)a->n, d->sm_count, &cfg->tile_m, &cfg->tile_n, &cfg->stages);

@@ -155,27 +155,42 @@ __global__ void __launch_bounds__(D_THREADS) gemv_direct_kernel(const Params p) 
 
 // ----------------------------------------------------------------------------- streamed kernel
 constexpr long long PDL_MAX_BYTES = 16ll << 20;      // weight bytes up to which launches start early
-constexpr int S_CONSUMERS = 12;                     // consumer warps
-constexpr int S_SLOTS_PER_CONSUMER = 1;             // a slot refills while its consumer works on the other
-constexpr int S_STAGES = S_CONSUMERS * S_SLOTS_PER_CONSUMER;   // one producer lane each: <= 32
-constexpr int S_THREADS = 32 * (1 + S_CONSUMERS);
-constexpr uint32_t S_STAGE_BYTES = (196608u / S_STAGES) & ~127u;
-static_assert(S_STAGE_BYTES == (uint32_t)STREAM_ROW_BYTES, "copy slot size");
-static_assert(16 * STREAM_SLICE * 2 <= STREAM_ROW_BYTES && STREAM_SLICE % 256 == 0, "a 16-row slice fills one slot");
-static_assert(S_STAGES <= 32, "one producer lane per slot");
 struct Meta {
     int prob, row0, rows, slice;   // prob < 0: no more units; slice: K slice of a sliced unit
 };
-// ring | x table | meta | full and empty barriers | abort flag | the group's problems (copied
-// from the kernel parameter once per CTA: dynamically indexed parameter reads are slow)
-constexpr uint32_t S_X_OFFSET = S_STAGES * S_STAGE_BYTES;
-constexpr uint32_t S_META_OFFSET = S_X_OFFSET + STREAM_X_BYTES;
-constexpr uint32_t S_BAR_OFFSET = S_META_OFFSET + S_STAGES * sizeof(Meta);
-constexpr uint32_t S_ABORT_OFFSET = S_BAR_OFFSET + 2 * S_STAGES * 8;
-constexpr uint32_t S_PROB_OFFSET = S_ABORT_OFFSET + 16;
-constexpr uint32_t S_SMEM_BYTES = S_PROB_OFFSET + GROUP_MAX * sizeof(Problem);
-static_assert(S_BAR_OFFSET % 8 == 0 && S_PROB_OFFSET % 8 == 0 && sizeof(Problem) % 8 == 0, "alignment");
-static_assert(S_SMEM_BYTES <= 232448, "shared memory");
+// Sliced launches keep the FP32 tile sums of the 16-row blocks they own in a ring of B_RING
+// shared-memory buffers of 16 rows x M x/K tiles (the host limits M x tiles to 64).
+constexpr int B_RING = 4;
+constexpr int BUF_FLOATS = 16 * STREAM_MAX_XTILES;
+constexpr int TILES_PER_SLICE = STREAM_SLICE / 256;
+constexpr int SWZ_BOX_K = 64;                        // K width of one 128-byte swizzled TMA box
+
+// Shared-memory plan: ring of 16 KB slots (one consumer warp per slot) | x table | meta | full and
+// empty barriers | abort flag | the group's problems (copied from the kernel parameter once per CTA:
+// dynamically indexed parameter reads are slow) | sliced only: tile-sum buffers, their arrival
+// counters and the block each buffer is open to. Whole-row launches use 12 slots; sliced launches
+// (a single long-K problem) give the 12th slot's space to the tile-sum buffers.
+template <bool SL>
+struct SCfg {
+    static constexpr int STAGES = SL ? 11 : 12;
+    static constexpr int THREADS = 32 * (1 + STAGES);
+    static constexpr uint32_t STAGE_BYTES = STREAM_ROW_BYTES;
+    static constexpr int PROBS = SL ? 1 : GROUP_MAX;
+    static constexpr uint32_t X_OFFSET = STAGES * STAGE_BYTES;
+    static constexpr uint32_t META_OFFSET = X_OFFSET + STREAM_X_BYTES;
+    static constexpr uint32_t BAR_OFFSET = META_OFFSET + STAGES * sizeof(Meta);
+    static constexpr uint32_t ABORT_OFFSET = BAR_OFFSET + 2 * STAGES * 8;
+    static constexpr uint32_t PROB_OFFSET = ABORT_OFFSET + 16;
+    static constexpr uint32_t BUF_OFFSET = (PROB_OFFSET + PROBS * (uint32_t)sizeof(Problem) + 15u) & ~15u;
+    static constexpr uint32_t CTL_OFFSET = BUF_OFFSET + (SL ? B_RING * BUF_FLOATS * 4u : 0u);
+    // sliced launches also reserve the room to align the ring to 1024 bytes (swizzle atom)
+    static constexpr uint32_t SMEM_BYTES = CTL_OFFSET + (SL ? 2u * B_RING * 4u + 1024u : 0u);
+};
+static_assert(SCfg<false>::SMEM_BYTES <= 232448 && SCfg<true>::SMEM_BYTES <= 232448, "shared memory");
+static_assert(SCfg<false>::STAGES <= 32 && SCfg<true>::STAGES <= 32, "one producer lane per slot");
+static_assert(SCfg<false>::BAR_OFFSET % 8 == 0 && SCfg<true>::BAR_OFFSET % 8 == 0, "barrier alignment");
+static_assert(SCfg<false>::PROB_OFFSET % 8 == 0 && sizeof(Problem) % 8 == 0, "problem table alignment");
+static_assert(16 * STREAM_SLICE * 2 == STREAM_ROW_BYTES && STREAM_SLICE % 256 == 0, "a 16-row slice fills one slot");
 
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
@@ -190,6 +205,28 @@ __device__ __forceinline__ void tma_box(uint32_t dst, const CUtensorMap *map, ui
                  : "memory");
 }
 
+// Non-blocking test of an mbarrier phase (the producer polls all its slots without suspending).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // D += A * B, m16n8k16, FP16 inputs, FP32 accumulation.
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -200,66 +237,85 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Lane `slot` of warp 0 feeds ring slot `slot`: it streams this CTA's units q = slot, slot +
-// S_STAGES, ... (unit u = blockIdx.x + q * gridDim.x) into that slot, then an end marker. A
-// whole-row unit is one bulk copy of its rows; a sliced unit (one K slice of a 16-row block of a
-// long-K problem, unit = block * slices + slice) is one bulk copy per row onto the slot's barrier.
-// The slots' producers run side by side, so the latency of the barrier and bulk-copy instructions
-// of one slot overlaps the others'. On abort a lane waits (bounded) for its own copy in flight.
+// The units of one CTA. Whole-row launches deal units round-robin (unit blockIdx.x + q * gridDim.x);
+// sliced launches give each CTA one contiguous range [first, end) of the block-major unit order
+// (unit = block * slices + slice), so a CTA sees every slice of most of its blocks and only the
+// blocks at the ends of its range are shared with a neighbour.
+struct Range {
+    long long first, end;
+};
+__device__ __forceinline__ Range cta_range(int units) {
+    return Range{(long long)blockIdx.x * units / gridDim.x, (long long)(blockIdx.x + 1) * units / gridDim.x};
+}
+
+// The producer warp: lane s < STAGES feeds ring slot s with this CTA's local units q = s, s + STAGES,
+// ... then an end marker. All lanes poll their slots' empty barriers together with a non-blocking
+// test, so no lane's wait holds up another lane's copy. A whole-row unit is one bulk copy of its
+// rows; a sliced unit (one 512-wide K slice of a 16-row block) is eight 64 x 16 tensor boxes with
+// the 128-byte swizzle. After an abort or a wait that ran out, each lane waits (bounded) for its own
+// copy in flight.
+template <bool SL>
 __device__ __forceinline__ void produce(const Group &g, const Problem *prob, uint8_t *smem, Meta *meta, uint32_t full0,
-                                        uint32_t empty0, volatile int *abort_flag, int slot) {
+                                        uint32_t empty0, volatile int *abort_flag, int lane) {
+    using C = SCfg<SL>;
     const int count = g.count, units = g.units;
+    const bool mine = lane < C::STAGES;
+    const int slot = mine ? lane : 0;
     const uint32_t full = full0 + 8 * slot, empty = empty0 + 8 * slot;
-    const uint32_t dst = smem_u32(smem + (size_t)slot * S_STAGE_BYTES);
+    const uint32_t dst = smem_u32(smem + (size_t)slot * C::STAGE_BYTES);
+    const Range rg = cta_range(units);
     uint32_t ph = 0;
-    bool armed = false, ok = true;
-    int pi = 0;
-    // the current problem's fields, reloaded only when the unit index crosses into the next one
-    int next_begin = count > 1 ? prob[1].unit_begin : units;
-    int begin = prob[0].unit_begin, R = prob[0].rows_per_unit, N = prob[0].N, K8 = (prob[0].K + 7) & ~7;
-    int kslice = prob[0].kslice, slices = prob[0].slices;
-    long long ldw = prob[0].ldw;
-    const __half *w = prob[0].w;
-    for (int u = blockIdx.x + slot * gridDim.x; u < units; u += S_STAGES * gridDim.x) {
-        if (u >= next_begin) {
-            while (pi + 1 < count && u >= prob[pi + 1].unit_begin) ++pi;
-            next_begin = pi + 1 < count ? prob[pi + 1].unit_begin : units;
-            begin = prob[pi].unit_begin;
-            R = prob[pi].rows_per_unit;
-            N = prob[pi].N;
-            K8 = (prob[pi].K + 7) & ~7;
-            kslice = prob[pi].kslice;
-            slices = prob[pi].slices;
-            ldw = prob[pi].ldw;
-            w = prob[pi].w;
+    bool done = !mine, armed = false;
+    int q = slot, pi = 0;
+    uint64_t t0 = 0;
+    for (uint32_t polls = 1;; ++polls) {
+        if (!done && mbar_test_wait(empty, ph ^ 1u)) {
+            const long long u = SL ? rg.first + q : (long long)blockIdx.x + (long long)q * gridDim.x;
+            if (u < (SL ? rg.end : (long long)units)) {
+                while (pi + 1 < count && u >= prob[pi + 1].unit_begin) ++pi;
+                const Problem &p = prob[pi];
+                const int uq = (int)u - p.unit_begin;
+                const int blk = SL ? uq / p.slices : uq, sl = SL ? uq - blk * p.slices : 0;
+                const int row0 = blk * p.rows_per_unit;
+                meta[slot] = Meta{pi, row0, min(p.rows_per_unit, p.N - row0), sl};
+                if (SL) {
+                    // box b: rows [row0, row0 + 16) x K [k0 + 64b, k0 + 64b + 64); rows past N and
+                    // columns past K arrive as zeros
+                    const int k0 = sl * p.kslice, K8 = (p.K + 7) & ~7;
+                    const int boxes = min(p.kslice / SWZ_BOX_K, (K8 - k0 + SWZ_BOX_K - 1) / SWZ_BOX_K);
+                    mbar_arrive_expect_tx(full, (uint32_t)boxes * 16u * SWZ_BOX_K * 2u);
+                    for (int b = 0; b < boxes; ++b)
+                        tma_box(dst + (uint32_t)b * 16u * SWZ_BOX_K * 2u, &g.wmap, full, k0 + SWZ_BOX_K * b, row0);
+                } else {
+                    const uint32_t bytes = (uint32_t)meta[slot].rows * (uint32_t)p.ldw * 2u;
+                    mbar_arrive_expect_tx(full, bytes);
+                    bulk_g2s(dst, p.w + (size_t)row0 * p.ldw, bytes, full);
+                }
+                armed = true;
+                ph ^= 1u;
+                q += C::STAGES;
+            } else {
+                meta[slot] = Meta{-1, 0, 0, 0};
+                mbar_arrive(full);
+                done = true;
+            }
+            t0 = 0;
         }
-        const int q = u - begin;
-        const int blk = kslice ? q / slices : q, sl = kslice ? q - blk * slices : 0;
-        const int row0 = blk * R;
-        const int rows = min(R, N - row0);
-        if (!wait_phase(empty, ph ^ 1u, abort_flag, g.flags)) {
-            ok = false;
-            break;
+        if (__all_sync(0xffffffffu, done)) return;
+        if ((polls & 255u) == 0) {   // the abort flag and the clock, every 256 polls
+            bool stop = *abort_flag != 0;
+            if (!stop && !done) {
+                const uint64_t t = global_ns();
+                if (!t0) {
+                    t0 = t;
+                } else if (t - t0 > WAIT_LIMIT_NS) {
+                    *abort_flag = 1;
+                    raise_flag(g.flags, FLAG_TIMEOUT);
+                    stop = true;
+                }
+            }
+            if (__any_sync(0xffffffffu, stop)) break;
         }
-        meta[slot] = Meta{pi, row0, rows, sl};
-        if (kslice) {
-            // one 2-D tensor copy per 256-wide half of the slice (rows past N and K past the end
-            // arrive as zeros); box b holds rows [row0, row0+16) x K [k0 + 256b, k0 + 256b + 256)
-            const int k0 = sl * kslice, boxes = min(kslice / 256, (K8 - k0 + 255) / 256);
-            mbar_arrive_expect_tx(full, (uint32_t)boxes * 16u * 256u * 2u);
-            for (int b = 0; b < boxes; ++b) tma_box(dst + (uint32_t)b * 16u * 256u * 2u, &g.wmap, full, k0 + 256 * b, row0);
-        } else {
-            const uint32_t bytes = (uint32_t)rows * (uint32_t)ldw * 2u;
-            mbar_arrive_expect_tx(full, bytes);
-            bulk_g2s(dst, w + (size_t)row0 * ldw, bytes, full);
-        }
-        armed = true;
-        ph ^= 1u;
-    }
-    if (ok && wait_phase(empty, ph ^ 1u, abort_flag, g.flags)) {
-        meta[slot] = Meta{-1, 0, 0, 0};
-        mbar_arrive(full);
-        return;
     }
     if (armed) drain_phase(full, ph ^ 1u);   // the last copy this lane issued
 }
@@ -271,7 +327,7 @@ __device__ __forceinline__ void produce(const Group &g, const Problem *prob, uin
 // product only needs A and B to use the same k order, and this order depends on t alone. Four
 // accumulators (one per 16-wide slice of a 64-wide step) keep consecutive MMAs independent; their
 // sum is the tile sum (tile-16) or the row total (FP32). The accumulator of lane (g, t) holds rows
-// g and g+8 for x rows 2t and 2t+1. The state lives across the K slices of a sliced unit.
+// g and g+8 for x rows 2t and 2t+1.
 struct BlockAcc {
     float acc[4][4];
     float run[4];
@@ -286,31 +342,29 @@ __device__ __forceinline__ void block_reset(BlockAcc &s) {
     for (int i = 0; i < 4; ++i) s.run[i] = 0.0f;
 }
 
-// Accumulates K positions [kb, ke) (ke <= roundup(K, 8); kb and, except at the end, ke multiples of
-// 256) of W rows wa / wc (element 0 of each is K position kb; va / vc: the row exists) against x row
-// xrow (nullptr past M). Tile-16 folds run = fp16(run + tile) at every 256-K tile (the first tile
-// of the row starts the running sum); FP32 keeps summing.
+// Accumulates K positions [0, K8) of W rows wa / wc (va / vc: the row exists) against x row xrow
+// (nullptr past M). Tile-16 folds run = fp16(run + tile) at every 256-K tile (the first tile starts
+// the running sum); FP32 keeps summing.
 __device__ __forceinline__ void block_accumulate(const __half *wa, const __half *wc, bool va, bool vc,
-                                                 const __half *xrow, int kb, int ke, int K8, bool fold, int lane,
-                                                 BlockAcc &s) {
+                                                 const __half *xrow, int K8, bool fold, int lane, BlockAcc &s) {
     const int t4 = lane & 3;
     const uint4 z = make_uint4(0, 0, 0, 0);
-    for (int t0 = kb; t0 < ke; t0 += 256) {
+    for (int t0 = 0; t0 < K8; t0 += 256) {
         if (fold) {
 #pragma unroll
             for (int j = 0; j < 4; ++j)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) s.acc[j][i] = 0.0f;
         }
-        const int kend = min(ke, t0 + 256);
+        const int kend = min(K8, t0 + 256);
 #pragma unroll 4
         for (int kw = t0; kw < kend; kw += 64) {
             const int k0 = kw + t4 * 8, k1 = k0 + 32;
             const bool l0 = k0 < K8, l1 = k1 < K8;
-            const uint4 a0 = (va && l0) ? *reinterpret_cast<const uint4 *>(wa + (k0 - kb)) : z;
-            const uint4 a1 = (va && l1) ? *reinterpret_cast<const uint4 *>(wa + (k1 - kb)) : z;
-            const uint4 b0 = (vc && l0) ? *reinterpret_cast<const uint4 *>(wc + (k0 - kb)) : z;
-            const uint4 b1 = (vc && l1) ? *reinterpret_cast<const uint4 *>(wc + (k1 - kb)) : z;
+            const uint4 a0 = (va && l0) ? *reinterpret_cast<const uint4 *>(wa + k0) : z;
+            const uint4 a1 = (va && l1) ? *reinterpret_cast<const uint4 *>(wa + k1) : z;
+            const uint4 b0 = (vc && l0) ? *reinterpret_cast<const uint4 *>(wc + k0) : z;
+            const uint4 b1 = (vc && l1) ? *reinterpret_cast<const uint4 *>(wc + k1) : z;
             const uint4 x0 = (xrow && l0) ? *reinterpret_cast<const uint4 *>(xrow + k0) : z;
             const uint4 x1 = (xrow && l1) ? *reinterpret_cast<const uint4 *>(xrow + k1) : z;
             mma16816(s.acc[0], a0.x, b0.x, a0.y, b0.y, x0.x, x0.y);
@@ -326,31 +380,37 @@ __device__ __forceinline__ void block_accumulate(const __half *wa, const __half 
     }
 }
 
+// Writes one output: raw FP32 / raw FP16 / bias + activation. Returns true if a final FP16 output is
+// not finite.
+__device__ __forceinline__ bool store_out(const Problem &pr, int xr, int n, float total) {
+    if (pr.out_mode == OUT_RAW32) {
+        pr.partial[(size_t)xr * pr.ldp + n] = total;
+        return false;
+    }
+    if (pr.out_mode == OUT_RAW16) {
+        pr.y[(size_t)xr * pr.ldy + n] = __float2half_rn(total);
+        return false;
+    }
+    const bool has_bias = pr.bias != nullptr;
+    const float b = has_bias ? __half2float(pr.bias[n]) : 0.0f;
+    const float v = pr.fold ? finish_tile16(total, b, has_bias, pr.post) : finish_fp32(total, b, pr.post);
+    const __half h = __float2half_rn(v);
+    pr.y[(size_t)xr * pr.ldy + n] = h;
+    return half_nonfinite(h);
+}
+
 // Writes the block's results: lane (g, t4) element 0 is row g / x row 2t4, 1 row g / x row 2t4+1,
-// 2 and 3 the same for row g+8 (rows relative to the block's first row `n0`). Returns true if a
-// final FP16 output is not finite.
+// 2 and 3 the same for row g+8 (rows relative to the block's first row `n0`).
 __device__ __forceinline__ bool block_finish(const Problem &pr, int M, int n0, int ra, int rc, int rows, int lane,
                                              const BlockAcc &s) {
     const int t4 = lane & 3;
-    const bool fold = pr.fold != 0, has_bias = pr.bias != nullptr;
     bool bad = false;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int r = (i < 2 ? ra : rc), xr = 2 * t4 + (i & 1);
         if (r >= rows || xr >= M) continue;
-        const int n = n0 + r;
-        const float total = fold ? s.run[i] : (s.acc[0][i] + s.acc[1][i]) + (s.acc[2][i] + s.acc[3][i]);
-        if (pr.out_mode == OUT_RAW32) {
-            pr.partial[(size_t)xr * pr.ldp + n] = total;
-        } else if (pr.out_mode == OUT_RAW16) {
-            pr.y[(size_t)xr * pr.ldy + n] = __float2half_rn(total);
-        } else {
-            const float b = has_bias ? __half2float(pr.bias[n]) : 0.0f;
-            const float v = fold ? finish_tile16(total, b, has_bias, pr.post) : finish_fp32(total, b, pr.post);
-            const __half h = __float2half_rn(v);
-            bad |= half_nonfinite(h);
-            pr.y[(size_t)xr * pr.ldy + n] = h;
-        }
+        const float total = pr.fold ? s.run[i] : (s.acc[0][i] + s.acc[1][i]) + (s.acc[2][i] + s.acc[3][i]);
+        bad |= store_out(pr, xr, n0 + r, total);
     }
     return bad;
 }
@@ -366,42 +426,38 @@ __device__ __forceinline__ bool process_unit(const Problem &pr, int M, const __h
         const int ra = rb + g, rc = rb + g + 8;
         BlockAcc s;
         block_reset(s);
-        block_accumulate(stage + (size_t)ra * pr.ldw, stage + (size_t)rc * pr.ldw, ra < rows, rc < rows, xrow, 0, K8,
-                         K8, pr.fold != 0, lane, s);
+        block_accumulate(stage + (size_t)ra * pr.ldw, stage + (size_t)rc * pr.ldw, ra < rows, rc < rows, xrow, K8,
+                         pr.fold != 0, lane, s);
         bad |= block_finish(pr, M, row0, ra, rc, rows, lane, s);
     }
     return bad;
 }
 
-// Slice `sl` of a sliced unit: rows [0, rows <= 16) of the block at row0, staged with pitch kslice,
-// K positions [sl * kslice, ...). Each 256-K tile's FP32 sum goes to the scratch (row, x row, tile);
-// the unit that completes the block's last slice (arrival counter) reads the block's tile sums back
-// in K order and finishes them exactly as the whole-row path does: fp16 fold over the tiles
-// (tile-16) or their FP32 sum, then bias / HardSigmoid. It resets the counter for the next launch.
-template <typename Release>
-__device__ __forceinline__ bool process_slice(const Group &grp, const Problem &pr, int M, const __half *stage,
-                                              const __half *xtab, int row0, int rows, int sl, int lane,
-                                              Release release) {
+// The FP32 sums of the (up to) two 256-K tiles of slice `sl` of a 16-row block, staged as eight
+// 64 x 16 boxes with the 128-byte swizzle (16-byte chunk c of box row r sits at chunk c ^ (r & 7),
+// so the eight rows a warp reads at once fall on different banks). Same products and summation
+// order as block_accumulate: ts[tt][i] is tile 2sl + tt of lane element i.
+__device__ __forceinline__ void slice_sums(const __half *stage, const __half *xrow, bool va, bool vc, int sl, int K8,
+                                           int lane, float (&ts)[TILES_PER_SLICE][4]) {
     const int g = lane >> 2, t4 = lane & 3;
-    const int K8 = (pr.K + 7) & ~7, T = (K8 + 255) >> 8, kb = sl * pr.kslice, ke = min(K8, kb + pr.kslice);
-    const __half *xrow = g < M ? xtab + pr.x_off + (size_t)g * K8 : nullptr;
-    float *ts = grp.scratch.tsum + (size_t)row0 * M * T;   // this block's tile sums
-    const bool va = g < rows, vc = g + 8 < rows;
     const uint4 z = make_uint4(0, 0, 0, 0);
-    for (int t0 = kb; t0 < ke; t0 += 256) {
-        // the tile's box: 16 rows of 256 (rows past N are zeros, never written)
-        const __half *box = stage + (size_t)((t0 - kb) >> 8) * 16 * 256;
-        const __half *wa = box + (size_t)g * 256, *wc = box + (size_t)(g + 8) * 256;
+    const int ca = (t4 ^ g) * 8, cb = ((t4 ^ g) ^ 4) * 8;   // swizzled chunk offsets (halves) of k0, k1
+    const int kb = sl * STREAM_SLICE;
+#pragma unroll
+    for (int tt = 0; tt < TILES_PER_SLICE; ++tt) {
         float acc[4][4] = {};
-        const int kend = min(ke, t0 + 256);
-#pragma unroll 4
-        for (int kw = t0; kw < kend; kw += 64) {
+#pragma unroll
+        for (int st = 0; st < 256 / SWZ_BOX_K; ++st) {
+            const int box = tt * (256 / SWZ_BOX_K) + st;
+            const int kw = kb + box * SWZ_BOX_K;
+            if (kw >= K8) break;   // past the end of K (uniform): the tile ends here
+            const __half *bx = stage + box * 16 * SWZ_BOX_K;
             const int k0 = kw + t4 * 8, k1 = k0 + 32;
             const bool l0 = k0 < K8, l1 = k1 < K8;
-            const uint4 a0 = (va && l0) ? *reinterpret_cast<const uint4 *>(wa + (k0 - t0)) : z;
-            const uint4 a1 = (va && l1) ? *reinterpret_cast<const uint4 *>(wa + (k1 - t0)) : z;
-            const uint4 b0 = (vc && l0) ? *reinterpret_cast<const uint4 *>(wc + (k0 - t0)) : z;
-            const uint4 b1 = (vc && l1) ? *reinterpret_cast<const uint4 *>(wc + (k1 - t0)) : z;
+            const uint4 a0 = (va && l0) ? *reinterpret_cast<const uint4 *>(bx + g * SWZ_BOX_K + ca) : z;
+            const uint4 a1 = (va && l1) ? *reinterpret_cast<const uint4 *>(bx + g * SWZ_BOX_K + cb) : z;
+            const uint4 b0 = (vc && l0) ? *reinterpret_cast<const uint4 *>(bx + (g + 8) * SWZ_BOX_K + ca) : z;
+            const uint4 b1 = (vc && l1) ? *reinterpret_cast<const uint4 *>(bx + (g + 8) * SWZ_BOX_K + cb) : z;
             const uint4 x0 = (xrow && l0) ? *reinterpret_cast<const uint4 *>(xrow + k0) : z;
             const uint4 x1 = (xrow && l1) ? *reinterpret_cast<const uint4 *>(xrow + k1) : z;
             mma16816(acc[0], a0.x, b0.x, a0.y, b0.y, x0.x, x0.y);
@@ -409,61 +465,171 @@ __device__ __forceinline__ bool process_slice(const Group &grp, const Problem &p
             mma16816(acc[2], a1.x, b1.x, a1.y, b1.y, x1.x, x1.y);
             mma16816(acc[3], a1.z, b1.z, a1.w, b1.w, x1.z, x1.w);
         }
-        const int t = t0 >> 8;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ts[tt][i] = (acc[0][i] + acc[1][i]) + (acc[2][i] + acc[3][i]);
+    }
+}
+
+// Shared-memory state of a sliced launch's tile-sum buffers.
+struct SliceCtl {
+    float *buf;              // B_RING x BUF_FLOATS: [row (16)][x row (M)][tile (T)]
+    unsigned *count;         // [B_RING] slices of the buffer's block that have arrived
+    volatile int *open;      // [B_RING] local block index the buffer is open to
+};
+
+// Bounded spin of lane 0 until the buffer is open to local block lb (its previous block was folded).
+__device__ __forceinline__ bool wait_open(const SliceCtl &ctl, int bb, int lb, volatile int *abort_flag,
+                                          unsigned *flags) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 1; ctl.open[bb] != lb; ++i) {
+        if ((i & 255u) == 0) {
+            if (*abort_flag) return false;
+            const uint64_t t = global_ns();
+            if (!t0) {
+                t0 = t;
+            } else if (t - t0 > WAIT_LIMIT_NS) {
+                *abort_flag = 1;
+                raise_flag(flags, FLAG_TIMEOUT);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// Bounded wait of the whole warp (every lane acquires) until `expected` slices have arrived on the
+// block counter from other CTAs.
+__device__ __forceinline__ bool wait_remote(const unsigned *cnt, unsigned expected, volatile int *abort_flag,
+                                            unsigned *flags) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 1; !__all_sync(0xffffffffu, ld_acquire(cnt) >= expected); ++i) {
+        if ((i & 63u) == 0) {
+            bool stop = *abort_flag != 0;
+            if (!stop) {
+                const uint64_t t = global_ns();
+                if (!t0) {
+                    t0 = t;
+                } else if (t - t0 > WAIT_LIMIT_NS) {
+                    stop = true;
+                }
+            }
+            if (__any_sync(0xffffffffu, stop)) {
+                if ((threadIdx.x & 31) == 0 && !*abort_flag) {
+                    *abort_flag = 1;
+                    raise_flag(flags, FLAG_TIMEOUT);
+                }
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// Hands one slice's tile sums on and finishes the block when they complete it. The owner of a
+// block is the CTA whose range holds the block's slice 0. It meets every other slice of the block
+// in its own range, except for the block at the end of its range, whose remaining slices open the
+// ranges of the following CTAs (processed first there, so they are in by the time the owner needs
+// them).
+//   Owner: the sums go to the block's shared buffer. The warp that brings the block's last local
+//   slice folds the tile sums in K order -- the fp16 fold of the tile-16 arithmetic, or their FP32
+//   sum -- after a bounded wait for the other CTAs' slices, writes Y and reopens the buffer.
+//   Other CTAs: the sums go to the block's rows of the device scratch, and one release reduction
+//   counts the slice on the block's counter (nothing waits for it). The owner resets the counter.
+// The bits are those of folding the same tile sums in one place.
+__device__ __forceinline__ bool deliver_slice(const Group &grp, const Problem &pr, int M, const SliceCtl &ctl,
+                                              const Range &rg, int row0, int rows, int sl, int lane,
+                                              const float (&ts)[TILES_PER_SLICE][4], volatile int *abort_flag) {
+    const int g = lane >> 2, t4 = lane & 3;
+    const int K8 = (pr.K + 7) & ~7, T = (K8 + 255) >> 8, S = pr.slices;
+    const int blk = row0 / 16;
+    const long long b0 = (long long)blk * S;   // unit of the block's slice 0
+    const int tiles = min(TILES_PER_SLICE, T - sl * TILES_PER_SLICE);
+    unsigned *cnt = grp.scratch.tcount + blk;
+    float *tg = grp.scratch.tsum + (size_t)row0 * M * T;   // the block's tile sums in the scratch
+    if (b0 < rg.first) {
+#pragma unroll
+        for (int tt = 0; tt < TILES_PER_SLICE; ++tt) {
+            if (tt >= tiles) break;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int r = i < 2 ? g : g + 8, xr = 2 * t4 + (i & 1);
+                if (r < rows && xr < M) tg[((size_t)r * M + xr) * T + sl * TILES_PER_SLICE + tt] = ts[tt][i];
+            }
+        }
+        __syncwarp();   // the warp's sums are ordered before lane 0's release
+        if (lane == 0) red_release_add(cnt, 1u);
+        return false;
+    }
+    const int lb = blk - (int)((rg.first + S - 1) / S);   // local index among the blocks this CTA owns
+    const int bb = lb % B_RING;
+    float *buf = ctl.buf + bb * BUF_FLOATS;
+    bool ok = true;
+    if (lane == 0) {
+        ok = wait_open(ctl, bb, lb, abort_flag, grp.flags);
+        __threadfence_block();
+    }
+    __syncwarp();   // the buffer's previous reads are ordered before this warp's writes
+    if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
+#pragma unroll
+    for (int tt = 0; tt < TILES_PER_SLICE; ++tt) {
+        if (tt >= tiles) break;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int r = i < 2 ? g : g + 8, xr = 2 * t4 + (i & 1);
-            if (r < rows && xr < M) ts[((size_t)r * M + xr) * T + t] = (acc[0][i] + acc[1][i]) + (acc[2][i] + acc[3][i]);
+            if (r < rows && xr < M) buf[(r * M + xr) * T + sl * TILES_PER_SLICE + tt] = ts[tt][i];
         }
     }
-    // the slot's data is consumed: the producer may refill it while the tile sums are published
+    const long long lend = min(rg.end, b0 + S);   // local slices of the block: [b0, lend)
+    const unsigned local = (unsigned)(lend - b0), remote = (unsigned)S - local;
     __syncwarp();
-    release();
-    // arrival: the warp's tile sums (ordered before lane 0's fence by the warp barrier) are visible
-    // device-wide before the block counter moves
-    unsigned *cnt = grp.scratch.tcount + row0 / 16;
     int last = 0;
     if (lane == 0) {
-        __threadfence();
-        last = atomicAdd(cnt, 1u) == (unsigned)(pr.slices - 1);
+        __threadfence_block();
+        last = atomicAdd(&ctl.count[bb], 1u) == local - 1u;
+        __threadfence_block();
     }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return false;
-    __threadfence();   // the other units' tile sums, written before their arrivals
-    const bool fold = pr.fold != 0, has_bias = pr.bias != nullptr;
+    __syncwarp();   // the other warps' sums are ordered before this warp's reads
+    if (!__shfl_sync(0xffffffffu, last, 0)) return false;
+    if (remote && !wait_remote(cnt, remote, abort_flag, grp.flags)) return false;
+    const int ltiles = (int)local * TILES_PER_SLICE;   // tiles [0, ltiles) are in the buffer
     bool bad = false;
     for (int o = lane; o < rows * M; o += 32) {
-        const int r = o / M, xr = o - r * M, n = row0 + r;
-        const float *p = ts + ((size_t)r * M + xr) * T;
+        const int r = o / M, xr = o - r * M;
+        const float *pl = buf + (r * M + xr) * T;
+        const float *pg = tg + ((size_t)r * M + xr) * T;
         float total = 0.0f;
         for (int t = 0; t < T; ++t) {
-            const float v = __ldcg(p + t);
-            total = fold ? fold16(total, v, t == 0) : (t == 0 ? v : total + v);
+            const float v = t < ltiles ? pl[t] : __ldcg(pg + t);
+            total = pr.fold ? fold16(total, v, t == 0) : (t == 0 ? v : total + v);
         }
-        if (pr.out_mode == OUT_RAW32) {
-            pr.partial[(size_t)xr * pr.ldp + n] = total;
-        } else if (pr.out_mode == OUT_RAW16) {
-            pr.y[(size_t)xr * pr.ldy + n] = __float2half_rn(total);
-        } else {
-            const float b = has_bias ? __half2float(pr.bias[n]) : 0.0f;
-            const float v = fold ? finish_tile16(total, b, has_bias, pr.post) : finish_fp32(total, b, pr.post);
-            const __half h = __float2half_rn(v);
-            bad |= half_nonfinite(h);
-            pr.y[(size_t)xr * pr.ldy + n] = h;
-        }
+        bad |= store_out(pr, xr, row0 + r, total);
     }
-    if (lane == 0) *cnt = 0u;   // every unit of this block has arrived: ready for the next launch
+    __syncwarp();
+    if (lane == 0) {
+        if (remote) *cnt = 0u;   // every other slice of this launch has arrived
+        ctl.count[bb] = 0u;
+        __threadfence_block();
+        ctl.open[bb] = lb + B_RING;
+    }
     return bad;
 }
 
-__global__ void __launch_bounds__(S_THREADS, 1) gemv_stream_kernel(const __grid_constant__ Group g) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    Meta *meta = reinterpret_cast<Meta *>(smem + S_META_OFFSET);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S_BAR_OFFSET);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + S_ABORT_OFFSET);
-    Problem *prob = reinterpret_cast<Problem *>(smem + S_PROB_OFFSET);
-    __half *xtab = reinterpret_cast<__half *>(smem + S_X_OFFSET);
-    const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S_STAGES;
+template <bool SL>
+__global__ void __launch_bounds__(SCfg<SL>::THREADS, 1) gemv_stream_kernel(const __grid_constant__ Group g) {
+    using C = SCfg<SL>;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    // sliced launches read 128-byte-swizzled boxes, whose pattern repeats every 1024 bytes
+    uint8_t *smem = SL ? reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                     ~static_cast<uintptr_t>(1023))
+                       : smem_raw;
+    Meta *meta = reinterpret_cast<Meta *>(smem + C::META_OFFSET);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFFSET);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::ABORT_OFFSET);
+    Problem *prob = reinterpret_cast<Problem *>(smem + C::PROB_OFFSET);
+    __half *xtab = reinterpret_cast<__half *>(smem + C::X_OFFSET);
+    SliceCtl ctl{reinterpret_cast<float *>(smem + C::BUF_OFFSET), reinterpret_cast<unsigned *>(smem + C::CTL_OFFSET),
+                 reinterpret_cast<volatile int *>(smem + C::CTL_OFFSET + 4 * B_RING)};
+    const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * C::STAGES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // Programmatic dependent launch (when the launch allows it): the next kernel on the stream may
     // start as SMs free up. This kernel's producer only reads W, which no kernel writes; every read
@@ -472,31 +638,38 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_stream_kernel(const __grid_
     // a write-after-read crosses. Without the attribute both instructions have no effect.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (warp == 0) {
-        // Warp 0 sets up the barriers and the problem table, hands both to the consumer warps with a
-        // non-blocking arrive on named barrier 2, and its producer lanes start streaming at once.
+        // Warp 0 sets up the barriers, the problem table and the tile-sum buffers' state, hands them
+        // to the consumer warps with a non-blocking arrive on named barrier 2, and its producer lanes
+        // start streaming at once.
+        if (SL && lane == 0)
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&g.wmap)) : "memory");
         if (lane == 0) {
-            for (int s = 0; s < S_STAGES; ++s) {
+            for (int s = 0; s < C::STAGES; ++s) {
                 mbar_init(full0 + 8 * s, 1);
                 mbar_init(empty0 + 8 * s, 1);
             }
             *abort_flag = 0;
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         }
+        if (SL && lane < B_RING) {
+            ctl.count[lane] = 0u;
+            ctl.open[lane] = lane;
+        }
         const int words = g.count * (int)(sizeof(Problem) / 8);
         const unsigned long long *src = reinterpret_cast<const unsigned long long *>(g.prob);
         unsigned long long *dst = reinterpret_cast<unsigned long long *>(prob);
         for (int i = lane; i < words; i += 32) dst[i] = src[i];
         __syncwarp();
-        asm volatile("bar.arrive 2, %0;" ::"r"(S_THREADS) : "memory");
-        if (lane < S_STAGES) produce(g, prob, smem, meta, full0, empty0, abort_flag, lane);
+        asm volatile("bar.arrive 2, %0;" ::"r"(C::THREADS) : "memory");
+        produce<SL>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
         return;
     }
-    asm volatile("bar.sync 2, %0;" ::"r"(S_THREADS) : "memory");   // barriers and problem table ready
+    asm volatile("bar.sync 2, %0;" ::"r"(C::THREADS) : "memory");   // barriers and problem table ready
     asm volatile("griddepcontrol.wait;" ::: "memory");              // the previous kernel is done
 
     // The consumer warps fill the x table (x rows, zero past K) while the producer streams W.
     {
-        const int ct = threadIdx.x - 32, nct = S_CONSUMERS * 32;
+        const int ct = threadIdx.x - 32, nct = C::STAGES * 32;
         for (int e = 0; e < g.nx; ++e) {
             const XSource xs = g.xsrc[e];
             const int K8 = (xs.K + 7) & ~7, per_row = K8 / 8;
@@ -517,33 +690,31 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_stream_kernel(const __grid_
         asm volatile("bar.sync 1, %0;" ::"r"(nct) : "memory");
     }
 
-    // Consumer warp c owns slots c, c + S_CONSUMERS, ... and visits them in turn, which is the
-    // order of its units (slot s holds units s, s + S_STAGES, ...); it stops at the first end marker.
+    // Consumer warp c owns slot c and takes its units in order (the producer fills slot c with the
+    // CTA's units c, c + STAGES, ...); it stops at the end marker.
     const int c = warp - 1;
+    const uint32_t full = full0 + 8 * c, empty = empty0 + 8 * c;
+    const __half *stage = reinterpret_cast<const __half *>(smem + (size_t)c * C::STAGE_BYTES);
+    const Range rg = cta_range(g.units);
     bool bad = false;
-    uint32_t ph = 0;
-    for (int j = 0;;) {
-        const int slot = c + S_CONSUMERS * j;
+    for (uint32_t ph = 0;; ph ^= 1u) {
         // Every lane waits (each gets the barrier's acquire); the warp leaves together.
-        const bool ok = __all_sync(0xffffffffu, wait_phase(full0 + 8 * slot, ph, abort_flag, g.flags));
-        if (!ok) break;
-        const Meta mt = meta[slot];
+        if (!__all_sync(0xffffffffu, wait_phase(full, ph, abort_flag, g.flags))) break;
+        const Meta mt = meta[c];
         if (mt.prob < 0) break;
-        const __half *stage = reinterpret_cast<const __half *>(smem + (size_t)slot * S_STAGE_BYTES);
         const Problem &pr = prob[mt.prob];
-        const uint32_t empty = empty0 + 8 * slot;
-        if (pr.kslice) {
-            bad |= process_slice(g, pr, g.M, stage, xtab, mt.row0, mt.rows, mt.slice, lane, [&] {
-                if (lane == 0) mbar_arrive(empty);
-            });
+        if (SL) {
+            const int gq = lane >> 2, K8 = (pr.K + 7) & ~7;
+            const __half *xrow = gq < g.M ? xtab + pr.x_off + (size_t)gq * K8 : nullptr;
+            float ts[TILES_PER_SLICE][4];
+            slice_sums(stage, xrow, gq < mt.rows, gq + 8 < mt.rows, mt.slice, K8, lane, ts);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty);   // the slot refills while the sums are handed on
+            bad |= deliver_slice(g, pr, g.M, ctl, rg, mt.row0, mt.rows, mt.slice, lane, ts, abort_flag);
         } else {
             bad |= process_unit(pr, g.M, stage, xtab, mt.row0, mt.rows, lane);
             __syncwarp();
             if (lane == 0) mbar_arrive(empty);
-        }
-        if (++j == S_SLOTS_PER_CONSUMER) {
-            j = 0;
-            ph ^= 1u;
         }
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) raise_flag(g.flags, FLAG_NONFINITE_OUTPUT);
@@ -560,8 +731,11 @@ cudaError_t stream_attr() {
     static bool done[64] = {};
     const int dev = device_index();
     if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
-    const cudaError_t e =
-        cudaFuncSetAttribute(gemv_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S_SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)SCfg<false>::SMEM_BYTES);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemv_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)SCfg<true>::SMEM_BYTES);
     if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
     return e;
 }
@@ -600,12 +774,12 @@ void plan_units(Group &g, int sm_count) {
     long long total = 0;
     for (int i = 0; i < g.count; ++i) total += (long long)g.prob[i].N * g.prob[i].ldw * 2;
     long long target = total / (2LL * (sm_count > 0 ? sm_count : 1));
-    if (target > (long long)S_STAGE_BYTES) target = S_STAGE_BYTES;
+    if (target > (long long)STREAM_ROW_BYTES) target = STREAM_ROW_BYTES;
     int units = 0;
     for (int i = 0; i < g.count; ++i) {
         Problem &p = g.prob[i];
         const int k8 = (p.K + 7) & ~7;
-        if (k8 > STREAM_WHOLE_K || p.ldw * 2 > (long long)S_STAGE_BYTES) {
+        if (k8 > STREAM_WHOLE_K || p.ldw * 2 > (long long)STREAM_ROW_BYTES) {
             p.kslice = STREAM_SLICE;
             p.slices = (k8 + STREAM_SLICE - 1) / STREAM_SLICE;
             p.rows_per_unit = 16;
@@ -617,7 +791,7 @@ void plan_units(Group &g, int sm_count) {
         p.slices = 1;
         const long long row_bytes = p.ldw * 2;
         long long r = target / row_bytes;
-        const long long rmax = (long long)S_STAGE_BYTES / row_bytes;
+        const long long rmax = (long long)STREAM_ROW_BYTES / row_bytes;
         if (r < 1) r = 1;
         if (r > rmax) r = rmax;
         p.rows_per_unit = (int)r;
@@ -645,17 +819,17 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// W [N, ldw] of which K columns are valid, as 256 (K) x 16 (rows) boxes, unswizzled: the layout
-// process_slice reads. Columns >= K and rows >= N arrive as zeros.
+// W [N, ldw] of which K columns are valid, as 64 (K) x 16 (rows) boxes with the 128-byte swizzle:
+// the layout slice_sums reads. Columns >= K and rows >= N arrive as zeros.
 static bool make_wmap(CUtensorMap *map, const __half *w, int K, int N, long long ldw) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
     cuuint64_t strides[1] = {(cuuint64_t)ldw * 2};
-    cuuint32_t box[2] = {256, 16};
+    cuuint32_t box[2] = {(cuuint32_t)SWZ_BOX_K, 16};
     cuuint32_t estr[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(w), dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -667,7 +841,7 @@ cudaError_t prepare() {
 
 bool sliced(int K, long long ldw) {
     const long long k8 = ((long long)K + 7) & ~7ll;
-    return k8 > STREAM_WHOLE_K || ldw * 2 > (long long)S_STAGE_BYTES;
+    return k8 > STREAM_WHOLE_K || ldw * 2 > (long long)STREAM_ROW_BYTES;
 }
 
 // x rows of one launch: as many as the x table holds (and, for a sliced problem, as many as the
@@ -677,11 +851,18 @@ static long long rows_that_fit(int N, int K, long long ldw) {
     long long fit = (long long)STREAM_X_BYTES / (k8 * 2);
     if (sliced(K, ldw)) {
         if ((N + 15) / 16 > TCOUNT_WORDS) return 0;
-        const long long per_row = ((long long)N + 15) / 16 * 16 * ((k8 + 255) / 256);
-        const long long fs = TSUM_FLOATS / per_row;
+        const long long tiles = (k8 + 255) / 256;
+        const long long per_row = ((long long)N + 15) / 16 * 16 * tiles;
+        const long long fs = TSUM_FLOATS / per_row, fb = STREAM_MAX_XTILES / tiles;
         if (fs < fit) fit = fs;
+        if (fb < fit) fit = fb;
     }
     return fit;
+}
+
+int stream_stages(int M, int N, int K, long long ldw) {
+    if (!stream_launches(M, N, K, ldw)) return 0;
+    return sliced(K, ldw) ? SCfg<true>::STAGES : SCfg<false>::STAGES;
 }
 
 int stream_launches(int M, int N, int K, long long ldw) {
@@ -747,10 +928,11 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
             return cudaErrorInvalidValue;
         const unsigned grid = (unsigned)(g.units < sm_count ? g.units : sm_count);
         if (grid_out) *grid_out = grid;
+        const bool sl = g.prob[0].kslice != 0;   // a sliced problem is alone in its launch
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
-        cfg.blockDim = dim3(S_THREADS);
-        cfg.dynamicSmemBytes = S_SMEM_BYTES;
+        cfg.blockDim = dim3(sl ? SCfg<true>::THREADS : SCfg<false>::THREADS);
+        cfg.dynamicSmemBytes = sl ? SCfg<true>::SMEM_BYTES : SCfg<false>::SMEM_BYTES;
         cfg.stream = stream;
         // Early start of the next kernel pays off where the fixed per-launch cost dominates (it hid
         // 0.6-0.7 us of a 1.8 MB projection) but slowed 56 MB launches with M >= 4 by ~10 %: only
@@ -762,7 +944,8 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
         attr[0].val.programmaticStreamSerializationAllowed = wbytes <= PDL_MAX_BYTES ? 1 : 0;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        const cudaError_t le0 = cudaLaunchKernelEx(&cfg, gemv_stream_kernel, g);
+        const cudaError_t le0 = sl ? cudaLaunchKernelEx(&cfg, gemv_stream_kernel<true>, g)
+                                   : cudaLaunchKernelEx(&cfg, gemv_stream_kernel<false>, g);
         if (le0 != cudaSuccess) return le0;
         const cudaError_t le = cudaGetLastError();
         if (le != cudaSuccess) return le;

@@ -10,9 +10,9 @@ namespace gemv {
 constexpr int MAX_M = 8;
 enum OutMode : int { OUT_FINAL = 0, OUT_RAW16 = 1, OUT_RAW32 = 2 };
 
-// Per-handle device scratch of the long-K (sliced) streamed launches: FP32 sums of every 256-K tile
-// of every (W row, x row), and one arrival counter per 16-row block (zero between launches: the
-// unit that completes a block resets it).
+// Per-handle device scratch of the long-K (sliced) streamed launches: FP32 sums of the 256-K tiles
+// of a (W row, x row) that a CTA computes for a block another CTA finishes, and one arrival counter
+// per 16-row block (zero between launches: the CTA that finishes the block resets it).
 constexpr long long TSUM_FLOATS = 2ll << 20;   // 8 MB
 constexpr int TCOUNT_WORDS = 1 << 16;
 struct Scratch {
@@ -39,10 +39,12 @@ constexpr int STREAM_MAX_M = 8;         // x rows: the n8 dimension of the m16n8
 constexpr int STREAM_X_BYTES = 32768;   // shared-memory table of the launch's distinct x rows
 constexpr int STREAM_ROW_BYTES = 16384; // one copy slot
 // A unit of a problem with K <= STREAM_WHOLE_K is whole W rows (as many as fill a slot); above it a
-// unit is a 16-row block whose K is streamed in slices of STREAM_SLICE through the same slot, so the
-// 16 W rows of every m16n8k16 MMA are real rows however long K is.
+// unit is one K slice of STREAM_SLICE of a 16-row block, so the 16 W rows of every m16n8k16 MMA are
+// real rows however long K is. Each CTA takes a contiguous range of the block-major unit order and
+// finishes the blocks whose first slice it holds.
 constexpr int STREAM_WHOLE_K = 2048;
 constexpr int STREAM_SLICE = 512;       // 16 rows x 512 FP16 = one slot; a multiple of the 256-K tile
+constexpr int STREAM_MAX_XTILES = 64;   // sliced launches: M x (256-K tiles) per block buffer
 
 struct Problem {
     const __half *x; long long ldx;
@@ -76,12 +78,17 @@ struct Group {
 
 // The streamed kernel serves M <= 8 when the M x rows fit the x table (M * roundup(K, 8) FP16):
 // K <= 16384 for M = 1, 8192 for M = 2, 4096 for M = 4, 2048 for M = 8; a long-K problem also needs
-// its tile sums (N * M * K/256 floats) and block counters (N / 16) to fit the scratch.
+// M x (K/256 tiles) <= STREAM_MAX_XTILES, its tile sums (N * M * K/256 floats) and block counters
+// (N / 16) to fit the scratch.
 bool streamed(int M, int N, int K, long long ldw);
 // Streamed launches that serve a single problem in `launch`: 1 when streamed(), else M is split into
 // row groups whose x rows fit the table (each group streams all of W; every row's result is the same
 // as in a one-launch run); 0 when no row group fits: the per-lane kernel serves it.
 int stream_launches(int M, int N, int K, long long ldw);
+
+// Ring slots of the streamed kernel that would serve this shape (11 for long K, else 12); 0 when
+// the per-lane-load kernel serves it.
+int stream_stages(int M, int N, int K, long long ldw);
 
 // Picks the kernel for p (streamed when eligible, else the per-lane-load kernel) and launches it.
 cudaError_t launch(const Params &p, cudaStream_t stream, int sm_count, unsigned *grid_out);
