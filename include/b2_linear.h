@@ -128,7 +128,7 @@ typedef struct {
     unsigned m, k, n;
     unsigned kernel;             /* 0 = tcgen05 GEMM, 1 = GEMV (small M) */
     unsigned tile_m, tile_n, tile_k;
-    unsigned stages;             /* GEMM: TMA ring depth; streamed GEMV: 12 copy slots; else 0 */
+    unsigned stages;             /* GEMM: TMA ring depth; streamed GEMV: copy slots (6, 11 or 12); else 0 */
     unsigned grid;               /* CTAs of the main kernel for the create-time m */
     unsigned launches_per_run;   /* CUDA launches of one co_linear_run */
     enum b2_accumulate acc;

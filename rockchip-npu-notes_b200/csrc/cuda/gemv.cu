@@ -14,7 +14,9 @@
 //   in slot s and computes them on the tensor cores (below). The launch's x rows are copied once per CTA into a 32 KB shared table (problems
 //   that share an input share the entry), filled by the consumer warps while the first weights
 //   are in flight. A launch covers a group of up to GROUP_MAX independent projections (same M):
-//   units of R rows from all of them are spread over the CTAs.
+//   units of R rows from all of them are spread over the CTAs. Launches whose x rows fit 12 KB run
+//   as half-SM CTAs (6 slots, two CTAs per SM) under programmatic dependent launch, so the next
+//   launch's CTAs stream their weights while this launch runs or drains (see half_sm).
 // Per-lane-load kernel (the other M <= 8 shapes): each warp owns one W row at a time and every
 //   lane reads 16 bytes per 256-element K tile with read-only, L1-bypassing loads; several tiles'
 //   loads are issued before any arithmetic. The grid is the number of co-resident CTAs.
@@ -170,14 +172,21 @@ constexpr int SWZ_BOX_K = 64;                        // K width of one 128-byte 
 // dynamically indexed parameter reads are slow) | sliced only: tile-sum buffers, their arrival
 // counters and the block each buffer is open to. Whole-row launches use 12 slots; sliced launches
 // (a single long-K problem) give the 12th slot's space to the tile-sum buffers.
-template <bool SL>
+// Half-SM whole-row launches (HF: see half_sm) use 6 slots and the small x table, ~110 KB in all,
+// so two CTAs fit one SM: a CTA of the next launch on the stream (programmatic dependent launch)
+// becomes resident while this launch's CTA still runs there and streams its own weights into its
+// ring, hiding the launch's ramp-up and tail.
+template <bool SL, bool HF = false>
 struct SCfg {
-    static constexpr int STAGES = SL ? 11 : 12;
+    static_assert(!(SL && HF), "half-SM launches are whole-row launches");
+    static constexpr int STAGES = HF ? 6 : (SL ? 11 : 12);
     static constexpr int THREADS = 32 * (1 + STAGES);
+    static constexpr int MIN_BLOCKS = HF ? 2 : 1;
     static constexpr uint32_t STAGE_BYTES = STREAM_ROW_BYTES;
     static constexpr int PROBS = SL ? 1 : GROUP_MAX;
+    static constexpr uint32_t X_BYTES = HF ? STREAM_X_HALF_BYTES : STREAM_X_BYTES;
     static constexpr uint32_t X_OFFSET = STAGES * STAGE_BYTES;
-    static constexpr uint32_t META_OFFSET = X_OFFSET + STREAM_X_BYTES;
+    static constexpr uint32_t META_OFFSET = X_OFFSET + X_BYTES;
     static constexpr uint32_t BAR_OFFSET = META_OFFSET + STAGES * sizeof(Meta);
     static constexpr uint32_t ABORT_OFFSET = BAR_OFFSET + 2 * STAGES * 8;
     static constexpr uint32_t PROB_OFFSET = ABORT_OFFSET + 16;
@@ -187,9 +196,13 @@ struct SCfg {
     static constexpr uint32_t SMEM_BYTES = CTL_OFFSET + (SL ? 2u * B_RING * 4u + 1024u : 0u);
 };
 static_assert(SCfg<false>::SMEM_BYTES <= 232448 && SCfg<true>::SMEM_BYTES <= 232448, "shared memory");
+// two half-SM CTAs (each with the 1 KB the hardware reserves per CTA) in the SM's 228 KB
+static_assert(2 * (SCfg<false, true>::SMEM_BYTES + 1024) <= 233472, "two half-SM CTAs per SM");
 static_assert(SCfg<false>::STAGES <= 32 && SCfg<true>::STAGES <= 32, "one producer lane per slot");
-static_assert(SCfg<false>::BAR_OFFSET % 8 == 0 && SCfg<true>::BAR_OFFSET % 8 == 0, "barrier alignment");
-static_assert(SCfg<false>::PROB_OFFSET % 8 == 0 && sizeof(Problem) % 8 == 0, "problem table alignment");
+static_assert(SCfg<false>::BAR_OFFSET % 8 == 0 && SCfg<true>::BAR_OFFSET % 8 == 0 &&
+              SCfg<false, true>::BAR_OFFSET % 8 == 0, "barrier alignment");
+static_assert(SCfg<false>::PROB_OFFSET % 8 == 0 && SCfg<false, true>::PROB_OFFSET % 8 == 0 &&
+              sizeof(Problem) % 8 == 0, "problem table alignment");
 static_assert(16 * STREAM_SLICE * 2 == STREAM_ROW_BYTES && STREAM_SLICE % 256 == 0, "a 16-row slice fills one slot");
 
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
@@ -254,10 +267,10 @@ __device__ __forceinline__ Range cta_range(int units) {
 // rows; a sliced unit (one 512-wide K slice of a 16-row block) is eight 64 x 16 tensor boxes with
 // the 128-byte swizzle. After an abort or a wait that ran out, each lane waits (bounded) for its own
 // copy in flight.
-template <bool SL>
+template <bool SL, bool HF>
 __device__ __forceinline__ void produce(const Group &g, const Problem *prob, uint8_t *smem, Meta *meta, uint32_t full0,
                                         uint32_t empty0, volatile int *abort_flag, int lane) {
-    using C = SCfg<SL>;
+    using C = SCfg<SL, HF>;
     const int count = g.count, units = g.units;
     const bool mine = lane < C::STAGES;
     const int slot = mine ? lane : 0;
@@ -614,9 +627,10 @@ __device__ __forceinline__ bool deliver_slice(const Group &grp, const Problem &p
     return bad;
 }
 
-template <bool SL>
-__global__ void __launch_bounds__(SCfg<SL>::THREADS, 1) gemv_stream_kernel(const __grid_constant__ Group g) {
-    using C = SCfg<SL>;
+template <bool SL, bool HF>
+__global__ void __launch_bounds__(SCfg<SL, HF>::THREADS, SCfg<SL, HF>::MIN_BLOCKS)
+    gemv_stream_kernel(const __grid_constant__ Group g) {
+    using C = SCfg<SL, HF>;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // sliced launches read 128-byte-swizzled boxes, whose pattern repeats every 1024 bytes
     uint8_t *smem = SL ? reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -661,7 +675,7 @@ __global__ void __launch_bounds__(SCfg<SL>::THREADS, 1) gemv_stream_kernel(const
         for (int i = lane; i < words; i += 32) dst[i] = src[i];
         __syncwarp();
         asm volatile("bar.arrive 2, %0;" ::"r"(C::THREADS) : "memory");
-        produce<SL>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
+        produce<SL, HF>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
         return;
     }
     asm volatile("bar.sync 2, %0;" ::"r"(C::THREADS) : "memory");   // barriers and problem table ready
@@ -731,11 +745,14 @@ cudaError_t stream_attr() {
     static bool done[64] = {};
     const int dev = device_index();
     if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)SCfg<false>::SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<false, false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SCfg<false>::SMEM_BYTES);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemv_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(gemv_stream_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)SCfg<true>::SMEM_BYTES);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemv_stream_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)SCfg<false, true>::SMEM_BYTES);
     if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
     return e;
 }
@@ -844,6 +861,19 @@ bool sliced(int K, long long ldw) {
     return k8 > STREAM_WHOLE_K || ldw * 2 > (long long)STREAM_ROW_BYTES;
 }
 
+// Half-SM CTAs (6 slots, two CTAs per SM) serve the whole-row launches whose x rows fit the small
+// table, with programmatic dependent launch:
+//   * up to PDL_MAX_BYTES of weights, one CTA per SM: the next launch's CTA becomes resident beside
+//     this one and prefetches its weights while this one runs (1.8 MB projection 3.3 -> 2.6 us);
+//   * larger launches, two CTAs per SM (192 KB in flight per SM, as with full-SM CTAs; one 96 KB CTA
+//     per SM streamed the 56 MB LM head in 13.9 us against 12.4 us): each CTA of the next launch takes
+//     the place of one that exits and streams during this launch's drain (LM head 12.4 -> 11.5 us).
+static bool half_sm(bool sl, long long x_elems) { return !sl && x_elems * 2 <= STREAM_X_HALF_BYTES; }
+static unsigned stream_grid(bool hf, long long wbytes, int units, int sm_count) {
+    const int ctas = hf && wbytes > PDL_MAX_BYTES ? 2 * sm_count : sm_count;
+    return (unsigned)(units < ctas ? units : ctas);
+}
+
 // x rows of one launch: as many as the x table holds (and, for a sliced problem, as many as the
 // scratch holds the tile sums of); 0 when not even one fits.
 static long long rows_that_fit(int N, int K, long long ldw) {
@@ -862,7 +892,9 @@ static long long rows_that_fit(int N, int K, long long ldw) {
 
 int stream_stages(int M, int N, int K, long long ldw) {
     if (!stream_launches(M, N, K, ldw)) return 0;
-    return sliced(K, ldw) ? SCfg<true>::STAGES : SCfg<false>::STAGES;
+    if (sliced(K, ldw)) return SCfg<true>::STAGES;
+    const long long xelems = (long long)M * (((long long)K + 7) & ~7ll);
+    return half_sm(false, xelems) ? SCfg<false, true>::STAGES : SCfg<false>::STAGES;
 }
 
 int stream_launches(int M, int N, int K, long long ldw) {
@@ -926,26 +958,35 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
         plan_units(g, sm_count);
         if (g.prob[0].kslice && !make_wmap(&g.wmap, g.prob[0].w, g.prob[0].K, g.prob[0].N, g.prob[0].ldw))
             return cudaErrorInvalidValue;
-        const unsigned grid = (unsigned)(g.units < sm_count ? g.units : sm_count);
-        if (grid_out) *grid_out = grid;
         const bool sl = g.prob[0].kslice != 0;   // a sliced problem is alone in its launch
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(grid);
-        cfg.blockDim = dim3(sl ? SCfg<true>::THREADS : SCfg<false>::THREADS);
-        cfg.dynamicSmemBytes = sl ? SCfg<true>::SMEM_BYTES : SCfg<false>::SMEM_BYTES;
-        cfg.stream = stream;
-        // Early start of the next kernel pays off where the fixed per-launch cost dominates (it hid
-        // 0.6-0.7 us of a 1.8 MB projection) but slowed 56 MB launches with M >= 4 by ~10 %: only
-        // launches of at most PDL_MAX_BYTES of weights allow it.
+        int xused = 0;                           // FP16 elements of the x table this launch fills
+        for (int e = 0; e < g.nx; ++e) {
+            const int end = g.xsrc[e].off + g.M * ((g.xsrc[e].K + 7) & ~7);
+            if (end > xused) xused = end;
+        }
         long long wbytes = 0;
         for (int i = 0; i < g.count; ++i) wbytes += (long long)g.prob[i].N * g.prob[i].ldw * 2;
+        const bool hf = half_sm(sl, xused);
+        const unsigned grid = stream_grid(hf, wbytes, g.units, sm_count);
+        if (grid_out) *grid_out = grid;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(sl ? SCfg<true>::THREADS : hf ? SCfg<false, true>::THREADS : SCfg<false>::THREADS);
+        cfg.dynamicSmemBytes = sl ? SCfg<true>::SMEM_BYTES : hf ? SCfg<false, true>::SMEM_BYTES
+                                                               : SCfg<false>::SMEM_BYTES;
+        cfg.stream = stream;
+        // Early start of the next kernel: always for half-SM launches (half_sm); full-SM launches
+        // (whose next CTAs cannot become resident before this launch's exit) allow it where the fixed
+        // per-launch cost dominates (it hid 0.6-0.7 us of a 1.8 MB projection), up to PDL_MAX_BYTES
+        // of weights (it had slowed 56 MB full-SM launches with M >= 4 by ~10 %).
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = wbytes <= PDL_MAX_BYTES ? 1 : 0;
+        attr[0].val.programmaticStreamSerializationAllowed = (hf || wbytes <= PDL_MAX_BYTES) ? 1 : 0;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        const cudaError_t le0 = sl ? cudaLaunchKernelEx(&cfg, gemv_stream_kernel<true>, g)
-                                   : cudaLaunchKernelEx(&cfg, gemv_stream_kernel<false>, g);
+        const cudaError_t le0 = sl   ? cudaLaunchKernelEx(&cfg, gemv_stream_kernel<true, false>, g)
+                                : hf ? cudaLaunchKernelEx(&cfg, gemv_stream_kernel<false, true>, g)
+                                     : cudaLaunchKernelEx(&cfg, gemv_stream_kernel<false, false>, g);
         if (le0 != cudaSuccess) return le0;
         const cudaError_t le = cudaGetLastError();
         if (le != cudaSuccess) return le;
@@ -964,7 +1005,8 @@ unsigned grid_for(int M, int N, int K, long long ldw, int sm_count) {
     g.prob[0].K = K;
     g.prob[0].ldw = ldw;
     plan_units(g, sm_count);
-    return (unsigned)(g.units < sm_count ? g.units : sm_count);
+    const bool hf = half_sm(sliced(K, ldw), (long long)M * (((long long)K + 7) & ~7ll));
+    return stream_grid(hf, (long long)N * ldw * 2, g.units, sm_count);
 }
 
 cudaError_t launch(const Params &p, cudaStream_t stream, int sm_count, unsigned *grid_out) {

@@ -37,6 +37,7 @@ struct Params {
 constexpr int GROUP_MAX = 16;
 constexpr int STREAM_MAX_M = 8;         // x rows: the n8 dimension of the m16n8k16 MMA
 constexpr int STREAM_X_BYTES = 32768;   // shared-memory table of the launch's distinct x rows
+constexpr int STREAM_X_HALF_BYTES = 12288; // the x table of half-SM launches (two CTAs per SM)
 constexpr int STREAM_ROW_BYTES = 16384; // one copy slot
 // A unit of a problem with K <= STREAM_WHOLE_K is whole W rows (as many as fill a slot); above it a
 // unit is one K slice of STREAM_SLICE of a 16-row block, so the 16 W rows of every m16n8k16 MMA are
@@ -86,8 +87,8 @@ bool streamed(int M, int N, int K, long long ldw);
 // as in a one-launch run); 0 when no row group fits: the per-lane kernel serves it.
 int stream_launches(int M, int N, int K, long long ldw);
 
-// Ring slots of the streamed kernel that would serve this shape (11 for long K, else 12); 0 when
-// the per-lane-load kernel serves it.
+// Ring slots of the streamed kernel that would serve this shape (11 for long K; 6 for a half-SM
+// launch, whose x rows fit STREAM_X_HALF_BYTES; else 12); 0 when the per-lane-load kernel serves it.
 int stream_stages(int M, int N, int K, long long ldw);
 
 // Picks the kernel for p (streamed when eligible, else the per-lane-load kernel) and launches it.
