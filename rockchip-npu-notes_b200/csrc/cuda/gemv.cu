@@ -355,13 +355,34 @@ __device__ __forceinline__ void block_reset(BlockAcc &s) {
     for (int i = 0; i < 4; ++i) s.run[i] = 0.0f;
 }
 
-// Accumulates K positions [0, K8) of W rows wa / wc (va / vc: the row exists) against x row xrow
-// (nullptr past M). Tile-16 folds run = fp16(run + tile) at every 256-K tile (the first tile starts
-// the running sum); FP32 keeps summing.
-__device__ __forceinline__ void block_accumulate(const __half *wa, const __half *wc, bool va, bool vc,
-                                                 const __half *xrow, int K8, bool fold, int lane, BlockAcc &s) {
-    const int t4 = lane & 3;
+// One 64-wide K window at kw: 4 MMAs over W rows wa / wc and x row xrow. With `tail`, chunks at or
+// past K8 load as zeros (only the last window of a K that is not a multiple of 64).
+template <bool TAIL>
+__device__ __forceinline__ void block_window(const __half *wa, const __half *wc, const __half *xrow, int kw, int K8,
+                                             int t4, BlockAcc &s) {
     const uint4 z = make_uint4(0, 0, 0, 0);
+    const int k0 = kw + t4 * 8, k1 = k0 + 32;
+    const bool l0 = !TAIL || k0 < K8, l1 = !TAIL || k1 < K8;
+    const uint4 a0 = l0 ? *reinterpret_cast<const uint4 *>(wa + k0) : z;
+    const uint4 a1 = l1 ? *reinterpret_cast<const uint4 *>(wa + k1) : z;
+    const uint4 b0 = l0 ? *reinterpret_cast<const uint4 *>(wc + k0) : z;
+    const uint4 b1 = l1 ? *reinterpret_cast<const uint4 *>(wc + k1) : z;
+    const uint4 x0 = l0 ? *reinterpret_cast<const uint4 *>(xrow + k0) : z;
+    const uint4 x1 = l1 ? *reinterpret_cast<const uint4 *>(xrow + k1) : z;
+    mma16816(s.acc[0], a0.x, b0.x, a0.y, b0.y, x0.x, x0.y);
+    mma16816(s.acc[1], a0.z, b0.z, a0.w, b0.w, x0.z, x0.w);
+    mma16816(s.acc[2], a1.x, b1.x, a1.y, b1.y, x1.x, x1.y);
+    mma16816(s.acc[3], a1.z, b1.z, a1.w, b1.w, x1.z, x1.w);
+}
+
+// Accumulates K positions [0, K8) of W rows wa / wc against x row xrow. Rows past the unit and x rows
+// past M are given the pointer of a real row by the caller: they only feed outputs that are never
+// stored, so every full window loads without predication. Tile-16 folds run = fp16(run + tile) at
+// every 256-K tile (the first tile starts the running sum); FP32 keeps summing.
+__device__ __forceinline__ void block_accumulate(const __half *wa, const __half *wc, const __half *xrow, int K8,
+                                                 bool fold, int lane, BlockAcc &s) {
+    const int t4 = lane & 3;
+    const int full = K8 & ~63;   // K covered by full 64-wide windows
     for (int t0 = 0; t0 < K8; t0 += 256) {
         if (fold) {
 #pragma unroll
@@ -369,21 +390,14 @@ __device__ __forceinline__ void block_accumulate(const __half *wa, const __half 
 #pragma unroll
                 for (int i = 0; i < 4; ++i) s.acc[j][i] = 0.0f;
         }
-        const int kend = min(K8, t0 + 256);
-#pragma unroll 4
-        for (int kw = t0; kw < kend; kw += 64) {
-            const int k0 = kw + t4 * 8, k1 = k0 + 32;
-            const bool l0 = k0 < K8, l1 = k1 < K8;
-            const uint4 a0 = (va && l0) ? *reinterpret_cast<const uint4 *>(wa + k0) : z;
-            const uint4 a1 = (va && l1) ? *reinterpret_cast<const uint4 *>(wa + k1) : z;
-            const uint4 b0 = (vc && l0) ? *reinterpret_cast<const uint4 *>(wc + k0) : z;
-            const uint4 b1 = (vc && l1) ? *reinterpret_cast<const uint4 *>(wc + k1) : z;
-            const uint4 x0 = (xrow && l0) ? *reinterpret_cast<const uint4 *>(xrow + k0) : z;
-            const uint4 x1 = (xrow && l1) ? *reinterpret_cast<const uint4 *>(xrow + k1) : z;
-            mma16816(s.acc[0], a0.x, b0.x, a0.y, b0.y, x0.x, x0.y);
-            mma16816(s.acc[1], a0.z, b0.z, a0.w, b0.w, x0.z, x0.w);
-            mma16816(s.acc[2], a1.x, b1.x, a1.y, b1.y, x1.x, x1.y);
-            mma16816(s.acc[3], a1.z, b1.z, a1.w, b1.w, x1.z, x1.w);
+        if (t0 + 256 <= full) {
+#pragma unroll
+            for (int w = 0; w < 4; ++w) block_window<false>(wa, wc, xrow, t0 + 64 * w, K8, t4, s);
+        } else {
+            const int kend = min(K8, t0 + 256);
+            int kw = t0;
+            for (; kw + 64 <= kend; kw += 64) block_window<false>(wa, wc, xrow, kw, K8, t4, s);
+            if (kw < kend) block_window<true>(wa, wc, xrow, kw, K8, t4, s);
         }
         if (fold) {
 #pragma unroll
@@ -395,7 +409,11 @@ __device__ __forceinline__ void block_accumulate(const __half *wa, const __half 
 
 // Writes one output: raw FP32 / raw FP16 / bias + activation. Returns true if a final FP16 output is
 // not finite.
-__device__ __forceinline__ bool store_out(const Problem &pr, int xr, int n, float total) {
+// `b` is bias[n] (0 without a bias), loaded by the caller ahead of the sums.
+__device__ __forceinline__ float bias_at(const Problem &pr, int n, bool valid) {
+    return (pr.bias && valid) ? __half2float(__ldg(pr.bias + n)) : 0.0f;
+}
+__device__ __forceinline__ bool store_out(const Problem &pr, int xr, int n, float total, float b) {
     if (pr.out_mode == OUT_RAW32) {
         pr.partial[(size_t)xr * pr.ldp + n] = total;
         return false;
@@ -405,17 +423,26 @@ __device__ __forceinline__ bool store_out(const Problem &pr, int xr, int n, floa
         return false;
     }
     const bool has_bias = pr.bias != nullptr;
-    const float b = has_bias ? __half2float(pr.bias[n]) : 0.0f;
     const float v = pr.fold ? finish_tile16(total, b, has_bias, pr.post) : finish_fp32(total, b, pr.post);
     const __half h = __float2half_rn(v);
     pr.y[(size_t)xr * pr.ldy + n] = h;
     return half_nonfinite(h);
 }
+__device__ __forceinline__ bool store_out(const Problem &pr, int xr, int n, float total) {
+    return store_out(pr, xr, n, total, bias_at(pr, n, pr.out_mode == OUT_FINAL));
+}
+
+// Hands the warp's ring slot back to the producer: every lane's reads of it are complete (their
+// values have been consumed by the instructions before the __syncwarp).
+__device__ __forceinline__ void release_slot(uint32_t empty, int lane) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty);
+}
 
 // Writes the block's results: lane (g, t4) element 0 is row g / x row 2t4, 1 row g / x row 2t4+1,
 // 2 and 3 the same for row g+8 (rows relative to the block's first row `n0`).
 __device__ __forceinline__ bool block_finish(const Problem &pr, int M, int n0, int ra, int rc, int rows, int lane,
-                                             const BlockAcc &s) {
+                                             const BlockAcc &s, float ba, float bc) {
     const int t4 = lane & 3;
     bool bad = false;
 #pragma unroll
@@ -423,25 +450,32 @@ __device__ __forceinline__ bool block_finish(const Problem &pr, int M, int n0, i
         const int r = (i < 2 ? ra : rc), xr = 2 * t4 + (i & 1);
         if (r >= rows || xr >= M) continue;
         const float total = pr.fold ? s.run[i] : (s.acc[0][i] + s.acc[1][i]) + (s.acc[2][i] + s.acc[3][i]);
-        bad |= store_out(pr, xr, n0 + r, total);
+        bad |= store_out(pr, xr, n0 + r, total, i < 2 ? ba : bc);
     }
     return bad;
 }
 
-// A whole-row unit: rows [0, rows) staged at `stage` (pitch ldw), all of K, in 16-row blocks.
+// A whole-row unit: rows [0, rows) staged at `stage` (pitch ldw), all of K, in 16-row blocks. The
+// slot is handed back (`empty`) once the last block's sums are in registers, before its outputs are
+// finished and stored; the bias values are loaded before the sums.
 __device__ __forceinline__ bool process_unit(const Problem &pr, int M, const __half *stage, const __half *xtab,
-                                             int row0, int rows, int lane) {
+                                             int row0, int rows, int lane, uint32_t empty) {
     const int g = lane >> 2;
     const int K8 = (pr.K + 7) & ~7;
-    const __half *xrow = g < M ? xtab + pr.x_off + (size_t)g * K8 : nullptr;
+    // x rows past M read row M - 1 (their outputs are not stored)
+    const __half *xrow = xtab + pr.x_off + (size_t)min(g, M - 1) * K8;
+    const bool fin = pr.out_mode == OUT_FINAL;
     bool bad = false;
     for (int rb = 0; rb < rows; rb += 16) {
         const int ra = rb + g, rc = rb + g + 8;
+        const float ba = bias_at(pr, row0 + ra, fin && ra < rows), bc = bias_at(pr, row0 + rc, fin && rc < rows);
         BlockAcc s;
         block_reset(s);
-        block_accumulate(stage + (size_t)ra * pr.ldw, stage + (size_t)rc * pr.ldw, ra < rows, rc < rows, xrow, K8,
-                         pr.fold != 0, lane, s);
-        bad |= block_finish(pr, M, row0, ra, rc, rows, lane, s);
+        // rows past the unit read its first row (their outputs are not stored)
+        block_accumulate(stage + (size_t)(ra < rows ? ra : 0) * pr.ldw, stage + (size_t)(rc < rows ? rc : 0) * pr.ldw,
+                         xrow, K8, pr.fold != 0, lane, s);
+        if (rb + 16 >= rows) release_slot(empty, lane);
+        bad |= block_finish(pr, M, row0, ra, rc, rows, lane, s, ba, bc);
     }
     return bad;
 }
@@ -726,9 +760,7 @@ __global__ void __launch_bounds__(SCfg<SL, HF>::THREADS, SCfg<SL, HF>::MIN_BLOCK
             if (lane == 0) mbar_arrive(empty);   // the slot refills while the sums are handed on
             bad |= deliver_slice(g, pr, g.M, ctl, rg, mt.row0, mt.rows, mt.slice, lane, ts, abort_flag);
         } else {
-            bad |= process_unit(pr, g.M, stage, xtab, mt.row0, mt.rows, lane);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(empty);
+            bad |= process_unit(pr, g.M, stage, xtab, mt.row0, mt.rows, lane, empty);
         }
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) raise_flag(g.flags, FLAG_NONFINITE_OUTPUT);
