@@ -193,7 +193,7 @@ struct SCfg {
     static constexpr uint32_t BUF_OFFSET = (PROB_OFFSET + PROBS * (uint32_t)sizeof(Problem) + 15u) & ~15u;
     static constexpr uint32_t CTL_OFFSET = BUF_OFFSET + (SL ? B_RING * BUF_FLOATS * 4u : 0u);
     // sliced launches also reserve the room to align the ring to 1024 bytes (swizzle atom)
-    static constexpr uint32_t SMEM_BYTES = CTL_OFFSET + (SL ? 2u * B_RING * 4u + 1024u : 0u);
+    static constexpr uint32_t SMEM_BYTES = CTL_OFFSET + (SL ? 2u * B_RING * 4u + 16u + 1024u : 0u);
 };
 static_assert(SCfg<false>::SMEM_BYTES <= 232448 && SCfg<true>::SMEM_BYTES <= 232448, "shared memory");
 // two half-SM CTAs (each with the 1 KB the hardware reserves per CTA) in the SM's 228 KB
@@ -218,6 +218,14 @@ __device__ __forceinline__ void tma_box(uint32_t dst, const CUtensorMap *map, ui
                  : "memory");
 }
 
+// One 3-D box (64 K x 16 rows x 8 K chunks of 64) into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_box3(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
 // Non-blocking test of an mbarrier phase (the producer polls all its slots without suspending).
 __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
@@ -240,6 +248,22 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
     return v;
 }
 
+// CTA-scope acquire load, release store and acquire-release add on shared-memory words (the
+// ordering of the tile-sum buffers among the consumer warps of one CTA).
+__device__ __forceinline__ int ld_acquire_cta(volatile int *p) {
+    int v;
+    asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_u32(const_cast<int *>(p))) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_cta(volatile int *p, int v) {
+    asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(const_cast<int *>(p))), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned atom_add_acq_rel_cta(unsigned *p) {
+    unsigned old;
+    asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;" : "=r"(old) : "r"(smem_u32(p)) : "memory");
+    return old;
+}
+
 // D += A * B, m16n8k16, FP16 inputs, FP32 accumulation.
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -259,6 +283,80 @@ struct Range {
 };
 __device__ __forceinline__ Range cta_range(int units) {
     return Range{(long long)blockIdx.x * units / gridDim.x, (long long)(blockIdx.x + 1) * units / gridDim.x};
+}
+
+// The producer warp of a sliced launch (one long-K problem): lane s < STAGES feeds ring slot s with
+// the units rg.first + s, + STAGES, ... of the CTA's range, then an end marker. The problem's fields
+// stay in registers and each lane steps its (block, slice) position without a division, and the
+// next position is computed as soon as a copy is issued, so a freed slot costs the lane the meta
+// store, the expect-tx and the copy: one 3-D box of 8 x (64 K x 16 rows) when map3, else eight
+// 2-D boxes. Polling, abort and the bounded wait are those of produce().
+template <bool HF>
+__device__ __forceinline__ void produce_sliced(const Group &g, const Problem *prob, uint8_t *smem, Meta *meta,
+                                               uint32_t full0, uint32_t empty0, volatile int *abort_flag, int lane) {
+    using C = SCfg<true, HF>;
+    const bool mine = lane < C::STAGES;
+    const int slot = mine ? lane : 0;
+    const uint32_t full = full0 + 8 * slot, empty = empty0 + 8 * slot;
+    const uint32_t dst = smem_u32(smem + (size_t)slot * C::STAGE_BYTES);
+    const Range rg = cta_range(g.units);
+    const int S = prob[0].slices, N = prob[0].N, kslice = prob[0].kslice, K8 = (prob[0].K + 7) & ~7;
+    const bool map3 = g.map3 != 0;
+    long long u = rg.first + slot;
+    const int uq = (int)(u - prob[0].unit_begin);
+    int blk = uq / S, sl = uq - blk * S;
+    uint32_t ph = 0;
+    bool done = !mine, armed = false;
+    uint64_t t0 = 0;
+    for (uint32_t polls = 1;; ++polls) {
+        if (!done && mbar_test_wait(empty, ph ^ 1u)) {
+            if (u < rg.end) {
+                const int row0 = blk * 16, k0 = sl * kslice;
+                meta[slot] = Meta{0, row0, min(16, N - row0), sl};
+                if (map3) {
+                    // chunks past K arrive as zeros; the box's bytes are always counted in full
+                    mbar_arrive_expect_tx(full, (uint32_t)C::STAGE_BYTES);
+                    tma_box3(dst, &g.wmap, full, 0, row0, k0 / SWZ_BOX_K);
+                } else {
+                    // box b: rows [row0, row0 + 16) x K [k0 + 64b, k0 + 64b + 64); rows past N and
+                    // columns past K arrive as zeros
+                    const int boxes = min(kslice / SWZ_BOX_K, (K8 - k0 + SWZ_BOX_K - 1) / SWZ_BOX_K);
+                    mbar_arrive_expect_tx(full, (uint32_t)boxes * 16u * SWZ_BOX_K * 2u);
+                    for (int b = 0; b < boxes; ++b)
+                        tma_box(dst + (uint32_t)b * 16u * SWZ_BOX_K * 2u, &g.wmap, full, k0 + SWZ_BOX_K * b, row0);
+                }
+                armed = true;
+                ph ^= 1u;
+                u += C::STAGES;
+                sl += C::STAGES;
+                while (sl >= S) {
+                    sl -= S;
+                    ++blk;
+                }
+            } else {
+                meta[slot] = Meta{-1, 0, 0, 0};
+                mbar_arrive(full);
+                done = true;
+            }
+            t0 = 0;
+        }
+        if (__all_sync(0xffffffffu, done)) return;
+        if ((polls & 255u) == 0) {   // the abort flag and the clock, every 256 polls
+            bool stop = *abort_flag != 0;
+            if (!stop && !done) {
+                const uint64_t t = global_ns();
+                if (!t0) {
+                    t0 = t;
+                } else if (t - t0 > WAIT_LIMIT_NS) {
+                    *abort_flag = 1;
+                    raise_flag(g.flags, FLAG_TIMEOUT);
+                    stop = true;
+                }
+            }
+            if (__any_sync(0xffffffffu, stop)) break;
+        }
+    }
+    if (armed) drain_phase(full, ph ^ 1u);   // the last copy this lane issued
 }
 
 // The producer warp: lane s < STAGES feeds ring slot s with this CTA's local units q = s, s + STAGES,
@@ -428,9 +526,6 @@ __device__ __forceinline__ bool store_out(const Problem &pr, int xr, int n, floa
     pr.y[(size_t)xr * pr.ldy + n] = h;
     return half_nonfinite(h);
 }
-__device__ __forceinline__ bool store_out(const Problem &pr, int xr, int n, float total) {
-    return store_out(pr, xr, n, total, bias_at(pr, n, pr.out_mode == OUT_FINAL));
-}
 
 // Hands the warp's ring slot back to the producer: every lane's reads of it are complete (their
 // values have been consumed by the instructions before the __syncwarp).
@@ -484,8 +579,8 @@ __device__ __forceinline__ bool process_unit(const Problem &pr, int M, const __h
 // 64 x 16 boxes with the 128-byte swizzle (16-byte chunk c of box row r sits at chunk c ^ (r & 7),
 // so the eight rows a warp reads at once fall on different banks). Same products and summation
 // order as block_accumulate: ts[tt][i] is tile 2sl + tt of lane element i.
-__device__ __forceinline__ void slice_sums(const __half *stage, const __half *xrow, bool va, bool vc, int sl, int K8,
-                                           int lane, float (&ts)[TILES_PER_SLICE][4]) {
+__device__ __forceinline__ void slice_sums(const __half *stage, const __half *xrow, int sl, int K8, int lane,
+                                           float (&ts)[TILES_PER_SLICE][4]) {
     const int g = lane >> 2, t4 = lane & 3;
     const uint4 z = make_uint4(0, 0, 0, 0);
     const int ca = (t4 ^ g) * 8, cb = ((t4 ^ g) ^ 4) * 8;   // swizzled chunk offsets (halves) of k0, k1
@@ -500,13 +595,15 @@ __device__ __forceinline__ void slice_sums(const __half *stage, const __half *xr
             if (kw >= K8) break;   // past the end of K (uniform): the tile ends here
             const __half *bx = stage + box * 16 * SWZ_BOX_K;
             const int k0 = kw + t4 * 8, k1 = k0 + 32;
-            const bool l0 = k0 < K8, l1 = k1 < K8;
-            const uint4 a0 = (va && l0) ? *reinterpret_cast<const uint4 *>(bx + g * SWZ_BOX_K + ca) : z;
-            const uint4 a1 = (va && l1) ? *reinterpret_cast<const uint4 *>(bx + g * SWZ_BOX_K + cb) : z;
-            const uint4 b0 = (vc && l0) ? *reinterpret_cast<const uint4 *>(bx + (g + 8) * SWZ_BOX_K + ca) : z;
-            const uint4 b1 = (vc && l1) ? *reinterpret_cast<const uint4 *>(bx + (g + 8) * SWZ_BOX_K + cb) : z;
-            const uint4 x0 = (xrow && l0) ? *reinterpret_cast<const uint4 *>(xrow + k0) : z;
-            const uint4 x1 = (xrow && l1) ? *reinterpret_cast<const uint4 *>(xrow + k1) : z;
+            // W: rows past N and columns past K of a loaded box arrive as zeros
+            const uint4 a0 = *reinterpret_cast<const uint4 *>(bx + g * SWZ_BOX_K + ca);
+            const uint4 a1 = *reinterpret_cast<const uint4 *>(bx + g * SWZ_BOX_K + cb);
+            const uint4 b0 = *reinterpret_cast<const uint4 *>(bx + (g + 8) * SWZ_BOX_K + ca);
+            const uint4 b1 = *reinterpret_cast<const uint4 *>(bx + (g + 8) * SWZ_BOX_K + cb);
+            // x: only the box that crosses K8 has chunks past the x row
+            const bool full = kw + SWZ_BOX_K <= K8;
+            const uint4 x0 = (full || k0 < K8) ? *reinterpret_cast<const uint4 *>(xrow + k0) : z;
+            const uint4 x1 = (full || k1 < K8) ? *reinterpret_cast<const uint4 *>(xrow + k1) : z;
             mma16816(acc[0], a0.x, b0.x, a0.y, b0.y, x0.x, x0.y);
             mma16816(acc[1], a0.z, b0.z, a0.w, b0.w, x0.z, x0.w);
             mma16816(acc[2], a1.x, b1.x, a1.y, b1.y, x1.x, x1.y);
@@ -519,9 +616,10 @@ __device__ __forceinline__ void slice_sums(const __half *stage, const __half *xr
 
 // Shared-memory state of a sliced launch's tile-sum buffers.
 struct SliceCtl {
-    float *buf;              // B_RING x BUF_FLOATS: [row (16)][x row (M)][tile (T)]
+    float *buf;              // B_RING x BUF_FLOATS: [tile (T)][row (16)][x row (M)]
     unsigned *count;         // [B_RING] slices of the buffer's block that have arrived
     volatile int *open;      // [B_RING] local block index the buffer is open to
+    unsigned *lead;          // slices handed on so far of the block owned by the previous CTA
 };
 
 // Bounded spin of lane 0 until the buffer is open to local block lb (its previous block was folded).
@@ -573,18 +671,20 @@ __device__ __forceinline__ bool wait_remote(const unsigned *cnt, unsigned expect
 }
 
 // Hands one slice's tile sums on and finishes the block when they complete it. The owner of a
-// block is the CTA whose range holds the block's slice 0. It meets every other slice of the block
-// in its own range, except for the block at the end of its range, whose remaining slices open the
+// block is the CTA whose range holds the block's slice 0. It meets every other slice of the block in
+// its own range, except for the block at the end of its range, whose remaining slices open the
 // ranges of the following CTAs (processed first there, so they are in by the time the owner needs
 // them).
-//   Owner: the sums go to the block's shared buffer. The warp that brings the block's last local
-//   slice folds the tile sums in K order -- the fp16 fold of the tile-16 arithmetic, or their FP32
-//   sum -- after a bounded wait for the other CTAs' slices, writes Y and reopens the buffer.
-//   Other CTAs: the sums go to the block's rows of the device scratch, and one release reduction
-//   counts the slice on the block's counter (nothing waits for it). The owner resets the counter.
-// The bits are those of folding the same tile sums in one place.
+//   Owner: the sums go to the block's shared buffer (tile-major, so the folding lanes read
+//   consecutive words). The warp that brings the block's last local slice folds the tile sums in K
+//   order -- the fp16 fold of the tile-16 arithmetic, or their FP32 sum -- after a bounded wait for
+//   the other CTAs' slices, writes Y and reopens the buffer.
+//   Other CTAs: the sums go to the block's rows of the device scratch, counted as described below.
+//   The owner resets the block counter.
+// The bits are those of folding the same tile sums in one place. `fb` is the first block this CTA
+// owns (the first whose slice 0 lies in its range).
 __device__ __forceinline__ bool deliver_slice(const Group &grp, const Problem &pr, int M, const SliceCtl &ctl,
-                                              const Range &rg, int row0, int rows, int sl, int lane,
+                                              const Range &rg, int fb, int row0, int rows, int sl, int lane,
                                               const float (&ts)[TILES_PER_SLICE][4], volatile int *abort_flag) {
     const int g = lane >> 2, t4 = lane & 3;
     const int K8 = (pr.K + 7) & ~7, T = (K8 + 255) >> 8, S = pr.slices;
@@ -603,19 +703,25 @@ __device__ __forceinline__ bool deliver_slice(const Group &grp, const Problem &p
                 if (r < rows && xr < M) tg[((size_t)r * M + xr) * T + sl * TILES_PER_SLICE + tt] = ts[tt][i];
             }
         }
-        __syncwarp();   // the warp's sums are ordered before lane 0's release
-        if (lane == 0) red_release_add(cnt, 1u);
+        // The CTA's slices of this block are the first units of its range: each counts itself in
+        // shared memory (acquire-release), and the one that completes them publishes them all with one
+        // GPU-scope release (cumulative over the sums the count has ordered before it).
+        __syncwarp();   // the warp's sums are ordered before lane 0's count
+        if (lane == 0) {
+            const unsigned lead = (unsigned)(min(rg.end, b0 + S) - rg.first);
+            if (atom_add_acq_rel_cta(ctl.lead) == lead - 1u) red_release_add(cnt, lead);
+        }
         return false;
     }
-    const int lb = blk - (int)((rg.first + S - 1) / S);   // local index among the blocks this CTA owns
-    const int bb = lb % B_RING;
+    const int lb = blk - fb;   // local index among the blocks this CTA owns
+    const int bb = lb & (B_RING - 1);
     float *buf = ctl.buf + bb * BUF_FLOATS;
     bool ok = true;
-    if (lane == 0) {
+    if (lane == 0 && ld_acquire_cta(ctl.open + bb) != lb) {   // acquire: the buffer's previous reads are done
         ok = wait_open(ctl, bb, lb, abort_flag, grp.flags);
         __threadfence_block();
     }
-    __syncwarp();   // the buffer's previous reads are ordered before this warp's writes
+    __syncwarp();   // ... and ordered before this warp's writes
     if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
 #pragma unroll
     for (int tt = 0; tt < TILES_PER_SLICE; ++tt) {
@@ -623,40 +729,46 @@ __device__ __forceinline__ bool deliver_slice(const Group &grp, const Problem &p
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int r = i < 2 ? g : g + 8, xr = 2 * t4 + (i & 1);
-            if (r < rows && xr < M) buf[(r * M + xr) * T + sl * TILES_PER_SLICE + tt] = ts[tt][i];
+            if (r < rows && xr < M) buf[(sl * TILES_PER_SLICE + tt) * 16 * M + r * M + xr] = ts[tt][i];
         }
     }
     const long long lend = min(rg.end, b0 + S);   // local slices of the block: [b0, lend)
     const unsigned local = (unsigned)(lend - b0), remote = (unsigned)S - local;
     __syncwarp();
     int last = 0;
-    if (lane == 0) {
-        __threadfence_block();
-        last = atomicAdd(&ctl.count[bb], 1u) == local - 1u;
-        __threadfence_block();
-    }
-    __syncwarp();   // the other warps' sums are ordered before this warp's reads
+    // release: this warp's sums before the count; acquire: the other warps' sums before the fold
+    if (lane == 0) last = atom_add_acq_rel_cta(ctl.count + bb) == local - 1u;
+    __syncwarp();
     if (!__shfl_sync(0xffffffffu, last, 0)) return false;
     if (remote && !wait_remote(cnt, remote, abort_flag, grp.flags)) return false;
     const int ltiles = (int)local * TILES_PER_SLICE;   // tiles [0, ltiles) are in the buffer
     bool bad = false;
     for (int o = lane; o < rows * M; o += 32) {
         const int r = o / M, xr = o - r * M;
-        const float *pl = buf + (r * M + xr) * T;
+        const float *pl = buf + r * M + xr;   // tile t at pl[16 M t]
         const float *pg = tg + ((size_t)r * M + xr) * T;
+        const float b = bias_at(pr, row0 + r, pr.out_mode == OUT_FINAL);
         float total = 0.0f;
-        for (int t = 0; t < T; ++t) {
-            const float v = t < ltiles ? pl[t] : __ldcg(pg + t);
-            total = pr.fold ? fold16(total, v, t == 0) : (t == 0 ? v : total + v);
+        for (int t0 = 0; t0 < T; t0 += 8) {   // eight tile sums loaded ahead of their fold
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int t = t0 + j;
+                v[j] = t >= T ? 0.0f : t < ltiles ? pl[t * 16 * M] : __ldcg(pg + t);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int t = t0 + j;
+                if (t < T) total = pr.fold ? fold16(total, v[j], t == 0) : (t == 0 ? v[j] : total + v[j]);
+            }
         }
-        bad |= store_out(pr, xr, row0 + r, total);
+        bad |= store_out(pr, xr, row0 + r, total, b);
     }
     __syncwarp();
     if (lane == 0) {
         if (remote) *cnt = 0u;   // every other slice of this launch has arrived
         ctl.count[bb] = 0u;
-        __threadfence_block();
-        ctl.open[bb] = lb + B_RING;
+        st_release_cta(ctl.open + bb, lb + B_RING);   // after the count reset and the warp's reads
     }
     return bad;
 }
@@ -676,7 +788,8 @@ __global__ void __launch_bounds__(SCfg<SL, HF>::THREADS, SCfg<SL, HF>::MIN_BLOCK
     Problem *prob = reinterpret_cast<Problem *>(smem + C::PROB_OFFSET);
     __half *xtab = reinterpret_cast<__half *>(smem + C::X_OFFSET);
     SliceCtl ctl{reinterpret_cast<float *>(smem + C::BUF_OFFSET), reinterpret_cast<unsigned *>(smem + C::CTL_OFFSET),
-                 reinterpret_cast<volatile int *>(smem + C::CTL_OFFSET + 4 * B_RING)};
+                 reinterpret_cast<volatile int *>(smem + C::CTL_OFFSET + 4 * B_RING),
+                 reinterpret_cast<unsigned *>(smem + C::CTL_OFFSET + 8 * B_RING)};
     const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * C::STAGES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // Programmatic dependent launch (when the launch allows it): the next kernel on the stream may
@@ -703,13 +816,15 @@ __global__ void __launch_bounds__(SCfg<SL, HF>::THREADS, SCfg<SL, HF>::MIN_BLOCK
             ctl.count[lane] = 0u;
             ctl.open[lane] = lane;
         }
+        if (SL && lane == 0) *ctl.lead = 0u;
         const int words = g.count * (int)(sizeof(Problem) / 8);
         const unsigned long long *src = reinterpret_cast<const unsigned long long *>(g.prob);
         unsigned long long *dst = reinterpret_cast<unsigned long long *>(prob);
         for (int i = lane; i < words; i += 32) dst[i] = src[i];
         __syncwarp();
         asm volatile("bar.arrive 2, %0;" ::"r"(C::THREADS) : "memory");
-        produce<SL, HF>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
+        if constexpr (SL) produce_sliced<HF>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
+        else produce<SL, HF>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
         return;
     }
     asm volatile("bar.sync 2, %0;" ::"r"(C::THREADS) : "memory");   // barriers and problem table ready
@@ -744,6 +859,7 @@ __global__ void __launch_bounds__(SCfg<SL, HF>::THREADS, SCfg<SL, HF>::MIN_BLOCK
     const uint32_t full = full0 + 8 * c, empty = empty0 + 8 * c;
     const __half *stage = reinterpret_cast<const __half *>(smem + (size_t)c * C::STAGE_BYTES);
     const Range rg = cta_range(g.units);
+    const int fb = SL ? (int)((rg.first + prob[0].slices - 1) / prob[0].slices) : 0;
     bool bad = false;
     for (uint32_t ph = 0;; ph ^= 1u) {
         // Every lane waits (each gets the barrier's acquire); the warp leaves together.
@@ -753,12 +869,13 @@ __global__ void __launch_bounds__(SCfg<SL, HF>::THREADS, SCfg<SL, HF>::MIN_BLOCK
         const Problem &pr = prob[mt.prob];
         if (SL) {
             const int gq = lane >> 2, K8 = (pr.K + 7) & ~7;
-            const __half *xrow = gq < g.M ? xtab + pr.x_off + (size_t)gq * K8 : nullptr;
+            // x rows past M read row M - 1 (their outputs are not kept)
+            const __half *xrow = xtab + pr.x_off + (size_t)min(gq, g.M - 1) * K8;
             float ts[TILES_PER_SLICE][4];
-            slice_sums(stage, xrow, gq < mt.rows, gq + 8 < mt.rows, mt.slice, K8, lane, ts);
+            slice_sums(stage, xrow, mt.slice, K8, lane, ts);
             __syncwarp();
             if (lane == 0) mbar_arrive(empty);   // the slot refills while the sums are handed on
-            bad |= deliver_slice(g, pr, g.M, ctl, rg, mt.row0, mt.rows, mt.slice, lane, ts, abort_flag);
+            bad |= deliver_slice(g, pr, g.M, ctl, rg, fb, mt.row0, mt.rows, mt.slice, lane, ts, abort_flag);
         } else {
             bad |= process_unit(pr, g.M, stage, xtab, mt.row0, mt.rows, lane, empty);
         }
@@ -882,6 +999,23 @@ static bool make_wmap(CUtensorMap *map, const __half *w, int K, int N, long long
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// W [N, ldw] with K a multiple of 64, as one 3-D box per unit: dimension 0 is 64 K elements,
+// dimension 1 the rows (stride ldw), dimension 2 the K chunks of 64 (stride 128 bytes), box 64 x 16 x 8
+// with the 128-byte swizzle. Shared memory receives the eight 64 x 16 boxes of make_wmap back to back.
+// Every element read lies inside its row ([0, K)), so the map reads nothing past W; chunks past K
+// arrive as zeros.
+static bool make_wmap3(CUtensorMap *map, const __half *w, int K, int N, long long ldw) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc || K % SWZ_BOX_K) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)SWZ_BOX_K, (cuuint64_t)N, (cuuint64_t)(K / SWZ_BOX_K)};
+    cuuint64_t strides[2] = {(cuuint64_t)ldw * 2, (cuuint64_t)SWZ_BOX_K * 2};
+    cuuint32_t box[3] = {(cuuint32_t)SWZ_BOX_K, 16, (cuuint32_t)(STREAM_SLICE / SWZ_BOX_K)};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half *>(w), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 cudaError_t prepare() {
     for (int m = 1; m <= MAX_M; m *= 2) direct_blocks(m);
     if (!encode_fn()) return cudaErrorNotSupported;
@@ -988,8 +1122,11 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
         const int next = pack_group(all, first, g);
         if (next == first) return cudaErrorInvalidValue;   // one problem always fits the table
         plan_units(g, sm_count);
-        if (g.prob[0].kslice && !make_wmap(&g.wmap, g.prob[0].w, g.prob[0].K, g.prob[0].N, g.prob[0].ldw))
-            return cudaErrorInvalidValue;
+        if (g.prob[0].kslice) {
+            const Problem &p0 = g.prob[0];
+            g.map3 = make_wmap3(&g.wmap, p0.w, p0.K, p0.N, p0.ldw) ? 1 : 0;
+            if (!g.map3 && !make_wmap(&g.wmap, p0.w, p0.K, p0.N, p0.ldw)) return cudaErrorInvalidValue;
+        }
         const bool sl = g.prob[0].kslice != 0;   // a sliced problem is alone in its launch
         int xused = 0;                           // FP16 elements of the x table this launch fills
         for (int e = 0; e < g.nx; ++e) {

@@ -69,10 +69,11 @@ struct XSource {
 };
 
 struct Group {
-    CUtensorMap wmap;                   // W of a sliced problem (alone in its launch): 256 x 16 boxes
+    CUtensorMap wmap;                   // W of a sliced problem (alone in its launch), see map3
     Problem prob[GROUP_MAX];
     XSource xsrc[GROUP_MAX];
     int count, M, units, nx;
+    int map3;                           // wmap is 3-D (one copy per 16-row x 512-K unit), else 2-D 64 x 16 boxes
     unsigned *flags;
     Scratch scratch;
 };
