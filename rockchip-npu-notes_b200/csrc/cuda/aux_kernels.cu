@@ -106,19 +106,34 @@ cudaError_t cube_scatter(const void *src, size_t ld, const CubeTiles &t, cudaStr
 }
 
 // ----------------------------------------------------------------------------- guard check
+// Buffer blockIdx.x, its slack + guard split over gridDim.y blocks: 16-byte loads when the region
+// starts on a 16-byte boundary and both lengths are multiples of 16 (every buffer of this library),
+// else byte loads.
+constexpr unsigned GUARD_SPLIT = 8;
 __global__ void __launch_bounds__(THREADS) guard_kernel(GuardList g, size_t slack, size_t guard, unsigned *flags) {
     const unsigned char *base = static_cast<const unsigned char *>(g.base[blockIdx.x]) + g.payload[blockIdx.x];
+    const size_t total = slack + guard, stride = (size_t)gridDim.y * THREADS;
     bool bad = false;
-    for (size_t i = threadIdx.x; i < slack + guard; i += THREADS) {
-        const unsigned char want = i < slack ? 0x00 : 0xa5;
-        if (base[i] != want) bad = true;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) == 0 && (slack & 15) == 0 && (guard & 15) == 0) {
+        const uint4 *v = reinterpret_cast<const uint4 *>(base);
+        const size_t nv = total >> 4, ns = slack >> 4;
+        for (size_t i = (size_t)blockIdx.y * THREADS + threadIdx.x; i < nv; i += stride) {
+            const uint4 w = __ldcg(v + i);
+            const unsigned want = i < ns ? 0u : 0xa5a5a5a5u;
+            bad |= ((w.x ^ want) | (w.y ^ want) | (w.z ^ want) | (w.w ^ want)) != 0u;
+        }
+    } else {
+        for (size_t i = (size_t)blockIdx.y * THREADS + threadIdx.x; i < total; i += stride) {
+            const unsigned char want = i < slack ? 0x00 : 0xa5;
+            if (base[i] != want) bad = true;
+        }
     }
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) raise_flag(flags, FLAG_GUARD);
 }
 
 cudaError_t guard_check(const GuardList &g, size_t slack, size_t guard, unsigned *flags, cudaStream_t s) {
     if (!g.count) return cudaSuccess;
-    guard_kernel<<<g.count, THREADS, 0, s>>>(g, slack, guard, flags);
+    guard_kernel<<<dim3(g.count, GUARD_SPLIT), THREADS, 0, s>>>(g, slack, guard, flags);
     return cudaGetLastError();
 }
 

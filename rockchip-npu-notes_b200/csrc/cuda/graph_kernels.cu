@@ -118,6 +118,17 @@ cudaError_t elementwise(const EwParams &p, cudaStream_t s, int sm_count) {
 // Thread (row r, hidden columns [j, j+8)): gate sums at packed columns 64*(j/32) + j%32 + e, up sums
 // 32 columns further; each is finished with its own bias like the Linear epilogue (fp16(run + b)
 // when the half has a bias), then y = fp16(fp16(g * fp16(gate(g))) * u).
+// The biases of columns [j, j + 8) as FP32 (zero past n or without a bias): one 16-byte load when
+// the 8 columns are inside n and 16-byte aligned, else element loads.
+__device__ __forceinline__ void bias8(const __half *b, int j, int n, float (&out)[8]) {
+    if (b && j + 8 <= n && (reinterpret_cast<uintptr_t>(b + j) & 15) == 0) {
+        unpack8(__ldg(reinterpret_cast<const uint4 *>(b + j)), out);
+        return;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) out[e] = (b && j + e < n) ? __half2float(b[j + e]) : 0.0f;
+}
+
 __global__ void __launch_bounds__(THREADS) gated_kernel(GatedParams p) {
     const int groups = (p.gate_n + 7) / 8;
     const long long total = (long long)p.rows * groups;
@@ -125,14 +136,15 @@ __global__ void __launch_bounds__(THREADS) gated_kernel(GatedParams p) {
     for (long long i = (long long)blockIdx.x * THREADS + threadIdx.x; i < total; i += (long long)gridDim.x * THREADS) {
         const int r = (int)(i / groups), j = (int)(i % groups) * 8;
         const __half *row = p.src + (size_t)r * p.lds + 64 * (j >> 5) + (j & 31);
-        float g[8], u[8], y[8];
+        float g[8], u[8], y[8], bgv[8], buv[8];
         unpack8(__ldg(reinterpret_cast<const uint4 *>(row)), g);
         unpack8(__ldg(reinterpret_cast<const uint4 *>(row + 32)), u);
+        bias8(p.bias_gate, j, p.gate_n, bgv);
+        bias8(p.bias_up, j, p.gate_n, buv);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             const bool in = j + e < p.gate_n;
-            const float bg = (p.bias_gate && in) ? __half2float(p.bias_gate[j + e]) : 0.0f;
-            const float bu = (p.bias_up && in) ? __half2float(p.bias_up[j + e]) : 0.0f;
+            const float bg = bgv[e], bu = buv[e];
             const float gv = finish_tile16(g[e], bg, p.bias_gate != nullptr, false);
             const float uv = finish_tile16(u[e], bu, p.bias_up != nullptr, false);
             y[e] = gated16(p.gate_table, gv, uv, p.act);
