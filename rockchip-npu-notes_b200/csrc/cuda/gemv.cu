@@ -77,7 +77,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 template <int MR>
 __device__ __forceinline__ bool finish_row(int M, int lane, int n, int out_mode, int fold, int post,
                                            const __half *bias, __half *y, long long ldy, float *partial,
-                                           long long ldp, const float (&acc)[MR], const float (&run)[MR]) {
+                                           long long ldp, const __half *res, long long ldr,
+                                           const float (&acc)[MR], const float (&run)[MR]) {
     const bool has_bias = bias != nullptr;
     const float b = has_bias ? __half2float(bias[n]) : 0.0f;
     bool bad = false;
@@ -92,7 +93,8 @@ __device__ __forceinline__ bool finish_row(int M, int lane, int n, int out_mode,
             y[(size_t)r * ldy + n] = __float2half_rn(total);
         } else {
             const float v = fold ? finish_tile16(total, b, has_bias, post) : finish_fp32(total, b, post);
-            const __half h = __float2half_rn(v);
+            __half h = __float2half_rn(v);
+            if (res) h = __float2half_rn(__fadd_rn(__half2float(h), __half2float(res[(size_t)r * ldr + n])));
             bad |= half_nonfinite(h);
             y[(size_t)r * ldy + n] = h;
         }
@@ -149,8 +151,8 @@ __global__ void __launch_bounds__(D_THREADS) gemv_direct_kernel(const Params p) 
                 }
             }
         }
-        bad |= finish_row<MR>(p.M, lane, n, p.out_mode, p.fold, p.post, p.bias, p.y, p.ldy, p.partial, p.ldp, acc,
-                              run);
+        bad |= finish_row<MR>(p.M, lane, n, p.out_mode, p.fold, p.post, p.bias, p.y, p.ldy, p.partial, p.ldp,
+                              p.out_mode == OUT_FINAL ? p.res : nullptr, p.ldr, acc, run);
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) raise_flag(p.flags, FLAG_NONFINITE_OUTPUT);
 }
@@ -507,11 +509,16 @@ __device__ __forceinline__ void block_accumulate(const __half *wa, const __half 
 
 // Writes one output: raw FP32 / raw FP16 / bias + activation. Returns true if a final FP16 output is
 // not finite.
-// `b` is bias[n] (0 without a bias), loaded by the caller ahead of the sums.
+// `b` is bias[n] (0 without a bias) and `rs` the residual res[xr, n] (with a residual), both loaded
+// by the caller ahead of the sums. The residual is added to the rounded result and rounded once,
+// y = fp16(res + fp16(result)), as the graph's ADD node computes it.
 __device__ __forceinline__ float bias_at(const Problem &pr, int n, bool valid) {
     return (pr.bias && valid) ? __half2float(__ldg(pr.bias + n)) : 0.0f;
 }
-__device__ __forceinline__ bool store_out(const Problem &pr, int xr, int n, float total, float b) {
+__device__ __forceinline__ float res_at(const Problem &pr, int xr, int n, bool valid) {
+    return (pr.res && valid) ? __half2float(pr.res[(size_t)xr * pr.ldr + n]) : 0.0f;
+}
+__device__ __forceinline__ bool store_out(const Problem &pr, int xr, int n, float total, float b, float rs) {
     if (pr.out_mode == OUT_RAW32) {
         pr.partial[(size_t)xr * pr.ldp + n] = total;
         return false;
@@ -522,7 +529,8 @@ __device__ __forceinline__ bool store_out(const Problem &pr, int xr, int n, floa
     }
     const bool has_bias = pr.bias != nullptr;
     const float v = pr.fold ? finish_tile16(total, b, has_bias, pr.post) : finish_fp32(total, b, pr.post);
-    const __half h = __float2half_rn(v);
+    __half h = __float2half_rn(v);
+    if (pr.res) h = __float2half_rn(__fadd_rn(__half2float(h), rs));
     pr.y[(size_t)xr * pr.ldy + n] = h;
     return half_nonfinite(h);
 }
@@ -537,7 +545,7 @@ __device__ __forceinline__ void release_slot(uint32_t empty, int lane) {
 // Writes the block's results: lane (g, t4) element 0 is row g / x row 2t4, 1 row g / x row 2t4+1,
 // 2 and 3 the same for row g+8 (rows relative to the block's first row `n0`).
 __device__ __forceinline__ bool block_finish(const Problem &pr, int M, int n0, int ra, int rc, int rows, int lane,
-                                             const BlockAcc &s, float ba, float bc) {
+                                             const BlockAcc &s, float ba, float bc, const float (&rs)[4]) {
     const int t4 = lane & 3;
     bool bad = false;
 #pragma unroll
@@ -545,7 +553,7 @@ __device__ __forceinline__ bool block_finish(const Problem &pr, int M, int n0, i
         const int r = (i < 2 ? ra : rc), xr = 2 * t4 + (i & 1);
         if (r >= rows || xr >= M) continue;
         const float total = pr.fold ? s.run[i] : (s.acc[0][i] + s.acc[1][i]) + (s.acc[2][i] + s.acc[3][i]);
-        bad |= store_out(pr, xr, n0 + r, total, i < 2 ? ba : bc);
+        bad |= store_out(pr, xr, n0 + r, total, i < 2 ? ba : bc, rs[i]);
     }
     return bad;
 }
@@ -564,13 +572,19 @@ __device__ __forceinline__ bool process_unit(const Problem &pr, int M, const __h
     for (int rb = 0; rb < rows; rb += 16) {
         const int ra = rb + g, rc = rb + g + 8;
         const float ba = bias_at(pr, row0 + ra, fin && ra < rows), bc = bias_at(pr, row0 + rc, fin && rc < rows);
+        float rs[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = i < 2 ? ra : rc, xr = 2 * (lane & 3) + (i & 1);
+            rs[i] = res_at(pr, xr, row0 + r, fin && r < rows && xr < M);
+        }
         BlockAcc s;
         block_reset(s);
         // rows past the unit read its first row (their outputs are not stored)
         block_accumulate(stage + (size_t)(ra < rows ? ra : 0) * pr.ldw, stage + (size_t)(rc < rows ? rc : 0) * pr.ldw,
                          xrow, K8, pr.fold != 0, lane, s);
         if (rb + 16 >= rows) release_slot(empty, lane);
-        bad |= block_finish(pr, M, row0, ra, rc, rows, lane, s, ba, bc);
+        bad |= block_finish(pr, M, row0, ra, rc, rows, lane, s, ba, bc, rs);
     }
     return bad;
 }
@@ -748,6 +762,7 @@ __device__ __forceinline__ bool deliver_slice(const Group &grp, const Problem &p
         const float *pl = buf + r * M + xr;   // tile t at pl[16 M t]
         const float *pg = tg + ((size_t)r * M + xr) * T;
         const float b = bias_at(pr, row0 + r, pr.out_mode == OUT_FINAL);
+        const float rsd = res_at(pr, xr, row0 + r, pr.out_mode == OUT_FINAL);
         float total = 0.0f;
         for (int t0 = 0; t0 < T; t0 += 8) {   // eight tile sums loaded ahead of their fold
             float v[8];
@@ -762,7 +777,7 @@ __device__ __forceinline__ bool deliver_slice(const Group &grp, const Problem &p
                 if (t < T) total = pr.fold ? fold16(total, v[j], t == 0) : (t == 0 ? v[j] : total + v[j]);
             }
         }
-        bad |= store_out(pr, xr, row0 + r, total, b);
+        bad |= store_out(pr, xr, row0 + r, total, b, rsd);
     }
     __syncwarp();
     if (lane == 0) {
@@ -1192,7 +1207,8 @@ cudaError_t launch(const Params &p, cudaStream_t stream, int sm_count, unsigned 
             g.prob[0] = Problem{p.x + (size_t)r0 * p.ldx, p.ldx, p.w, p.ldw, p.bias,
                                 p.y ? p.y + (size_t)r0 * p.ldy : nullptr, p.ldy,
                                 p.partial ? p.partial + (size_t)r0 * p.ldp : nullptr, p.ldp,
-                                p.N, p.K, p.out_mode, p.post, p.fold, 0, 0, 0, 0, 0, 0};
+                                p.N, p.K, p.out_mode, p.post, p.fold, 0, 0, 0, 0, 0, 0,
+                                p.res ? p.res + (size_t)r0 * p.ldr : nullptr, p.ldr};
             const cudaError_t e = launch_group(g, stream, sm_count, grid_out, nullptr);
             if (e != cudaSuccess) return e;
         }
