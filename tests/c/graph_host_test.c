@@ -375,6 +375,43 @@ static void topology_case(void) {
     EXPECT(co_graph_plan_init(&desc, &p) == ROCKET_E_SHAPE);
 }
 
+/* A large input (4 MiB) is checked for finiteness by several host threads: an infinity at the start,
+ * at every 1 MiB boundary and at the end is refused with no launch and the output untouched, and the
+ * all-finite input runs. */
+static void large_input_case(void) {
+    enum { R = 1024, C = 2048 };
+    const size_t n = (size_t)R * C;
+    h16 *x = malloc(n * 2), *y = malloc(n * 2);
+    if (!x || !y) exit(1);
+    for (size_t i = 0; i < n; i++) x[i] = fillv((unsigned)i, 5);
+    co_graph_node nodes[2];
+    memset(nodes, 0, sizeof(nodes));
+    nodes[0] = (co_graph_node){.op = CO_GRAPH_INPUT, .rows = R, .cols = C};
+    nodes[1] = (co_graph_node){.op = CO_GRAPH_HSIG, .a = 0};
+    co_graph_desc desc = {nodes, 2, 1, 0};
+    co_graph *g = NULL;
+    EXPECT(!co_graph_compile(FD, &desc, CO_CHAIN, &g));
+    if (!g) exit(1);
+    co_graph_input in = {0, F(x)};
+    const size_t at[] = {0, (1u << 19) - 1, 1u << 19, 3u << 19, n - 1};
+    for (unsigned i = 0; i < sizeof(at) / sizeof(at[0]); i++) {
+        const h16 saved = x[at[i]];
+        x[at[i]] = (i & 1) ? 0xfc00u : 0x7e00u;   /* -inf, NaN */
+        memset(y, 0x23, n * 2);
+        uint64_t before = rocket_launch_count();
+        EXPECT(co_graph_run(g, &in, 1, (_Float16 *)y) == ROCKET_E_SHAPE && rocket_launch_count() == before);
+        EXPECT(untouched(y, n * 2));
+        x[at[i]] = saved;
+    }
+    EXPECT(!co_graph_run(g, &in, 1, (_Float16 *)y));
+    int ok = 1;
+    for (size_t i = 0; i < n; i++) ok &= y[i] == oracle_ew16(4, x[i], 0);   /* HardSigmoid */
+    EXPECT(ok);
+    co_graph_destroy(g);
+    free(x);
+    free(y);
+}
+
 int main(void) {
     FD = rocket_open();
     EXPECT(FD >= 0);
@@ -386,6 +423,7 @@ int main(void) {
     execution_case(40, 96, 72, 1, 1);     /* GELU, biases on both halves */
     rmsnorm_case(257, 513);
     multiple_outputs_case();
+    large_input_case();
     rocket_close(FD);
     EXPECT(b2h_live_bytes() == 0);
     printf("graph_host_test: %d checks, %d failures\n", checks, failures);
