@@ -26,10 +26,8 @@
 #include "co_graph.h"
 
 #include <math.h>
-#include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
-#include <unistd.h>
 
 #define MAXN CO_GRAPH_MAX_NODES
 
@@ -310,7 +308,7 @@ int co_graph_plan_init(const co_graph_desc *d, co_graph_plan *out) {
 
 /* 1 if no FP16 value of v[0, n) is infinite or NaN: four values per 64-bit word at a time (an
  * exponent field of all ones plus one carries into the lane's sign bit). */
-static int finite16_serial(const _Float16 *v, size_t n) {
+static int finite16(const _Float16 *v, size_t n) {
     const uint16_t *b = (const uint16_t *)v;
     size_t i = 0;
     if (((uintptr_t)b & 7u) == 0) {
@@ -323,50 +321,6 @@ static int finite16_serial(const _Float16 *v, size_t n) {
     for (; i < n; i++)
         if ((b[i] & 0x7c00u) == 0x7c00u) return 0;
     return 1;
-}
-
-struct finite_part {
-    const _Float16 *v;
-    size_t n;
-    int ok;
-};
-
-static void *finite_worker(void *arg) {
-    struct finite_part *p = (struct finite_part *)arg;
-    p->ok = finite16_serial(p->v, p->n);
-    return NULL;
-}
-
-/* finite16_serial over up to 16 host threads for large arrays: one thread reads host memory at a
- * few GB/s, which made the input check the largest part of a graph run at m = 4096 (32 MiB). A part
- * whose thread cannot be started is checked by the calling thread. */
-static int finite16(const _Float16 *v, size_t n) {
-    enum { MAX_PARTS = 16 };
-    const size_t min_part = (size_t)1 << 19;   /* 1 MiB of FP16 values per thread at least */
-    long cpus = sysconf(_SC_NPROCESSORS_ONLN);
-    size_t parts = n / min_part;
-    if (cpus > 0 && parts > (size_t)cpus) parts = (size_t)cpus;
-    if (parts > MAX_PARTS) parts = MAX_PARTS;
-    if (parts < 2) return finite16_serial(v, n);
-    struct finite_part part[MAX_PARTS];
-    pthread_t thread[MAX_PARTS];
-    int started[MAX_PARTS] = {0};
-    const size_t per = (n / parts + 3) & ~(size_t)3;   /* parts start on 8-byte boundaries */
-    for (size_t i = 0; i < parts; i++) {
-        size_t a = i * per < n ? i * per : n, b = i + 1 == parts ? n : ((i + 1) * per < n ? (i + 1) * per : n);
-        part[i].v = v + a;
-        part[i].n = b - a;
-        part[i].ok = 1;
-    }
-    for (size_t i = 1; i < parts; i++) started[i] = pthread_create(&thread[i], NULL, finite_worker, &part[i]) == 0;
-    part[0].ok = finite16_serial(part[0].v, part[0].n);
-    int ok = part[0].ok;
-    for (size_t i = 1; i < parts; i++) {
-        if (started[i]) pthread_join(thread[i], NULL);
-        else part[i].ok = finite16_serial(part[i].v, part[i].n);
-        ok &= part[i].ok;
-    }
-    return ok;
 }
 
 void co_graph_destroy(co_graph *g) {

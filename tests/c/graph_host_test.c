@@ -375,9 +375,8 @@ static void topology_case(void) {
     EXPECT(co_graph_plan_init(&desc, &p) == ROCKET_E_SHAPE);
 }
 
-/* A large input (4 MiB) is checked for finiteness by several host threads: an infinity at the start,
- * at every 1 MiB boundary and at the end is refused with no launch and the output untouched, and the
- * all-finite input runs. */
+/* A large input (4 MiB): a NaN or an infinity at the start, on either side of a 1 MiB boundary and at
+ * the end is refused with no launch and the output untouched, and the all-finite input runs. */
 static void large_input_case(void) {
     enum { R = 1024, C = 2048 };
     const size_t n = (size_t)R * C;
