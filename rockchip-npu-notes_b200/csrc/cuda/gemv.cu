@@ -165,7 +165,6 @@ struct Meta {
 // Sliced launches keep the FP32 tile sums of the 16-row blocks they own in a ring of B_RING
 // shared-memory buffers of 16 rows x M x/K tiles (the host limits M x tiles to 64).
 constexpr int B_RING = 4;
-constexpr int BUF_FLOATS = 16 * STREAM_MAX_XTILES;
 constexpr int TILES_PER_SLICE = STREAM_SLICE / 256;
 constexpr int SWZ_BOX_K = 64;                        // K width of one 128-byte swizzled TMA box
 
@@ -178,26 +177,32 @@ constexpr int SWZ_BOX_K = 64;                        // K width of one 128-byte 
 // so two CTAs fit one SM: a CTA of the next launch on the stream (programmatic dependent launch)
 // becomes resident while this launch's CTA still runs there and streams its own weights into its
 // ring, hiding the launch's ramp-up and tail.
-template <bool SL, bool HF = false>
+// Wide sliced launches (WX: x rows beyond 32 KB, e.g. M = 8 at K = 4096) use 8 slots, a 64 KB x
+// table and buffers for M x tiles <= 128, so the batch streams W once.
+template <bool SL, bool HF = false, bool WX = false>
 struct SCfg {
     static_assert(!(SL && HF), "half-SM launches are whole-row launches");
-    static constexpr int STAGES = HF ? 6 : (SL ? 11 : 12);
+    static_assert(!WX || SL, "the wide x table is for sliced launches");
+    static constexpr int STAGES = HF ? 6 : (SL ? (WX ? 8 : 11) : 12);
     static constexpr int THREADS = 32 * (1 + STAGES);
     static constexpr int MIN_BLOCKS = HF ? 2 : 1;
     static constexpr uint32_t STAGE_BYTES = STREAM_ROW_BYTES;
     static constexpr int PROBS = SL ? 1 : GROUP_MAX;
-    static constexpr uint32_t X_BYTES = HF ? STREAM_X_HALF_BYTES : STREAM_X_BYTES;
+    static constexpr uint32_t X_BYTES = HF ? STREAM_X_HALF_BYTES : (WX ? STREAM_X_WIDE_BYTES : STREAM_X_BYTES);
+    static constexpr int BUF_FL = 16 * (WX ? STREAM_MAX_XTILES_WIDE : STREAM_MAX_XTILES);   // floats per buffer
     static constexpr uint32_t X_OFFSET = STAGES * STAGE_BYTES;
     static constexpr uint32_t META_OFFSET = X_OFFSET + X_BYTES;
     static constexpr uint32_t BAR_OFFSET = META_OFFSET + STAGES * sizeof(Meta);
     static constexpr uint32_t ABORT_OFFSET = BAR_OFFSET + 2 * STAGES * 8;
     static constexpr uint32_t PROB_OFFSET = ABORT_OFFSET + 16;
     static constexpr uint32_t BUF_OFFSET = (PROB_OFFSET + PROBS * (uint32_t)sizeof(Problem) + 15u) & ~15u;
-    static constexpr uint32_t CTL_OFFSET = BUF_OFFSET + (SL ? B_RING * BUF_FLOATS * 4u : 0u);
+    static constexpr uint32_t CTL_OFFSET = BUF_OFFSET + (SL ? B_RING * BUF_FL * 4u : 0u);
     // sliced launches also reserve the room to align the ring to 1024 bytes (swizzle atom)
     static constexpr uint32_t SMEM_BYTES = CTL_OFFSET + (SL ? 2u * B_RING * 4u + 16u + 1024u : 0u);
 };
-static_assert(SCfg<false>::SMEM_BYTES <= 232448 && SCfg<true>::SMEM_BYTES <= 232448, "shared memory");
+static_assert(SCfg<false>::SMEM_BYTES <= 232448 && SCfg<true>::SMEM_BYTES <= 232448 &&
+              SCfg<true, false, true>::SMEM_BYTES <= 232448, "shared memory");
+static_assert(SCfg<true, false, true>::BAR_OFFSET % 8 == 0, "barrier alignment");
 // two half-SM CTAs (each with the 1 KB the hardware reserves per CTA) in the SM's 228 KB
 static_assert(2 * (SCfg<false, true>::SMEM_BYTES + 1024) <= 233472, "two half-SM CTAs per SM");
 static_assert(SCfg<false>::STAGES <= 32 && SCfg<true>::STAGES <= 32, "one producer lane per slot");
@@ -293,10 +298,10 @@ __device__ __forceinline__ Range cta_range(int units) {
 // next position is computed as soon as a copy is issued, so a freed slot costs the lane the meta
 // store, the expect-tx and the copy: one 3-D box of 8 x (64 K x 16 rows) when map3, else eight
 // 2-D boxes. Polling, abort and the bounded wait are those of produce().
-template <bool HF>
+template <bool HF, bool WX>
 __device__ __forceinline__ void produce_sliced(const Group &g, const Problem *prob, uint8_t *smem, Meta *meta,
                                                uint32_t full0, uint32_t empty0, volatile int *abort_flag, int lane) {
-    using C = SCfg<true, HF>;
+    using C = SCfg<true, HF, WX>;
     const bool mine = lane < C::STAGES;
     const int slot = mine ? lane : 0;
     const uint32_t full = full0 + 8 * slot, empty = empty0 + 8 * slot;
@@ -630,10 +635,11 @@ __device__ __forceinline__ void slice_sums(const __half *stage, const __half *xr
 
 // Shared-memory state of a sliced launch's tile-sum buffers.
 struct SliceCtl {
-    float *buf;              // B_RING x BUF_FLOATS: [tile (T)][row (16)][x row (M)]
+    float *buf;              // B_RING x buf_floats: [tile (T)][row (16)][x row (M)]
     unsigned *count;         // [B_RING] slices of the buffer's block that have arrived
     volatile int *open;      // [B_RING] local block index the buffer is open to
     unsigned *lead;          // slices handed on so far of the block owned by the previous CTA
+    int buf_floats;          // floats per buffer (16 x the largest M x tiles of the configuration)
 };
 
 // Bounded spin of lane 0 until the buffer is open to local block lb (its previous block was folded).
@@ -729,7 +735,7 @@ __device__ __forceinline__ bool deliver_slice(const Group &grp, const Problem &p
     }
     const int lb = blk - fb;   // local index among the blocks this CTA owns
     const int bb = lb & (B_RING - 1);
-    float *buf = ctl.buf + bb * BUF_FLOATS;
+    float *buf = ctl.buf + bb * ctl.buf_floats;
     bool ok = true;
     if (lane == 0 && ld_acquire_cta(ctl.open + bb) != lb) {   // acquire: the buffer's previous reads are done
         ok = wait_open(ctl, bb, lb, abort_flag, grp.flags);
@@ -788,10 +794,10 @@ __device__ __forceinline__ bool deliver_slice(const Group &grp, const Problem &p
     return bad;
 }
 
-template <bool SL, bool HF>
-__global__ void __launch_bounds__(SCfg<SL, HF>::THREADS, SCfg<SL, HF>::MIN_BLOCKS)
+template <bool SL, bool HF, bool WX>
+__global__ void __launch_bounds__(SCfg<SL, HF, WX>::THREADS, SCfg<SL, HF, WX>::MIN_BLOCKS)
     gemv_stream_kernel(const __grid_constant__ Group g) {
-    using C = SCfg<SL, HF>;
+    using C = SCfg<SL, HF, WX>;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // sliced launches read 128-byte-swizzled boxes, whose pattern repeats every 1024 bytes
     uint8_t *smem = SL ? reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -804,7 +810,7 @@ __global__ void __launch_bounds__(SCfg<SL, HF>::THREADS, SCfg<SL, HF>::MIN_BLOCK
     __half *xtab = reinterpret_cast<__half *>(smem + C::X_OFFSET);
     SliceCtl ctl{reinterpret_cast<float *>(smem + C::BUF_OFFSET), reinterpret_cast<unsigned *>(smem + C::CTL_OFFSET),
                  reinterpret_cast<volatile int *>(smem + C::CTL_OFFSET + 4 * B_RING),
-                 reinterpret_cast<unsigned *>(smem + C::CTL_OFFSET + 8 * B_RING)};
+                 reinterpret_cast<unsigned *>(smem + C::CTL_OFFSET + 8 * B_RING), C::BUF_FL};
     const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * C::STAGES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // Programmatic dependent launch (when the launch allows it): the next kernel on the stream may
@@ -838,7 +844,7 @@ __global__ void __launch_bounds__(SCfg<SL, HF>::THREADS, SCfg<SL, HF>::MIN_BLOCK
         for (int i = lane; i < words; i += 32) dst[i] = src[i];
         __syncwarp();
         asm volatile("bar.arrive 2, %0;" ::"r"(C::THREADS) : "memory");
-        if constexpr (SL) produce_sliced<HF>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
+        if constexpr (SL) produce_sliced<HF, WX>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
         else produce<SL, HF>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
         return;
     }
@@ -909,13 +915,16 @@ cudaError_t stream_attr() {
     static bool done[64] = {};
     const int dev = device_index();
     if (dev >= 0 && dev < 64 && done[dev]) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<false, false>,
+    cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<false, false, false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SCfg<false>::SMEM_BYTES);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemv_stream_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(gemv_stream_kernel<true, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)SCfg<true>::SMEM_BYTES);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemv_stream_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(gemv_stream_kernel<true, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)SCfg<true, false, true>::SMEM_BYTES);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemv_stream_kernel<false, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)SCfg<false, true>::SMEM_BYTES);
     if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
     return e;
@@ -1055,16 +1064,24 @@ static unsigned stream_grid(bool hf, long long wbytes, int units, int sm_count) 
     return (unsigned)(units < ctas ? units : ctas);
 }
 
+// A sliced launch of M x rows needs the wide configuration when its x rows exceed the 32 KB table or
+// its M x tiles exceed the standard block buffers.
+static bool wide_x(int M, int K) {
+    const long long k8 = ((long long)K + 7) & ~7ll;
+    return (long long)M * k8 * 2 > STREAM_X_BYTES || (long long)M * ((k8 + 255) / 256) > STREAM_MAX_XTILES;
+}
+
 // x rows of one launch: as many as the x table holds (and, for a sliced problem, as many as the
 // scratch holds the tile sums of); 0 when not even one fits.
 static long long rows_that_fit(int N, int K, long long ldw) {
     const long long k8 = ((long long)K + 7) & ~7ll;
-    long long fit = (long long)STREAM_X_BYTES / (k8 * 2);
-    if (sliced(K, ldw)) {
+    const bool sl = sliced(K, ldw);
+    long long fit = (long long)(sl ? STREAM_X_WIDE_BYTES : STREAM_X_BYTES) / (k8 * 2);
+    if (sl) {
         if ((N + 15) / 16 > TCOUNT_WORDS) return 0;
         const long long tiles = (k8 + 255) / 256;
         const long long per_row = ((long long)N + 15) / 16 * 16 * tiles;
-        const long long fs = TSUM_FLOATS / per_row, fb = STREAM_MAX_XTILES / tiles;
+        const long long fs = TSUM_FLOATS / per_row, fb = STREAM_MAX_XTILES_WIDE / tiles;
         if (fs < fit) fit = fs;
         if (fb < fit) fit = fb;
     }
@@ -1073,7 +1090,7 @@ static long long rows_that_fit(int N, int K, long long ldw) {
 
 int stream_stages(int M, int N, int K, long long ldw) {
     if (!stream_launches(M, N, K, ldw)) return 0;
-    if (sliced(K, ldw)) return SCfg<true>::STAGES;
+    if (sliced(K, ldw)) return wide_x(M, K) ? SCfg<true, false, true>::STAGES : SCfg<true>::STAGES;
     const long long xelems = (long long)M * (((long long)K + 7) & ~7ll);
     return half_sm(false, xelems) ? SCfg<false, true>::STAGES : SCfg<false>::STAGES;
 }
@@ -1108,7 +1125,7 @@ int pack_group(const Group &all, int first, Group &g) {
         while (e < g.nx && !(g.xsrc[e].x == p.x && g.xsrc[e].ldx == p.ldx && g.xsrc[e].K == p.K)) ++e;
         if (e == g.nx) {
             const int need = all.M * ((p.K + 7) & ~7);
-            if ((used + need) * 2 > STREAM_X_BYTES) break;
+            if ((used + need) * 2 > (sliced(p.K, p.ldw) ? STREAM_X_WIDE_BYTES : STREAM_X_BYTES)) break;
             g.xsrc[g.nx++] = XSource{p.x, p.ldx, p.K, used};
             used += need;
         }
@@ -1155,9 +1172,11 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
         if (grid_out) *grid_out = grid;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
-        cfg.blockDim = dim3(sl ? SCfg<true>::THREADS : hf ? SCfg<false, true>::THREADS : SCfg<false>::THREADS);
-        cfg.dynamicSmemBytes = sl ? SCfg<true>::SMEM_BYTES : hf ? SCfg<false, true>::SMEM_BYTES
-                                                               : SCfg<false>::SMEM_BYTES;
+        const bool wx = sl && wide_x(g.M, g.prob[0].K);
+        cfg.blockDim = dim3(sl ? (wx ? SCfg<true, false, true>::THREADS : SCfg<true>::THREADS)
+                               : (hf ? SCfg<false, true>::THREADS : SCfg<false>::THREADS));
+        cfg.dynamicSmemBytes = sl ? (wx ? SCfg<true, false, true>::SMEM_BYTES : SCfg<true>::SMEM_BYTES)
+                                  : (hf ? SCfg<false, true>::SMEM_BYTES : SCfg<false>::SMEM_BYTES);
         cfg.stream = stream;
         // Early start of the next kernel: always for half-SM launches (half_sm); full-SM launches
         // (whose next CTAs cannot become resident before this launch's exit) allow it where the fixed
@@ -1168,9 +1187,10 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
         attr[0].val.programmaticStreamSerializationAllowed = (hf || wbytes <= PDL_MAX_BYTES) ? 1 : 0;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        const cudaError_t le0 = sl   ? cudaLaunchKernelEx(&cfg, gemv_stream_kernel<true, false>, g)
-                                : hf ? cudaLaunchKernelEx(&cfg, gemv_stream_kernel<false, true>, g)
-                                     : cudaLaunchKernelEx(&cfg, gemv_stream_kernel<false, false>, g);
+        const cudaError_t le0 = sl   ? (wx ? cudaLaunchKernelEx(&cfg, gemv_stream_kernel<true, false, true>, g)
+                                           : cudaLaunchKernelEx(&cfg, gemv_stream_kernel<true, false, false>, g))
+                                : hf ? cudaLaunchKernelEx(&cfg, gemv_stream_kernel<false, true, false>, g)
+                                     : cudaLaunchKernelEx(&cfg, gemv_stream_kernel<false, false, false>, g);
         if (le0 != cudaSuccess) return le0;
         const cudaError_t le = cudaGetLastError();
         if (le != cudaSuccess) return le;

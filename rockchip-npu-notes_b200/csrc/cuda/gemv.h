@@ -47,6 +47,10 @@ constexpr int STREAM_ROW_BYTES = 16384; // one copy slot
 constexpr int STREAM_WHOLE_K = 2048;
 constexpr int STREAM_SLICE = 512;       // 16 rows x 512 FP16 = one slot; a multiple of the 256-K tile
 constexpr int STREAM_MAX_XTILES = 64;   // sliced launches: M x (256-K tiles) per block buffer
+// Wide sliced launches (x rows beyond 32 KB, e.g. M = 8 at K = 4096): 8 ring slots, a 64 KB x table
+// and block buffers for M x tiles <= 128, so the batch streams W once instead of once per row group.
+constexpr int STREAM_X_WIDE_BYTES = 65536;
+constexpr int STREAM_MAX_XTILES_WIDE = 128;
 
 struct Problem {
     const __half *x; long long ldx;
@@ -81,17 +85,18 @@ struct Group {
 };
 
 // The streamed kernel serves M <= 8 when the M x rows fit the x table (M * roundup(K, 8) FP16):
-// K <= 16384 for M = 1, 8192 for M = 2, 4096 for M = 4, 2048 for M = 8; a long-K problem also needs
-// M x (K/256 tiles) <= STREAM_MAX_XTILES, its tile sums (N * M * K/256 floats) and block counters
-// (N / 16) to fit the scratch.
+// whole-row problems (K <= 2048) in 32 KB; long-K problems in 64 KB (K <= 16384 for M = 2, 8192 for
+// M = 4, 4096 for M = 8), with M x (K/256 tiles) <= STREAM_MAX_XTILES_WIDE, their tile sums
+// (N * M * K/256 floats) and block counters (N / 16) fitting the scratch.
 bool streamed(int M, int N, int K, long long ldw);
 // Streamed launches that serve a single problem in `launch`: 1 when streamed(), else M is split into
 // row groups whose x rows fit the table (each group streams all of W; every row's result is the same
 // as in a one-launch run); 0 when no row group fits: the per-lane kernel serves it.
 int stream_launches(int M, int N, int K, long long ldw);
 
-// Ring slots of the streamed kernel that would serve this shape (11 for long K; 6 for a half-SM
-// launch, whose x rows fit STREAM_X_HALF_BYTES; else 12); 0 when the per-lane-load kernel serves it.
+// Ring slots of the streamed kernel that would serve this shape (long K: 11, or 8 in a wide launch;
+// 6 for a half-SM launch, whose x rows fit STREAM_X_HALF_BYTES; else 12); 0 when the per-lane-load
+// kernel serves it.
 int stream_stages(int M, int N, int K, long long ldw);
 
 // Picks the kernel for p (streamed when eligible, else the per-lane-load kernel) and launches it.

@@ -50,9 +50,9 @@ def bits(t, cols):
 @pytest.mark.parametrize("k", [1, 17, 576, 1000, 1536, 2048, 2056, 4096, 8192])
 def test_small_m_rows_are_batch_independent_and_within_tolerance(b2, gpu_fd, k):
     """Rows of M=1, 2, 3 and 8 runs agree bit for bit (each x row's result does not depend on the
-    rest of the batch, also where M=8 is split into two streamed launches of 4 rows because 8 x rows
-    of K > 2048 exceed the kernel's 32 KB x table), in both accumulation modes, with and without
-    bias and HardSigmoid; all rows within tolerance."""
+    rest of the batch: M=8 at K=4096 is one wide launch with a 64 KB x table, at K=8192 two launches
+    of 4 rows), in both accumulation modes, with and without bias and HardSigmoid; all rows within
+    tolerance."""
     n = 300
     x, w, b = uniform_case(8, n, k, 7000 + k)
     ldx, ldy = r8(k), r8(n)
