@@ -260,8 +260,8 @@ static bool linear_args_ok(const b2k_linear *a) {
 }
 
 // One launch of the weight-streaming GEMV (M <= 8) or the GEMM in output mode `out_mode`, writing
-// y/ldy (FP16 modes) or a->partial (OUT_RAW32). The bias is applied in OUT_FINAL only; with `extra`
-// the residual goes to the store of either kernel, the gate fields to the GEMM's epilogue.
+// y/ldy (FP16 modes) or a->partial (OUT_RAW32). The bias is applied in OUT_FINAL only; the residual
+// and gate fields go to the GEMM's epilogue only with `extra`.
 static cudaError_t launch_core(b2_dev *d, const b2k_linear *a, int out_mode, bool fold, void *y, size_t ldy,
                                bool extra) {
     const __half *bias = static_cast<const __half *>(a->bias);
@@ -276,10 +276,6 @@ static cudaError_t launch_core(b2_dev *d, const b2k_linear *a, int out_mode, boo
         p.out_mode = out_mode; p.post = a->post; p.fold = fold ? 1 : 0;
         p.flags = d->flags_dev;
         p.scratch = d->gemv;
-        if (extra && out_mode == b2::gemv::OUT_FINAL) {
-            p.res = static_cast<const __half *>(a->res);
-            p.ldr = (long long)a->ldr;
-        }
         return b2::gemv::launch(p, d->stream, d->sm_count, nullptr);
     }
     b2::gemm::Params p = {};
@@ -358,7 +354,7 @@ int b2d_linear(b2_dev *d, const b2k_linear *a, unsigned *launches) {
     if (out_mode != b2::gemm::OUT_RAW32 && (!a->y || a->ldy < a->n)) return ROCKET_E_SHAPE;
     if (a->res && (a->raw_only || !fp16_operand_ok(a->res, a->ldr, a->n) || !fp16_operand_ok(a->y, a->ldy, a->n)))
         return ROCKET_E_SHAPE;
-    const bool fuse_res = a->res && a->fused;
+    const bool fuse_res = a->res && a->fused && !use_gemv(a);
     cudaError_t e = launch_core(d, a, out_mode, fold, a->y, a->ldy, fuse_res);
     if (e != cudaSuccess) return rc_of(e);
     *launches = core_launches(a);

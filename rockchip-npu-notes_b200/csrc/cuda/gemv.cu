@@ -6,17 +6,23 @@
 // (research/custom-ops/src/co_decoder.c:128-129). On B200 the small-M case is a weight stream,
 // served by two kernels with the same per-element arithmetic:
 //
-// Streamed kernel (M <= 8, K <= 2048: every decode projection of a small decoder):
-//   one persistent CTA per SM. Lanes 0-11 of warp 0 stream the weights with cp.async.bulk into
-//   12 slots of 16 KB shared memory (lane s feeds slot s), each slot a block of whole W rows --
-//   rows [n0, n0 + R) of a row-major [N, ldw] matrix are one contiguous byte range, so one bulk
-//   copy moves them; up to 192 KB are in flight per SM. Consumer warp s takes the units landing
-//   in slot s and computes them on the tensor cores (below). The launch's x rows are copied once per CTA into a 32 KB shared table (problems
-//   that share an input share the entry), filled by the consumer warps while the first weights
-//   are in flight. A launch covers a group of up to GROUP_MAX independent projections (same M):
-//   units of R rows from all of them are spread over the CTAs. Launches whose x rows fit 12 KB run
-//   as half-SM CTAs (6 slots, two CTAs per SM) under programmatic dependent launch, so the next
-//   launch's CTAs stream their weights while this launch runs or drains (see half_sm).
+// Streamed kernel (M <= 8, K <= 16384; every decode projection of a small decoder):
+//   persistent CTAs. Lanes of warp 0 each own one 16 KB shared-memory slot of a copy ring and keep
+//   it filled; consumer warp s takes the units landing in slot s and computes them on the tensor
+//   cores (below). The launch's x rows are copied once per CTA into a shared table (problems that
+//   share an input share the entry), filled by the consumer warps while the first weights are in
+//   flight. Configurations (SCfg):
+//   * whole-row (K <= 2048): a unit is whole W rows -- rows [n0, n0 + R) of a row-major [N, ldw]
+//     matrix are one contiguous byte range, one cp.async.bulk copy. 12 slots and a 32 KB x table
+//     per SM; launches whose x rows fit 12 KB run as half-SM CTAs (6 slots, two CTAs per SM) under
+//     programmatic dependent launch, so the next launch's CTAs stream their weights while this
+//     launch runs or drains (see half_sm). A launch covers a group of up to GROUP_MAX independent
+//     projections (same M): units of R rows from all of them are spread over the CTAs.
+//   * sliced (2048 < K <= 16384): a unit is one 512-wide K slice of a 16-row block, one 3-D TMA
+//     copy (eight 2-D boxes when K is not a multiple of 64); each CTA takes a contiguous range of
+//     units and the blocks' per-256-K tile sums are folded in K order by the block's owner
+//     (deliver_slice). 11 slots and a 32 KB x table, or 8 slots and a 64 KB table when the x rows
+//     need it (wide_x).
 // Per-lane-load kernel (the other M <= 8 shapes): each warp owns one W row at a time and every
 //   lane reads 16 bytes per 256-element K tile with read-only, L1-bypassing loads; several tiles'
 //   loads are issued before any arithmetic. The grid is the number of co-resident CTAs.
@@ -77,8 +83,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 template <int MR>
 __device__ __forceinline__ bool finish_row(int M, int lane, int n, int out_mode, int fold, int post,
                                            const __half *bias, __half *y, long long ldy, float *partial,
-                                           long long ldp, const __half *res, long long ldr,
-                                           const float (&acc)[MR], const float (&run)[MR]) {
+                                           long long ldp, const float (&acc)[MR], const float (&run)[MR]) {
     const bool has_bias = bias != nullptr;
     const float b = has_bias ? __half2float(bias[n]) : 0.0f;
     bool bad = false;
@@ -93,8 +98,7 @@ __device__ __forceinline__ bool finish_row(int M, int lane, int n, int out_mode,
             y[(size_t)r * ldy + n] = __float2half_rn(total);
         } else {
             const float v = fold ? finish_tile16(total, b, has_bias, post) : finish_fp32(total, b, post);
-            __half h = __float2half_rn(v);
-            if (res) h = __float2half_rn(__fadd_rn(__half2float(h), __half2float(res[(size_t)r * ldr + n])));
+            const __half h = __float2half_rn(v);
             bad |= half_nonfinite(h);
             y[(size_t)r * ldy + n] = h;
         }
@@ -151,8 +155,8 @@ __global__ void __launch_bounds__(D_THREADS) gemv_direct_kernel(const Params p) 
                 }
             }
         }
-        bad |= finish_row<MR>(p.M, lane, n, p.out_mode, p.fold, p.post, p.bias, p.y, p.ldy, p.partial, p.ldp,
-                              p.out_mode == OUT_FINAL ? p.res : nullptr, p.ldr, acc, run);
+        bad |= finish_row<MR>(p.M, lane, n, p.out_mode, p.fold, p.post, p.bias, p.y, p.ldy, p.partial, p.ldp, acc,
+                              run);
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) raise_flag(p.flags, FLAG_NONFINITE_OUTPUT);
 }
@@ -172,7 +176,8 @@ constexpr int SWZ_BOX_K = 64;                        // K width of one 128-byte 
 // empty barriers | abort flag | the group's problems (copied from the kernel parameter once per CTA:
 // dynamically indexed parameter reads are slow) | sliced only: tile-sum buffers, their arrival
 // counters and the block each buffer is open to. Whole-row launches use 12 slots; sliced launches
-// (a single long-K problem) give the 12th slot's space to the tile-sum buffers.
+// (a single long-K problem) give the 12th slot's space to the tile-sum buffers, wide ones (WX) four
+// slots to the 64 KB x table and the larger buffers.
 // Half-SM whole-row launches (HF: see half_sm) use 6 slots and the small x table, ~110 KB in all,
 // so two CTAs fit one SM: a CTA of the next launch on the stream (programmatic dependent launch)
 // becomes resident while this launch's CTA still runs there and streams its own weights into its
@@ -366,49 +371,35 @@ __device__ __forceinline__ void produce_sliced(const Group &g, const Problem *pr
     if (armed) drain_phase(full, ph ^ 1u);   // the last copy this lane issued
 }
 
-// The producer warp: lane s < STAGES feeds ring slot s with this CTA's local units q = s, s + STAGES,
-// ... then an end marker. All lanes poll their slots' empty barriers together with a non-blocking
-// test, so no lane's wait holds up another lane's copy. A whole-row unit is one bulk copy of its
-// rows; a sliced unit (one 512-wide K slice of a 16-row block) is eight 64 x 16 tensor boxes with
-// the 128-byte swizzle. After an abort or a wait that ran out, each lane waits (bounded) for its own
-// copy in flight.
-template <bool SL, bool HF>
+// The producer warp of a whole-row launch: lane s < STAGES feeds ring slot s with this CTA's local
+// units q = s, s + STAGES, ... then an end marker. All lanes poll their slots' empty barriers
+// together with a non-blocking test, so no lane's wait holds up another lane's copy. A unit is one
+// bulk copy of its rows. After an abort or a wait that ran out, each lane waits (bounded) for its
+// own copy in flight. (Sliced launches use produce_sliced.)
+template <bool HF>
 __device__ __forceinline__ void produce(const Group &g, const Problem *prob, uint8_t *smem, Meta *meta, uint32_t full0,
                                         uint32_t empty0, volatile int *abort_flag, int lane) {
-    using C = SCfg<SL, HF>;
+    using C = SCfg<false, HF>;
     const int count = g.count, units = g.units;
     const bool mine = lane < C::STAGES;
     const int slot = mine ? lane : 0;
     const uint32_t full = full0 + 8 * slot, empty = empty0 + 8 * slot;
     const uint32_t dst = smem_u32(smem + (size_t)slot * C::STAGE_BYTES);
-    const Range rg = cta_range(units);
     uint32_t ph = 0;
     bool done = !mine, armed = false;
     int q = slot, pi = 0;
     uint64_t t0 = 0;
     for (uint32_t polls = 1;; ++polls) {
         if (!done && mbar_test_wait(empty, ph ^ 1u)) {
-            const long long u = SL ? rg.first + q : (long long)blockIdx.x + (long long)q * gridDim.x;
-            if (u < (SL ? rg.end : (long long)units)) {
+            const long long u = (long long)blockIdx.x + (long long)q * gridDim.x;   // round-robin units
+            if (u < (long long)units) {
                 while (pi + 1 < count && u >= prob[pi + 1].unit_begin) ++pi;
                 const Problem &p = prob[pi];
-                const int uq = (int)u - p.unit_begin;
-                const int blk = SL ? uq / p.slices : uq, sl = SL ? uq - blk * p.slices : 0;
-                const int row0 = blk * p.rows_per_unit;
-                meta[slot] = Meta{pi, row0, min(p.rows_per_unit, p.N - row0), sl};
-                if (SL) {
-                    // box b: rows [row0, row0 + 16) x K [k0 + 64b, k0 + 64b + 64); rows past N and
-                    // columns past K arrive as zeros
-                    const int k0 = sl * p.kslice, K8 = (p.K + 7) & ~7;
-                    const int boxes = min(p.kslice / SWZ_BOX_K, (K8 - k0 + SWZ_BOX_K - 1) / SWZ_BOX_K);
-                    mbar_arrive_expect_tx(full, (uint32_t)boxes * 16u * SWZ_BOX_K * 2u);
-                    for (int b = 0; b < boxes; ++b)
-                        tma_box(dst + (uint32_t)b * 16u * SWZ_BOX_K * 2u, &g.wmap, full, k0 + SWZ_BOX_K * b, row0);
-                } else {
-                    const uint32_t bytes = (uint32_t)meta[slot].rows * (uint32_t)p.ldw * 2u;
-                    mbar_arrive_expect_tx(full, bytes);
-                    bulk_g2s(dst, p.w + (size_t)row0 * p.ldw, bytes, full);
-                }
+                const int row0 = ((int)u - p.unit_begin) * p.rows_per_unit;
+                meta[slot] = Meta{pi, row0, min(p.rows_per_unit, p.N - row0), 0};
+                const uint32_t bytes = (uint32_t)meta[slot].rows * (uint32_t)p.ldw * 2u;
+                mbar_arrive_expect_tx(full, bytes);
+                bulk_g2s(dst, p.w + (size_t)row0 * p.ldw, bytes, full);
                 armed = true;
                 ph ^= 1u;
                 q += C::STAGES;
@@ -514,16 +505,11 @@ __device__ __forceinline__ void block_accumulate(const __half *wa, const __half 
 
 // Writes one output: raw FP32 / raw FP16 / bias + activation. Returns true if a final FP16 output is
 // not finite.
-// `b` is bias[n] (0 without a bias) and `rs` the residual res[xr, n] (with a residual), both loaded
-// by the caller ahead of the sums. The residual is added to the rounded result and rounded once,
-// y = fp16(res + fp16(result)), as the graph's ADD node computes it.
+// `b` is bias[n] (0 without a bias), loaded by the caller ahead of the sums.
 __device__ __forceinline__ float bias_at(const Problem &pr, int n, bool valid) {
     return (pr.bias && valid) ? __half2float(__ldg(pr.bias + n)) : 0.0f;
 }
-__device__ __forceinline__ float res_at(const Problem &pr, int xr, int n, bool valid) {
-    return (pr.res && valid) ? __half2float(pr.res[(size_t)xr * pr.ldr + n]) : 0.0f;
-}
-__device__ __forceinline__ bool store_out(const Problem &pr, int xr, int n, float total, float b, float rs) {
+__device__ __forceinline__ bool store_out(const Problem &pr, int xr, int n, float total, float b) {
     if (pr.out_mode == OUT_RAW32) {
         pr.partial[(size_t)xr * pr.ldp + n] = total;
         return false;
@@ -534,8 +520,7 @@ __device__ __forceinline__ bool store_out(const Problem &pr, int xr, int n, floa
     }
     const bool has_bias = pr.bias != nullptr;
     const float v = pr.fold ? finish_tile16(total, b, has_bias, pr.post) : finish_fp32(total, b, pr.post);
-    __half h = __float2half_rn(v);
-    if (pr.res) h = __float2half_rn(__fadd_rn(__half2float(h), rs));
+    const __half h = __float2half_rn(v);
     pr.y[(size_t)xr * pr.ldy + n] = h;
     return half_nonfinite(h);
 }
@@ -550,7 +535,7 @@ __device__ __forceinline__ void release_slot(uint32_t empty, int lane) {
 // Writes the block's results: lane (g, t4) element 0 is row g / x row 2t4, 1 row g / x row 2t4+1,
 // 2 and 3 the same for row g+8 (rows relative to the block's first row `n0`).
 __device__ __forceinline__ bool block_finish(const Problem &pr, int M, int n0, int ra, int rc, int rows, int lane,
-                                             const BlockAcc &s, float ba, float bc, const float (&rs)[4]) {
+                                             const BlockAcc &s, float ba, float bc) {
     const int t4 = lane & 3;
     bool bad = false;
 #pragma unroll
@@ -558,7 +543,7 @@ __device__ __forceinline__ bool block_finish(const Problem &pr, int M, int n0, i
         const int r = (i < 2 ? ra : rc), xr = 2 * t4 + (i & 1);
         if (r >= rows || xr >= M) continue;
         const float total = pr.fold ? s.run[i] : (s.acc[0][i] + s.acc[1][i]) + (s.acc[2][i] + s.acc[3][i]);
-        bad |= store_out(pr, xr, n0 + r, total, i < 2 ? ba : bc, rs[i]);
+        bad |= store_out(pr, xr, n0 + r, total, i < 2 ? ba : bc);
     }
     return bad;
 }
@@ -577,19 +562,13 @@ __device__ __forceinline__ bool process_unit(const Problem &pr, int M, const __h
     for (int rb = 0; rb < rows; rb += 16) {
         const int ra = rb + g, rc = rb + g + 8;
         const float ba = bias_at(pr, row0 + ra, fin && ra < rows), bc = bias_at(pr, row0 + rc, fin && rc < rows);
-        float rs[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int r = i < 2 ? ra : rc, xr = 2 * (lane & 3) + (i & 1);
-            rs[i] = res_at(pr, xr, row0 + r, fin && r < rows && xr < M);
-        }
         BlockAcc s;
         block_reset(s);
         // rows past the unit read its first row (their outputs are not stored)
         block_accumulate(stage + (size_t)(ra < rows ? ra : 0) * pr.ldw, stage + (size_t)(rc < rows ? rc : 0) * pr.ldw,
                          xrow, K8, pr.fold != 0, lane, s);
         if (rb + 16 >= rows) release_slot(empty, lane);
-        bad |= block_finish(pr, M, row0, ra, rc, rows, lane, s, ba, bc, rs);
+        bad |= block_finish(pr, M, row0, ra, rc, rows, lane, s, ba, bc);
     }
     return bad;
 }
@@ -768,7 +747,6 @@ __device__ __forceinline__ bool deliver_slice(const Group &grp, const Problem &p
         const float *pl = buf + r * M + xr;   // tile t at pl[16 M t]
         const float *pg = tg + ((size_t)r * M + xr) * T;
         const float b = bias_at(pr, row0 + r, pr.out_mode == OUT_FINAL);
-        const float rsd = res_at(pr, xr, row0 + r, pr.out_mode == OUT_FINAL);
         float total = 0.0f;
         for (int t0 = 0; t0 < T; t0 += 8) {   // eight tile sums loaded ahead of their fold
             float v[8];
@@ -783,7 +761,7 @@ __device__ __forceinline__ bool deliver_slice(const Group &grp, const Problem &p
                 if (t < T) total = pr.fold ? fold16(total, v[j], t == 0) : (t == 0 ? v[j] : total + v[j]);
             }
         }
-        bad |= store_out(pr, xr, row0 + r, total, b, rsd);
+        bad |= store_out(pr, xr, row0 + r, total, b);
     }
     __syncwarp();
     if (lane == 0) {
@@ -845,7 +823,7 @@ __global__ void __launch_bounds__(SCfg<SL, HF, WX>::THREADS, SCfg<SL, HF, WX>::M
         __syncwarp();
         asm volatile("bar.arrive 2, %0;" ::"r"(C::THREADS) : "memory");
         if constexpr (SL) produce_sliced<HF, WX>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
-        else produce<SL, HF>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
+        else produce<HF>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
         return;
     }
     asm volatile("bar.sync 2, %0;" ::"r"(C::THREADS) : "memory");   // barriers and problem table ready
@@ -1227,8 +1205,7 @@ cudaError_t launch(const Params &p, cudaStream_t stream, int sm_count, unsigned 
             g.prob[0] = Problem{p.x + (size_t)r0 * p.ldx, p.ldx, p.w, p.ldw, p.bias,
                                 p.y ? p.y + (size_t)r0 * p.ldy : nullptr, p.ldy,
                                 p.partial ? p.partial + (size_t)r0 * p.ldp : nullptr, p.ldp,
-                                p.N, p.K, p.out_mode, p.post, p.fold, 0, 0, 0, 0, 0, 0,
-                                p.res ? p.res + (size_t)r0 * p.ldr : nullptr, p.ldr};
+                                p.N, p.K, p.out_mode, p.post, p.fold, 0, 0, 0, 0, 0, 0};
             const cudaError_t e = launch_group(g, stream, sm_count, grid_out, nullptr);
             if (e != cudaSuccess) return e;
         }

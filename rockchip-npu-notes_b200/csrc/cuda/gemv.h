@@ -30,7 +30,6 @@ struct Params {
     int out_mode, post, fold;
     unsigned *flags;
     Scratch scratch;                    // tile sums of long-K problems (from the device handle)
-    const __half *res; long long ldr;   // OUT_FINAL only: y = fp16(res + fp16(result)), or nullptr
 };
 
 // Bulk-copy streamed kernel: one launch serves up to GROUP_MAX independent projections that share
@@ -64,7 +63,6 @@ struct Problem {
     int kslice;                         // 0: whole-row units; else K slice of the 16-row units
     int slices;                         // K slices of a sliced problem (units = blocks x slices)
     int pad;
-    const __half *res; long long ldr;   // OUT_FINAL only: y = fp16(res + fp16(result)), or nullptr
 };
 
 // One distinct x (problems that share x and K share the entry): M rows of K, pitch ldx in

@@ -170,8 +170,7 @@ static unsigned node_kernels(const co_graph_node *n, const struct fusion *f, uns
     const int small = rows <= B2D_GEMV_MAX_M;
     if (fused) {
         if (f->kind[id] == F_MEMBER) return 0;
-        if (f->kind[id] == F_GATED) return small ? 2 : 1;   /* small M: the GEMV, then the gated combine */
-        if (f->kind[id] == F_RESIDUAL) return 1;            /* the residual in the GEMM or GEMV store */
+        if (f->kind[id] == F_GATED || f->kind[id] == F_RESIDUAL) return small ? 2 : 1;
         if (n->op == CO_GRAPH_LINEAR) return 1;
     } else if (n->op == CO_GRAPH_LINEAR) {
         return 2;   /* GEMM/GEMV to the FP16 fold, then the separate epilogue */

@@ -162,7 +162,7 @@ int b2d_linear(b2_dev *d, const b2k_linear *a, unsigned *launches) {
                 *y = oracle_ew16(0, *y, ((const uint16_t *)a->res)[(size_t)r * a->ldr + c]);
                 if (f16_nonfinite(*y)) d->status |= B2D_ST_NONFINITE_OUTPUT;
             }
-        if (!a->fused) *launches += 1;   /* fused: in the GEMM or GEMV store */
+        if (!(a->fused && a->m > B2D_GEMV_MAX_M)) *launches += 1;
     }
     return rc;
 }
