@@ -97,7 +97,12 @@ int b2_linear_epilogue_device(b2_linear *, unsigned m, const float *partial, siz
  *   - m * roundup(n, 4) * 4 bytes must fit in B2_NOALLOC_SCRATCH_BYTES, else ROCKET_E_TILING
  *     (for example n = 4096 allows m <= 512).
  *   - The first call on a device looks up the scratch address (cudaGetSymbolAddress) and caches
- *     it; make that first call before any stream capture.
+ *     it; make that first call before any stream capture. The lookup switches the calling
+ *     thread's current CUDA device to the handle's device and back; the call leaves the current
+ *     device as it found it.
+ *   - m <= 8 runs the weight-streaming small-M kernel, which writes the raw FP32 sums into the
+ *     same scratch (its long-K tile-sum buffers belong to the handle and were allocated when the
+ *     handle was opened), so that route allocates nothing either.
  *   - All calls on a device share the one scratch array and it keeps the last call's contents.
  *     No clearing is needed (each call writes every scratch element it later reads), but calls
  *     whose work overlaps on the GPU -- two streams, or two operators at once -- race on it.
@@ -177,6 +182,14 @@ int b2_ksplit_connect(b2_ksplit *, const unsigned char *blobs /* world x B2_KSPL
 /* First row and row count of Y that this rank writes for a round of m rows. */
 int b2_ksplit_rows(const b2_ksplit *, unsigned m, unsigned *row0, unsigned *rows);
 int b2_ksplit_run(b2_ksplit *, unsigned m, const void *x, size_t ldx, void *y, size_t ldy);
+/* Phase timing of rounds (no counterpart in the reference; the reference's probes time whole
+ * submits). While enabled, every b2_ksplit_run records four CUDA timing events on the handle's
+ * stream: round start, GEMM done (including its stores into the owners' memory), signal done,
+ * reduction done. b2_ksplit_phase_ms waits for the last round's reduction and returns the three
+ * device intervals in milliseconds: ms[0] GEMM + NVLink stores, ms[1] signal, ms[2] the wait for
+ * every rank's signal + the reduction and epilogue of the owned rows. Disabling frees the events. */
+int b2_ksplit_set_timing(b2_ksplit *, int enable);
+int b2_ksplit_phase_ms(b2_ksplit *, float ms[3]);
 void b2_ksplit_destroy(b2_ksplit *);
 
 /* ----------------------------------------------------------------------- fault injection */

@@ -3,7 +3,7 @@
 
 Run once, on a machine that has the reference checkout (it is NOT needed at test time):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <reference checkout>
 
 It imports two standard-library-only scripts of the reference, unmodified:
 
@@ -152,4 +152,6 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: {sys.argv[0]} REFERENCE_CHECKOUT  (the Ecazy/rockchip-npu-notes root)")
+    main(sys.argv[1])

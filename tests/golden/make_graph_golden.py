@@ -3,7 +3,7 @@
 
 Run once, on a machine that has the reference checkout (it is NOT needed at test time):
 
-    python tests/golden/make_graph_golden.py /root/reference
+    python tests/golden/make_graph_golden.py <reference checkout>
 
 It imports research/custom-ops/tools/python/graph_gate.py (standard library only, unmodified;
 it imports cli_gate.py from the same directory) and, for every ``SHAPES`` case (m, d, h), with
@@ -69,4 +69,6 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: {sys.argv[0]} REFERENCE_CHECKOUT  (the Ecazy/rockchip-npu-notes root)")
+    main(sys.argv[1])

@@ -29,7 +29,10 @@ def _linear_view(b2, fd, elements):
     return buf, buf.view(t)
 
 
-@pytest.mark.parametrize("m,k,n", [(64, 512, 256), (33, 200, 70)])
+# m > 8 runs the tcgen05 GEMM; m <= 8 runs the weight-streaming small-M kernel (whole-row units
+# up to k = 2048, 16-row x 512-K slices with tile-sum buffers beyond), both writing raw FP32 sums
+# into the static scratch before the epilogue kernel.
+@pytest.mark.parametrize("m,k,n", [(64, 512, 256), (33, 200, 70), (1, 512, 256), (8, 200, 70), (4, 4096, 512)])
 def test_noalloc_matches_existing_entry_on_two_calls(b2, m, k, n):
     L = b2.lib()
     fd = b2.open_device(0)
