@@ -17,9 +17,17 @@ scaling, one process per GPU).
             dense 16-bit tensor peak; DRAM traffic per launch from the committed ncu summary.
   sharded   M=8192, N=16384, K=16384 over all ranks with the total fixed (strong scaling):
             column-parallel (no collective) and the K-split N=1024 variant (FP32 partials reduced
-            by NCCL all-reduce / reduce-scatter, then the epilogue).
+            by NCCL all-reduce / reduce-scatter, then the epilogue; or fused: the GEMM epilogue
+            stores each row block into its owner's memory over NVLink, with per-phase times).
+            K-split steps start together on every rank (one-element NCCL all-reduce first).
   gemv      M=1 decode projections of a SmolLM-135M-shaped layer (HBM GB/s per launch, weights
-            rotated over > 4x L2).
+            rotated over > 4x L2): each alone, the layer's 7 as one grouped launch, all 8 with the
+            LM head as one grouped launch and as a decode step's dependent chain in one CUDA
+            graph, and long-K decode shapes (4096x4096, 11008x4096, 4096x11008).
+  cfg1      the fused HardSigmoid at M=64, N=256, K=512 (the reference CLI's operator): device,
+            CUDA-graph and end-to-end microseconds, beside the CPU oracle (C port, all threads)
+            and the pure-Python form of the reference's file-gate oracle.
+  summary   the key figures of all sections, printed last so that a truncated log keeps them.
   gemm_tile16  the same 4096^3 Linear with the reference's per-256-K FP16 running sum (the
             co_linear_* default numerics), device-resident like `value`.
   graph_ffn the SwiGLU FFN Y = X + Linear(SiLU(Linear(X, Wg, b)) * Linear(X, Wu), Wd) through the
@@ -346,6 +354,11 @@ def main():
     if rank == 0 and world == 1 and not args.no_graph:
         graph = bench_graph(b2, fd, torch, stream, peak_tflops, peak_gbs, args.graph_m)
 
+    # ---------------------------------------------------------------- config 1 (rank 0, N=1 only)
+    cfg1 = None
+    if rank == 0 and world == 1:
+        cfg1 = bench_cfg1(b2, fd, torch, stream, steps)
+
     line = None
     if rank == 0:
         traffic = traffic_per_launch()
@@ -370,16 +383,20 @@ def main():
             "clocks": clocks.summary(),
             "spot_check": {"rows": int(rows.numel()), "worst_err_over_tol_vs_fp64": worst},
         }
-        if shard:
-            line["sharded"] = shard
-        if gemv:
-            line["gemv"] = gemv
-        if tile16:
-            line["gemm_tile16"] = tile16
+        # detail first, then the compact summary last (what a truncated log tail still shows)
         if graph:
             line["graph_ffn"] = graph
+        if tile16:
+            line["gemm_tile16"] = tile16
+        if gemv:
+            line["gemv"] = gemv
+        if shard:
+            line["sharded"] = shard
+        if cfg1:
+            line["cfg1"] = cfg1
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_sample()
+        line["summary"] = summarize(world, kernel_tflops, e2e_ms, tile16, cfg1, shard, gemv, graph)
     b2.close(fd)
     if world > 1:
         dist.barrier()
@@ -388,9 +405,51 @@ def main():
         print(json.dumps(line), flush=True)
 
 
-def _timed_steps(torch, dist, world, stream, fn, warmup, steps, flush=None):
+def _r(v, digits=4):
+    """Rounds to `digits` significant digits (None stays None)."""
+    if v is None:
+        return None
+    return float(f"{v:.{digits}g}")
+
+
+def summarize(world, kernel_tflops, e2e_ms, tile16, cfg1, shard, gemv, graph):
+    """The line's key figures in a few hundred bytes, printed as its last key."""
+    out = {"n_gpus": world, "gemm_4096_fp32acc_tflops": _r(kernel_tflops), "e2e_ms": _r(e2e_ms)}
+    if tile16:
+        out["gemm_4096_tile16_tflops"] = _r(tile16["tflops"])
+    if cfg1:
+        out["cfg1_hsig_64x256x512_us"] = {"device": _r(cfg1["device_us"]), "graph": _r(cfg1["graph_us"]),
+                                          "e2e": _r(cfg1["e2e_us"]), "cpu_c_port": _r(cfg1["cpu_c_port_us"]),
+                                          "cpu_literal_s": _r(cfg1["cpu_oracle_literal_s"])}
+    if shard:
+        cp = shard["column_parallel"]
+        out["cfg5_8192x16384x16384_column_parallel"] = {"ms": _r(cp["ms_per_step"]),
+                                                        "tflops_per_gpu": _r(cp["tflops_per_gpu"])}
+        out["cfg5_ksplit_n1024_ms"] = {key[8:]: _r(v["ms_per_step"]) for key, v in shard.items()
+                                       if key.startswith("k_split_")}
+        phases = shard.get("k_split_fused", {}).get("phases_ms")
+        if phases:
+            out["cfg5_ksplit_fused_phases_ms"] = {key: _r(v) for key, v in phases.items()}
+    if gemv:
+        fr = {"set_8_grouped": gemv["set_8_grouped"]["frac"], "set_8_chain": gemv["set_8_decode_chain"]["frac"],
+              "lm_head": gemv["projections"]["lm_head"]["frac"],
+              "layer_7_grouped": gemv["layer_7_projections_grouped"]["frac"]}
+        fr.update({key: v["frac"] for key, v in gemv["long_k"].items()})
+        out["gemv_m1_frac_of_hbm"] = {key: _r(v, 3) for key, v in fr.items()}
+        out["gemv_set_8_grouped_us"] = _r(gemv["set_8_grouped"]["us"])
+    if graph:
+        out["graph_ffn_chain_ms"] = {m: _r(c["chain"]["ms"]) for m, c in graph["cases"].items()}
+    return out
+
+
+def _timed_steps(torch, dist, world, stream, fn, warmup, steps, flush=None, align=False, after=None):
     """Mean device ms of `fn` over `steps` (per-step CUDA events on `stream`; an optional L2 flush
-    between steps, outside the events), max over ranks."""
+    between steps, outside the events), max over ranks. With `align` (steps that exchange data
+    between ranks), each step's start event follows a one-element NCCL all-reduce on `stream`, so
+    every rank's step starts when the slowest rank is ready: a rank's step time then holds its own
+    work and the exchange, not another rank's L2 flush. `after(i)` runs on the host after step i
+    (for per-step readouts; it may synchronise)."""
+    token = torch.zeros(1, device="cuda") if align and world > 1 else None
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -398,7 +457,7 @@ def _timed_steps(torch, dist, world, stream, fn, warmup, steps, flush=None):
         dist.barrier()
     pairs = []
     with ClockSampler(torch.cuda.current_device()) as clocks:
-        for _ in range(steps):
+        for i in range(steps):
             if flush is not None:
                 # on the launching stream, before the start event: write a buffer larger than L2, then
                 # read one (so the timed launch starts with a cold L2 that holds no dirty lines whose
@@ -406,11 +465,16 @@ def _timed_steps(torch, dist, world, stream, fn, warmup, steps, flush=None):
                 with torch.cuda.stream(stream):
                     flush.zero_()
                     flush.view(torch.float32).sum()
+            if token is not None:
+                with torch.cuda.stream(stream):
+                    dist.all_reduce(token)
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(stream)
             fn()
             e.record(stream)
             pairs.append((s, e))
+            if after is not None:
+                after(i)
         torch.cuda.synchronize()
     ms = sum(s.elapsed_time(e) for s, e in pairs) / steps
     if world > 1:
@@ -493,7 +557,7 @@ def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup,
 
         with torch.cuda.stream(stream):
             y.zero_()
-            ms, clk = _timed_steps(torch, dist, world, stream, fn, 3, ksteps, flush=flush)
+            ms, clk = _timed_steps(torch, dist, world, stream, fn, 3, ksteps, flush=flush, align=True)
         if b2.status(fd):
             raise RuntimeError("device status raised in the K-split run")
         r0, r1 = (0, m) if coll != "reduce_scatter" else ks.row_shard(m)
@@ -509,7 +573,8 @@ def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup,
             "ms_per_step": ms, "steps": ksteps, "tflops": tflops, "tflops_per_gpu": tflops / world,
             "frac_per_gpu": tflops / world / peak_tflops, "k_per_gpu": ks.k1 - ks.k0,
             "fp32_partial_bytes": partial_bytes, "worst_err_over_tol_vs_fp64": worst, "clocks_rank0": clk,
-            "l2": "flushed between steps (write of 2x L2, outside the events)"}
+            "l2": "flushed between steps (write of 2x L2, outside the events)",
+            "start": "ranks aligned by a one-element NCCL all-reduce before each step"}
     ks.destroy()
 
     # fused K-split: partial row blocks stored into their owner's memory by the GEMM epilogue
@@ -519,9 +584,28 @@ def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup,
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         ms, clk = _timed_steps(torch, dist, world, stream,
-                               lambda: fk.run(m, xs.data_ptr(), kk, y.data_ptr(), n_ks), 3, ksteps, flush=flush)
+                               lambda: fk.run(m, xs.data_ptr(), kk, y.data_ptr(), n_ks), 3, ksteps, flush=flush,
+                               align=True)
     if b2.status(fd):
         raise RuntimeError("device status raised in the fused K-split run")
+    # the same rounds again with phase events (GEMM + NVLink stores, signal, wait + reduction), read
+    # after every step; mean per rank, then the max over ranks of each phase
+    fk.set_timing(True)
+    acc = [0.0, 0.0, 0.0]
+
+    def read_phases(_i):
+        for j, v in enumerate(fk.phase_ms()):
+            acc[j] += v
+
+    psteps = max(5, min(ksteps, 30))
+    with torch.cuda.stream(stream):
+        _timed_steps(torch, dist, world, stream, lambda: fk.run(m, xs.data_ptr(), kk, y.data_ptr(), n_ks), 2,
+                     psteps, flush=flush, align=True, after=read_phases)
+    fk.set_timing(False)
+    phases = torch.tensor([v / psteps for v in acc], device="cuda")
+    if world > 1:
+        dist.all_reduce(phases, op=dist.ReduceOp.MAX)
+    phases_ms = dict(zip(("gemm_and_stores", "signal", "wait_and_reduce"), phases.tolist()))
     r0, r1 = fk.rows(m)
     rows = torch.tensor(sorted({r0, (r0 + r1) // 2, r1 - 1}), device="cuda")
     ref = oracle.linear("fp64", x[rows].cpu().numpy(), w_ks, None, post=0, want=("act",))["act"]
@@ -534,12 +618,92 @@ def bench_sharded(b2, fd, torch, dist, stream, world, rank, peak_tflops, warmup,
         "collective": "GEMM epilogue stores to the owner over NVLink + signal + owner reduction (b2_ksplit_run)",
         "ms_per_step": ms, "steps": ksteps, "tflops": tflops, "tflops_per_gpu": tflops / world,
         "frac_per_gpu": tflops / world / peak_tflops, "k_per_gpu": fk.k1 - fk.k0, "rows_per_gpu": r1 - r0,
-        "worst_err_over_tol_vs_fp64": worst, "clocks_rank0": clk,
-        "l2": "flushed between steps (write of 2x L2, outside the events)"}
+        "worst_err_over_tol_vs_fp64": worst, "clocks_rank0": clk, "phases_ms": phases_ms,
+        "l2": "flushed between steps (write of 2x L2, outside the events)",
+        "start": "ranks aligned by a one-element NCCL all-reduce before each step"}
     fk.destroy()
     del x, xs, y, flush
     torch.cuda.empty_cache()
     return out
+
+
+def bench_cfg1(b2, fd, torch, stream, steps):
+    """Fused FP16 HardSigmoid(X W^T + b) at M=64, N=256, K=512 (X ~ U(-1,1), W ~ U(-1/sqrt(K),
+    1/sqrt(K)), b ~ U(-0.1,0.1), seed 0): the operator the reference's file CLI and host oracle run
+    (research/custom-ops/tools/python/cli_gate.py:38-49). 16.8 MFLOP, so it is latency-bound and
+    reported as absolute times, with the co_linear_* default numerics (per-256-K FP16 running sum):
+      device_us  b2_linear_run_device, back-to-back launches on the library's stream (CUDA events)
+      graph_us   the same launches replayed as one CUDA graph
+      e2e_us     co_linear_hsig_run from pinned host X/Y (H2D, finiteness scan, GEMM, sync, status
+                 check, D2H), CUDA events around the host calls
+      cpu        the oracle's C restatement of the reference arithmetic (exact tile sums, all host
+                 threads), and its pure-Python form of the file-gate oracle on one core (the same
+                 per-element loop as cli_gate.oracle: math.fsum per 256-K tile, FP16 running sum)."""
+    import numpy as np
+    import oracle
+    m, n, k = 64, 256, 512
+    rng = np.random.default_rng(0)
+    x = rng.uniform(-1, 1, (m, k)).astype(np.float16)
+    w = rng.uniform(-1 / np.sqrt(k), 1 / np.sqrt(k), (n, k)).astype(np.float16)
+    b = rng.uniform(-0.1, 0.1, n).astype(np.float16)
+    op = b2.Linear(fd, m, k, n, w, b, post=b2.CO_LINEAR_HSIG, mode=b2.CO_CHAIN, acc=b2.ACC_TILE16, compat=True)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty(m, n, device="cuda", dtype=torch.float16)
+    torch.cuda.synchronize()
+
+    def launch(_i=0):
+        op.run_device(m, xd.data_ptr(), k, yd.data_ptr(), n)
+
+    for _ in range(10):
+        launch()
+    b2.sync(fd)
+    reps = max(50, min(steps, 2000))
+    eager, graph = _eager_and_graph_ms(torch, stream, launch, reps)
+    if b2.status(fd):
+        raise RuntimeError("device status raised in the config-1 run")
+    ref = oracle.linear("tile16", x, w, b, post=1)["y16"]
+    ok, worst = oracle.tolerance_ok(yd.cpu().numpy(), ref)
+    if not ok:
+        raise RuntimeError(f"config-1 output outside tolerance (worst err/tol {worst:.3f})")
+    # end to end through the reference-facing entry, pinned host buffers
+    hx = b2.lib().b2_host_alloc(m * k * 2)
+    hy = b2.lib().b2_host_alloc(m * n * 2)
+    xh = np.ctypeslib.as_array(ctypes.cast(hx, ctypes.POINTER(ctypes.c_uint16)), shape=(m, k))
+    yh = np.ctypeslib.as_array(ctypes.cast(hy, ctypes.POINTER(ctypes.c_uint16)), shape=(m, n))
+    xh[:] = x.view(np.uint16)
+    run = b2.lib().co_linear_hsig_run
+    for _ in range(10):
+        b2.check("co_linear_hsig_run", run(op.h, hx, hy))
+    e2e_reps = max(50, min(steps, 1000))
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    es.record(stream)
+    for _ in range(e2e_reps):
+        run(op.h, hx, hy)
+    ee.record(stream)
+    ee.synchronize()
+    wall_us = (time.perf_counter() - t0) / e2e_reps * 1e6
+    e2e_us = es.elapsed_time(ee) / e2e_reps * 1e3
+    if not np.array_equal(yh, yd.cpu().numpy().view(np.uint16)):
+        raise RuntimeError("config-1 host and device entries differ")
+    b2.lib().b2_host_free(hx)
+    b2.lib().b2_host_free(hy)
+    op.destroy()
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    for _ in range(5):
+        oracle.linear("tile16", x, w, b, post=1, threads=threads)
+    c_s = (time.perf_counter() - t0) / 5
+    xs, ws, bs = (a.astype(np.float64).ravel().tolist() for a in (x, w, b))
+    t0 = time.perf_counter()
+    oracle.linear_py(m, k, n, xs, ws, bs, post=1)
+    py_s = time.perf_counter() - t0
+    flops = 2 * m * n * k
+    return {"m": m, "n": n, "k": k, "op": "HardSigmoid(XW^T+b), tile-16 numerics", "device_us": eager * 1e3,
+            "graph_us": graph * 1e3, "e2e_us": e2e_us, "e2e_wall_us": wall_us,
+            "device_tflops": flops / (graph * 1e-3) / 1e12, "worst_err_over_tol_vs_oracle": worst,
+            "cpu_c_port_us": c_s * 1e6, "cpu_c_port_threads": threads, "cpu_oracle_literal_s": py_s,
+            "cpu_oracle_literal": "pure-Python restatement of cli_gate.oracle (one core)"}
 
 
 def bench_tile16(b2, fd, torch, stream, peak_tflops, steps):
@@ -806,6 +970,97 @@ def bench_gemv(b2, fd, torch, stream, peak_gbs):
                                           "frac": gbytes / (ms * 1e-3) / 1e9 / peak_gbs, "eager_us": eager * 1e3,
                                           "launches": group_launches, "weight_sets": copies}
     for ops in sets:
+        for op in ops:
+            op.destroy()
+
+    # the whole set -- the layer's 7 projections and the LM head (63.7 MB of weights) -- as ONE grouped
+    # launch, the inputs as in a decode step (q/k/v/gate/up share the layer input; o, down and the LM
+    # head read their own); weight sets rotated over >= 4x L2, replayed as a CUDA graph
+    full = list(GEMV_LAYER)
+    set_bytes = sum(2 * n * k for _, n, k in full)
+    copies = min(64, max(2, -(-4 * l2 // set_bytes)))
+    w_host = {name: (rng.standard_normal((n, k)) * 0.02).astype(np.float16) for name, n, k in full}
+    sets = [[b2.Linear(fd, 1, k, n, w_host[name], None, post=b2.CO_LINEAR_NONE, acc=b2.ACC_FP32, compat=False)
+             for name, n, k in full] for _ in range(copies)]
+    xin["lm"] = torch.randn(1, 576, device="cuda", generator=gen).half()
+    src["lm_head"] = "lm"
+    ys = [torch.empty(1, n, device="cuda", dtype=torch.float16) for _, n, _ in full]
+    xp = [xin[src[name]].data_ptr() for name, _, _ in full]
+    ldx = [k for _, _, k in full]
+    yp = [y.data_ptr() for y in ys]
+    ldy = [n for _, n, _ in full]
+    torch.cuda.synchronize()
+    for ops in sets:
+        b2.group_run_device(ops, 1, xp, ldx, yp, ldy)
+    b2.sync(fd)
+    launches0 = b2.counters()["launches"]
+    b2.group_run_device(sets[0], 1, xp, ldx, yp, ldy)
+    set_launches = b2.counters()["launches"] - launches0
+    reps = max(64, 4 * copies)
+    eager, ms = _eager_and_graph_ms(torch, stream, lambda i: b2.group_run_device(sets[i % copies], 1, xp, ldx, yp, ldy),
+                                    reps)
+    if b2.status(fd):
+        raise RuntimeError("device status raised in the grouped set run")
+    fbytes = sum(2 * n * k + 2 * k + 2 * n for _, n, k in full)
+    out["set_8_grouped"] = {"bytes": fbytes, "us": ms * 1e3, "gb_s": fbytes / (ms * 1e-3) / 1e9,
+                            "frac": fbytes / (ms * 1e-3) / 1e9 / peak_gbs, "eager_us": eager * 1e3,
+                            "launches": set_launches, "weight_sets": copies}
+
+    # the same set as a decode step's dependent chain, one CUDA graph: {q,k,v} -> o (input: q's output)
+    # -> {gate, up} (input: o's output) -> down (input: gate's output) -> LM head (input: down's output)
+    name_ix = {name: i for i, (name, _, _) in enumerate(full)}
+    x0 = xin["h"]
+
+    def chain(i):
+        ops = sets[i % copies]
+        b2.group_run_device([ops[name_ix[q]] for q in ("q", "k", "v")], 1, [x0.data_ptr()] * 3, [576] * 3,
+                            [ys[name_ix[q]].data_ptr() for q in ("q", "k", "v")], [576, 192, 192])
+        ops[name_ix["o"]].run_device(1, ys[name_ix["q"]].data_ptr(), 576, ys[name_ix["o"]].data_ptr(), 576)
+        b2.group_run_device([ops[name_ix["gate"]], ops[name_ix["up"]]], 1, [ys[name_ix["o"]].data_ptr()] * 2,
+                            [576, 576], [ys[name_ix["gate"]].data_ptr(), ys[name_ix["up"]].data_ptr()], [1536, 1536])
+        ops[name_ix["down"]].run_device(1, ys[name_ix["gate"]].data_ptr(), 1536, ys[name_ix["down"]].data_ptr(), 576)
+        ops[name_ix["lm_head"]].run_device(1, ys[name_ix["down"]].data_ptr(), 576, ys[name_ix["lm_head"]].data_ptr(),
+                                           49152)
+
+    for i in range(copies):
+        chain(i)
+    b2.sync(fd)
+    creps = max(16, 2 * copies)
+    eager, ms = _eager_and_graph_ms(torch, stream, chain, creps)
+    if b2.status(fd):
+        raise RuntimeError("device status raised in the decode chain run")
+    out["set_8_decode_chain"] = {"bytes": fbytes, "us": ms * 1e3, "gb_s": fbytes / (ms * 1e-3) / 1e9,
+                                 "frac": fbytes / (ms * 1e-3) / 1e9 / peak_gbs, "eager_us": eager * 1e3,
+                                 "launches": 5, "weight_sets": copies}
+    for ops in sets:
+        for op in ops:
+            op.destroy()
+    del sets
+
+    # long-K decode projections at M=1 (a 7B-class layer's attention and FFN shapes), weights rotated
+    out["long_k"] = {}
+    for n, k in ((4096, 4096), (11008, 4096), (4096, 11008)):
+        wbytes = 2 * n * k
+        copies = max(2, -(-4 * l2 // wbytes))
+        w_host = (np.random.default_rng(n + 3 * k).standard_normal((n, k)) * 0.02).astype(np.float16)
+        ops = [b2.Linear(fd, 1, k, n, w_host, None, post=b2.CO_LINEAR_NONE, acc=b2.ACC_TILE16, compat=False)
+               for _ in range(copies)]
+        x = torch.randn(1, k, device="cuda", generator=gen).half()
+        y = torch.empty(1, n, device="cuda", dtype=torch.float16)
+        torch.cuda.synchronize()
+        for op in ops:
+            op.run_device(1, x.data_ptr(), k, y.data_ptr(), n)
+        b2.sync(fd)
+        reps = max(32, 4 * copies)
+        eager, ms = _eager_and_graph_ms(
+            torch, stream, lambda i: ops[i % copies].run_device(1, x.data_ptr(), k, y.data_ptr(), n), reps)
+        if b2.status(fd):
+            raise RuntimeError(f"device status raised in the {n}x{k} GEMV")
+        nbytes = wbytes + 2 * k + 2 * n
+        info = ops[0].info()
+        out["long_k"][f"{n}x{k}"] = {"us": ms * 1e3, "gb_s": nbytes / (ms * 1e-3) / 1e9,
+                                      "frac": nbytes / (ms * 1e-3) / 1e9 / peak_gbs, "eager_us": eager * 1e3,
+                                      "stages": info.stages, "grid": info.grid, "weight_copies": copies}
         for op in ops:
             op.destroy()
     out["peak_gbs"] = peak_gbs

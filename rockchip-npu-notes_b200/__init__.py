@@ -228,6 +228,8 @@ SIGNATURES = {
     "b2_ksplit_connect": (_I, [_P, ctypes.c_char_p]),
     "b2_ksplit_rows": (_I, [_P, _U, ctypes.POINTER(_U), ctypes.POINTER(_U)]),
     "b2_ksplit_run": (_I, [_P, _U, _P, _Z, _P, _Z]),
+    "b2_ksplit_set_timing": (_I, [_P, _I]),
+    "b2_ksplit_phase_ms": (_I, [_P, ctypes.POINTER(ctypes.c_float)]),
     "b2_ksplit_destroy": (None, [_P]),
     # co_graph.h
     "co_graph_plan_init": (_I, [ctypes.POINTER(CoGraphDesc), ctypes.POINTER(CoGraphPlan)]),

@@ -157,6 +157,7 @@ int b2d_ipc_close(b2_dev *, void *ptr);
 /* One fused K-split round (ksplit.cu): the routed raw-FP32 GEMM of `a` (a->fused = 0,
  * a->raw_only = 1), the round signal to every rank, and the reduction + epilogue of the owned
  * rows into y_own. `bufs[q]` is rank q's buffer as mapped here (bufs[rank] = the local one). */
+typedef struct b2_timer b2_timer;
 typedef struct {
     unsigned world, rank, rows_per_rank, own_rows;
     size_t ldp;
@@ -164,8 +165,18 @@ typedef struct {
     const void *bias;
     int post;
     void *y_own; size_t ldy;
+    b2_timer *timer;                /* NULL, or marks 0..3: round start, GEMM done, signal done, reduce done */
 } b2k_ksplit;
 int b2d_ksplit_round(b2_dev *, const b2k_linear *a, const b2k_ksplit *ks, unsigned *launches);
+
+/* ---------------------------------------------------------------------- event timer
+ * B2D_TIMER_MARKS CUDA timing events of one handle: b2d_timer_mark records mark i on the handle's
+ * stream; b2d_timer_ms waits for mark `to` and returns the device time from mark `from` to it. */
+#define B2D_TIMER_MARKS 8u
+int b2d_timer_create(b2_dev *, b2_timer **out);
+void b2d_timer_destroy(b2_timer *);
+int b2d_timer_mark(b2_dev *, b2_timer *, unsigned mark);
+int b2d_timer_ms(b2_timer *, unsigned from, unsigned to, float *ms);
 
 /* Ordinal of the CUDA device behind a handle (-1 for NULL). */
 int b2d_ordinal(b2_dev *);

@@ -446,6 +446,49 @@ int b2d_ipc_close(b2_dev *d, void *ptr) {
     return rc_of(cudaIpcCloseMemHandle(ptr));
 }
 
+struct b2_timer {
+    int ordinal;
+    cudaEvent_t ev[B2D_TIMER_MARKS];
+};
+
+int b2d_timer_create(b2_dev *d, b2_timer **out) {
+    *out = nullptr;
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    b2_timer *t = static_cast<b2_timer *>(calloc(1, sizeof(b2_timer)));
+    if (!t) return ROCKET_E_NOMEM;
+    t->ordinal = d->ordinal;
+    for (unsigned i = 0; i < B2D_TIMER_MARKS; ++i)
+        if (cudaEventCreate(&t->ev[i]) != cudaSuccess) {
+            cudaGetLastError();
+            b2d_timer_destroy(t);
+            return ROCKET_E_DEVICE;
+        }
+    *out = t;
+    return 0;
+}
+
+void b2d_timer_destroy(b2_timer *t) {
+    if (!t) return;
+    cudaSetDevice(t->ordinal);
+    for (unsigned i = 0; i < B2D_TIMER_MARKS; ++i)
+        if (t->ev[i]) cudaEventDestroy(t->ev[i]);
+    free(t);
+}
+
+int b2d_timer_mark(b2_dev *d, b2_timer *t, unsigned mark) {
+    if (!t || mark >= B2D_TIMER_MARKS || !set_device(d)) return ROCKET_E_SHAPE;
+    return rc_of(cudaEventRecord(t->ev[mark], d->stream));
+}
+
+int b2d_timer_ms(b2_timer *t, unsigned from, unsigned to, float *ms) {
+    if (!t || !ms || from >= B2D_TIMER_MARKS || to >= B2D_TIMER_MARKS) return ROCKET_E_SHAPE;
+    cudaSetDevice(t->ordinal);
+    cudaError_t e = cudaEventSynchronize(t->ev[to]);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(ms, t->ev[from], t->ev[to]);
+    if (e != cudaSuccess) cudaGetLastError();
+    return e == cudaSuccess ? 0 : ROCKET_E_DEVICE;
+}
+
 int b2d_ksplit_round(b2_dev *d, const b2k_linear *a, const b2k_ksplit *ks, unsigned *launches) {
     *launches = 0;
     if (!set_device(d)) return ROCKET_E_DEVICE;
@@ -479,9 +522,11 @@ int b2d_ksplit_round(b2_dev *d, const b2k_linear *a, const b2k_ksplit *ks, unsig
     p.route_rows = (int)ks->rows_per_rank;
     p.partial = p.route_dst[ks->rank];
     b2::gemm::Shape s = {a->x, a->ldx, a->w, a->ldw};
+    if (ks->timer && cudaEventRecord(ks->timer->ev[0], d->stream) != cudaSuccess) return ROCKET_E_DEVICE;
     cudaError_t e = b2::gemm::launch(s, p, d->stream, d->ordinal, d->sm_count, nullptr);
     if (e != cudaSuccess) return rc_of(e);
     *launches = 1;
+    if (ks->timer && cudaEventRecord(ks->timer->ev[1], d->stream) != cudaSuccess) return ROCKET_E_DEVICE;
 
     // 2. round signal
     SignalParams sp = {};
@@ -491,6 +536,7 @@ int b2d_ksplit_round(b2_dev *d, const b2k_linear *a, const b2k_ksplit *ks, unsig
         sp.peer_flag[q] = reinterpret_cast<unsigned *>(static_cast<char *>(ks->bufs[q]) + FLAGS_OFFSET) + ks->rank;
     if ((e = b2::ksplit::signal(sp, d->stream)) != cudaSuccess) return rc_of(e);
     *launches = 2;
+    if (ks->timer && cudaEventRecord(ks->timer->ev[2], d->stream) != cudaSuccess) return ROCKET_E_DEVICE;
 
     // 3. reduction of the owned rows
     ReduceParams rp = {};
@@ -510,6 +556,7 @@ int b2d_ksplit_round(b2_dev *d, const b2k_linear *a, const b2k_ksplit *ks, unsig
     rp.ldy = (long long)ks->ldy;
     rp.status = d->flags_dev;
     if ((e = b2::ksplit::reduce(rp, d->stream, d->sm_count)) != cudaSuccess) return rc_of(e);
+    if (ks->timer && cudaEventRecord(ks->timer->ev[3], d->stream) != cudaSuccess) return ROCKET_E_DEVICE;
     *launches = ks->own_rows ? 3 : 2;
     return 0;
 }

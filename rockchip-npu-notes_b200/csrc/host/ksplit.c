@@ -24,6 +24,7 @@ struct b2_ksplit {
     size_t bytes;
     void *peer[B2_KSPLIT_MAX_WORLD];
     int connected;
+    b2_timer *timer;   /* phase marks of each round while timing is enabled */
 };
 
 static size_t ksplit_bytes(unsigned world, unsigned rpr, size_t ldp) {
@@ -136,6 +137,7 @@ int b2_ksplit_run(b2_ksplit *k, unsigned m, const void *x, size_t ldx, void *y, 
     ks.post = a.post;
     ks.y_own = rows ? (char *)y + (size_t)row0 * ldy * 2 : NULL;
     ks.ldy = ldy;
+    ks.timer = k->timer;
     if (b2h_fault(B2_FAULT_LAUNCH)) return ROCKET_E_DEVICE;
     unsigned launches = 0;
     int rc = b2d_ksplit_round(b2h_dev(b2h_linear_fd(k->op)), &a, &ks, &launches);
@@ -143,10 +145,31 @@ int b2_ksplit_run(b2_ksplit *k, unsigned m, const void *x, size_t ldx, void *y, 
     return rc;
 }
 
+int b2_ksplit_set_timing(b2_ksplit *k, int enable) {
+    if (!k) return ROCKET_E_SHAPE;
+    if (!enable) {
+        b2d_timer_destroy(k->timer);
+        k->timer = NULL;
+        return 0;
+    }
+    if (k->timer) return 0;
+    return b2d_timer_create(b2h_dev(b2h_linear_fd(k->op)), &k->timer);
+}
+
+int b2_ksplit_phase_ms(b2_ksplit *k, float ms[3]) {
+    if (!k || !ms || !k->timer) return ROCKET_E_SHAPE;
+    for (unsigned i = 0; i < 3; ++i) {
+        int rc = b2d_timer_ms(k->timer, i, i + 1, &ms[i]);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
 void b2_ksplit_destroy(b2_ksplit *k) {
     if (!k) return;
     int fd = b2h_linear_fd(k->op);
     b2d_sync(b2h_dev(fd));
+    b2d_timer_destroy(k->timer);
     close_peers(k);
     b2h_free(fd, k->buf, k->bytes);
     free(k);

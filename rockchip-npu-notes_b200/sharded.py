@@ -165,6 +165,17 @@ class FusedKSplit:
         """x_ptr: this rank's X[:, k0:k1] [m, ldx]; y_ptr: Y [m, ldy] (rows(m) written)."""
         _b2.check("b2_ksplit_run", _b2.lib().b2_ksplit_run(self.h, m, x_ptr, ldx, y_ptr, ldy))
 
+    def set_timing(self, enable=True):
+        """Record phase events in every round (b2_ksplit_set_timing)."""
+        _b2.check("b2_ksplit_set_timing", _b2.lib().b2_ksplit_set_timing(self.h, 1 if enable else 0))
+
+    def phase_ms(self):
+        """Device ms of the last round's phases: (GEMM + NVLink stores, signal, wait + reduction)."""
+        import ctypes
+        ms = (ctypes.c_float * 3)()
+        _b2.check("b2_ksplit_phase_ms", _b2.lib().b2_ksplit_phase_ms(self.h, ms))
+        return tuple(float(v) for v in ms)
+
     def destroy(self):
         if self.h:
             _b2.lib().b2_ksplit_destroy(self.h)

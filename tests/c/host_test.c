@@ -143,6 +143,16 @@ static void test_ragged_and_fp32(int fd) {
     for (unsigned r = 0; r < m; r++) same &= memcmp(yb + (size_t)r * 304, ref + (size_t)r * n, (size_t)n * 2) == 0;
     CHECK(same, "k-split round equals the FP32ACC model");
     CHECK(b2_ksplit_run(ks, 8, xp, 1000, yb, 304) == ROCKET_E_UNSUPPORTED, "k-split needs m > 8");
+    /* phase timing: refused before it is enabled, three intervals after a timed round, off again */
+    float phase[3] = {-1.0f, -1.0f, -1.0f};
+    CHECK(b2_ksplit_phase_ms(ks, phase) == ROCKET_E_SHAPE, "phase times need timing enabled");
+    CHECK(b2_ksplit_set_timing(ks, 1) == 0 && b2_ksplit_set_timing(ks, 1) == 0, "timing enabled (idempotent)");
+    CHECK(b2_ksplit_phase_ms(ks, phase) == ROCKET_E_SHAPE, "no phase times before a timed round");
+    CHECK(b2_ksplit_run(ks, m, xp, 1000, yb, 304) == 0, "timed k-split round");
+    CHECK(b2_ksplit_phase_ms(ks, phase) == 0 && phase[0] >= 0.0f && phase[1] >= 0.0f && phase[2] >= 0.0f,
+          "phase times of the timed round");
+    CHECK(b2_ksplit_set_timing(ks, 0) == 0 && b2_ksplit_phase_ms(ks, phase) == ROCKET_E_SHAPE, "timing disabled");
+    CHECK(b2_ksplit_set_timing(ks, 1) == 0, "timing left on for destroy");
     b2_ksplit_destroy(ks);
     co_linear_destroy(opk);
     co_linear_destroy(op32);

@@ -324,6 +324,27 @@ int b2d_ipc_close(b2_dev *d, void *ptr) {
 }
 
 /* One-rank round: the FP32 partial, then the epilogue of the owned rows. */
+/* Timing events: the mock completes everything at once, so every interval is 0. */
+struct b2_timer {
+    int marked[B2D_TIMER_MARKS];
+};
+int b2d_timer_create(b2_dev *d, b2_timer **out) {
+    *out = d ? calloc(1, sizeof(b2_timer)) : NULL;
+    return *out ? 0 : (d ? ROCKET_E_NOMEM : ROCKET_E_DEVICE);
+}
+void b2d_timer_destroy(b2_timer *t) { free(t); }
+int b2d_timer_mark(b2_dev *d, b2_timer *t, unsigned mark) {
+    if (!d || !t || mark >= B2D_TIMER_MARKS) return ROCKET_E_SHAPE;
+    t->marked[mark] = 1;
+    return 0;
+}
+int b2d_timer_ms(b2_timer *t, unsigned from, unsigned to, float *ms) {
+    if (!t || !ms || from >= B2D_TIMER_MARKS || to >= B2D_TIMER_MARKS || !t->marked[from] || !t->marked[to])
+        return ROCKET_E_SHAPE;
+    *ms = 0.0f;
+    return 0;
+}
+
 int b2d_ksplit_round(b2_dev *d, const b2k_linear *a, const b2k_ksplit *ks, unsigned *launches) {
     *launches = 0;
     if (!d || !a || !ks || ks->world != 1 || ks->rank != 0 || ks->rows_per_rank % 32) return ROCKET_E_SHAPE;
@@ -339,6 +360,7 @@ int b2d_ksplit_round(b2_dev *d, const b2k_linear *a, const b2k_ksplit *ks, unsig
     if (!rc && ks->own_rows) rc = b2d_epilogue(d, ks->own_rows, a->n, part, ldp, ks->bias, ks->post, 1, ks->y_own, ks->ldy);
     free(part);
     if (!rc) *launches = 3;
+    for (unsigned i = 0; !rc && ks->timer && i < 4; ++i) rc = b2d_timer_mark(d, ks->timer, i);
     return rc;
 }
 
