@@ -118,7 +118,9 @@ int b2_linear_run_device_noalloc(b2_linear *, unsigned m, const void *x, size_t 
  * Operators with m <= 8 whose m x k input fits the weight-streaming GEMV's 32 KB shared-memory
  * table (m * roundup(k, 8) * 2 bytes; k <= 8192 at m <= 2, 4096 at m = 4, 2048 at m = 8) share ONE
  * kernel launch as long as their distinct inputs (members passing the same X share it) fit the
- * table together; otherwise they are packed in order into consecutive launches that each fit. Any other member runs as its own b2_linear_run_device launch. Each result is bit-identical
+ * table together; otherwise they are packed in order into consecutive launches that each fit.
+ * A member whose K is streamed in slices (k > 2048 at m > 4, k > 8192) runs in a launch of its
+ * own, and any other member as its own b2_linear_run_device launch. Each result is bit-identical
  * to that operator's own b2_linear_run_device (CO_SEPARATE operators are finished in the same
  * launch with the same arithmetic as their separate epilogue). X_i and Y_i follow
  * b2_linear_run_device's rules; the X_i may alias (a shared input). Asynchronous on the handle's

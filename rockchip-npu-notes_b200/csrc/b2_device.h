@@ -94,9 +94,10 @@ typedef struct {
 int b2d_linear(b2_dev *, const b2k_linear *, unsigned *launches);
 int b2d_linear_config(b2_dev *, const b2k_linear *, b2k_config *);
 /* Runs `count` (<= B2D_GROUP_MAX) independent fused Linears with the same m. Those the streamed
- * small-M kernel serves in one launch (m <= 8, m x k input within its 32 KB x table, k <= 2048 to
- * share a launch with others) share one launch (or several when their distinct inputs exceed the
- * table); any other runs as b2d_linear.
+ * small-M kernel serves with whole-row units (m <= 8 with k <= 2048, or m <= 4 with k <= 8192, the
+ * m x k input within its 32 KB x table) share one launch (or several when their distinct inputs
+ * exceed the table); a long-K member streamed in K slices runs in a launch of its own; any other
+ * runs as b2d_linear.
  * Every op must have fused = 1 and raw_only = 0. */
 #define B2D_GROUP_MAX 16u
 int b2d_linear_group(b2_dev *, const b2k_linear *ops, unsigned count, unsigned *launches);

@@ -573,6 +573,100 @@ __device__ __forceinline__ bool process_unit(const Problem &pr, int M, const __h
     return bad;
 }
 
+// An octet unit (long K, whole rows): W rows ra = 0 and rc = 1 (rc = 0 when the unit has one row)
+// staged at `stage` (pitch ldw), against MR x rows (MR = 1, 2 or 4; x rows past M read row M - 1,
+// their outputs are not stored).
+// Octet o covers the 256-K tiles 8o .. 8o + 7. In its MMAs, A row i is W row (i < 8 ? ra : rc)
+// restricted to tile 8o + i % 8 and B column j is tile 8o + j of one x row, so D[i][j] is a tile sum
+// where i % 8 == j (the other outputs are discarded). Lane (g, t4) loads, per 64-wide window of its
+// tile 8o + g, the 8 consecutive elements at window + 8 t4 (and + 32) of both W rows and of the x
+// row: the k order of block_window, whose D[i][j] only needs A row i and B column j from the same
+// lanes -- here both come from lanes (g, *). Lanes with odd g take the upper half of each window
+// first (the 512-byte tile stride would otherwise put lanes g and g + 1 on the same banks); that
+// swaps accumulators 0/1 with 2/3, and their sum (acc0 + acc1) + (acc2 + acc3) is unchanged because
+// FP32 addition commutes. So every tile sum is the same bits as slice_sums gives, and the fold below
+// is deliver_slice's: the result equals the sliced path's for any batch size.
+// Tile (8o + g)'s sums land in lane 4g + g/2 (elements g % 2 and 2 + g % 2); after each octet they are
+// gathered with shuffles and folded in K order into the running total of the lane that finishes
+// that output. The slot is handed back after the last octet's reads.
+// x rows [xb, xb + MR) of the batch (MR = 1 or 2; M = 3..4 runs two passes over the staged rows);
+// the pass with `release` hands the slot back.
+template <int MR>
+__device__ __forceinline__ bool process_octet_unit(const Problem &pr, int M, const __half *stage, const __half *xtab,
+                                                   int row0, int rows, int lane, uint32_t empty, int xb,
+                                                   bool release) {
+    const int g = lane >> 2, t4 = lane & 3;
+    const int K8 = (pr.K + 7) & ~7, T = (K8 + 255) >> 8, O = (T + 7) >> 3;
+    const __half *wa = stage;
+    const __half *wc = stage + (size_t)(rows > 1 ? 1 : 0) * pr.ldw;
+    const __half *xr[MR];
+#pragma unroll
+    for (int m = 0; m < MR; ++m) xr[m] = xtab + pr.x_off + (size_t)min(xb + m, M - 1) * K8;
+    // output of this lane in the fold: lane L < 2 MR finishes W row L / MR, x row xb + L % MR
+    const int orow = lane / MR, oxr = xb + lane % MR;
+    const bool owner = lane < 2 * MR && orow < rows && oxr < M;
+    const float b = bias_at(pr, row0 + orow, owner && pr.out_mode == OUT_FINAL);
+    const int lo = (g & 1) ? 32 : 0, hi = 32 - lo;   // bank-spreading order of the two window halves
+    const int e = g & 1;                              // element of D[g][g] in this lane's fragment
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    float total = 0.0f;
+#pragma unroll 1
+    for (int o = 0; o < O; ++o) {
+        const int kt = (o * 8 + g) * 256;   // this lane's tile; past K its chunks load as zeros
+        float acc[MR][4][4];
+#pragma unroll
+        for (int m = 0; m < MR; ++m)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[m][j][i] = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const int k0 = kt + 64 * w + 8 * t4 + lo, k1 = kt + 64 * w + 8 * t4 + hi;
+            const bool l0 = k0 < K8, l1 = k1 < K8;
+            const uint4 a0 = l0 ? *reinterpret_cast<const uint4 *>(wa + k0) : z;
+            const uint4 a1 = l1 ? *reinterpret_cast<const uint4 *>(wa + k1) : z;
+            const uint4 c0 = l0 ? *reinterpret_cast<const uint4 *>(wc + k0) : z;
+            const uint4 c1 = l1 ? *reinterpret_cast<const uint4 *>(wc + k1) : z;
+#pragma unroll
+            for (int m = 0; m < MR; ++m) {
+                const uint4 x0 = l0 ? *reinterpret_cast<const uint4 *>(xr[m] + k0) : z;
+                const uint4 x1 = l1 ? *reinterpret_cast<const uint4 *>(xr[m] + k1) : z;
+                mma16816(acc[m][0], a0.x, c0.x, a0.y, c0.y, x0.x, x0.y);
+                mma16816(acc[m][1], a0.z, c0.z, a0.w, c0.w, x0.z, x0.w);
+                mma16816(acc[m][2], a1.x, c1.x, a1.y, c1.y, x1.x, x1.y);
+                mma16816(acc[m][3], a1.z, c1.z, a1.w, c1.w, x1.z, x1.w);
+            }
+        }
+        float ts[MR][2];
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+            float s[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) s[i] = (acc[m][0][i] + acc[m][1][i]) + (acc[m][2][i] + acc[m][3][i]);
+            ts[m][0] = e ? s[1] : s[0];   // W row ra, tile 8o + g
+            ts[m][1] = e ? s[3] : s[2];   // W row rc, tile 8o + g
+        }
+        if (release && o == O - 1) release_slot(empty, lane);   // every read of the stage is done
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int t = o * 8 + j;
+            if (t >= T) break;   // uniform
+            const int src = j * 4 + (j >> 1);
+            float mine = 0.0f;
+#pragma unroll
+            for (int r = 0; r < 2; ++r)
+#pragma unroll
+                for (int m = 0; m < MR; ++m) {
+                    const float v = __shfl_sync(0xffffffffu, ts[m][r], src);
+                    if (lane == r * MR + m) mine = v;
+                }
+            total = pr.fold ? fold16(total, mine, t == 0) : (t == 0 ? mine : total + mine);
+        }
+    }
+    return owner ? store_out(pr, oxr, row0 + orow, total, b) : false;
+}
+
 // The FP32 sums of the (up to) two 256-K tiles of slice `sl` of a 16-row block, staged as eight
 // 64 x 16 boxes with the 128-byte swizzle (16-byte chunk c of box row r sits at chunk c ^ (r & 7),
 // so the eight rows a warp reads at once fall on different banks). Same products and summation
@@ -875,6 +969,15 @@ __global__ void __launch_bounds__(SCfg<SL, HF, WX>::THREADS, SCfg<SL, HF, WX>::M
             __syncwarp();
             if (lane == 0) mbar_arrive(empty);   // the slot refills while the sums are handed on
             bad |= deliver_slice(g, pr, g.M, ctl, rg, fb, mt.row0, mt.rows, mt.slice, lane, ts, abort_flag);
+        } else if (pr.octet) {
+            if (g.M == 1) {
+                bad |= process_octet_unit<1>(pr, g.M, stage, xtab, mt.row0, mt.rows, lane, empty, 0, true);
+            } else {
+                const bool two = g.M > 2;   // a half-SM launch's 12 KB table holds two long-K x rows at most
+                bad |= process_octet_unit<2>(pr, g.M, stage, xtab, mt.row0, mt.rows, lane, empty, 0, HF || !two);
+                if (!HF && two)
+                    bad |= process_octet_unit<2>(pr, g.M, stage, xtab, mt.row0, mt.rows, lane, empty, 2, true);
+            }
         } else {
             bad |= process_unit(pr, g.M, stage, xtab, mt.row0, mt.rows, lane, empty);
         }
@@ -936,8 +1039,17 @@ unsigned direct_grid(int M, int N, int sm_count) {
     return (unsigned)(need < cap ? need : cap);
 }
 
+// Long-K whole-row (octet) units: 2048 < K <= 8192 with the row in one slot, M <= 4, and the M x rows
+// within the 32 KB x table.
+bool octet(int M, int K, long long ldw) {
+    const long long k8 = ((long long)K + 7) & ~7ll;
+    return k8 > STREAM_WHOLE_K && k8 <= STREAM_OCTET_MAX_K && ldw * 2 <= (long long)STREAM_ROW_BYTES && M >= 1 &&
+           M <= STREAM_OCTET_MAX_M && (long long)M * k8 * 2 <= STREAM_X_BYTES;
+}
+
 // Whole-row problems: rows per unit spread the group's weight bytes over about two units per SM, one
-// slot at most. Long-K problems (or rows wider than a slot): 16-row units streamed in K slices.
+// slot at most. Octet problems: one or two whole rows per unit. Other long-K problems (or rows wider
+// than a slot): 16-row units streamed in K slices.
 void plan_units(Group &g, int sm_count) {
     long long total = 0;
     for (int i = 0; i < g.count; ++i) total += (long long)g.prob[i].N * g.prob[i].ldw * 2;
@@ -947,6 +1059,17 @@ void plan_units(Group &g, int sm_count) {
     for (int i = 0; i < g.count; ++i) {
         Problem &p = g.prob[i];
         const int k8 = (p.K + 7) & ~7;
+        p.octet = 0;
+        if (octet(g.M, p.K, p.ldw)) {
+            // two rows per unit while they fit a slot (the A rows of an octet MMA hold two W rows)
+            p.octet = 1;
+            p.kslice = 0;
+            p.slices = 1;
+            p.rows_per_unit = 2 * p.ldw * 2 <= (long long)STREAM_ROW_BYTES ? 2 : 1;
+            p.unit_begin = units;
+            units += (p.N + p.rows_per_unit - 1) / p.rows_per_unit;
+            continue;
+        }
         if (k8 > STREAM_WHOLE_K || p.ldw * 2 > (long long)STREAM_ROW_BYTES) {
             p.kslice = STREAM_SLICE;
             p.slices = (k8 + STREAM_SLICE - 1) / STREAM_SLICE;
@@ -1024,9 +1147,9 @@ cudaError_t prepare() {
     return stream_attr();
 }
 
-bool sliced(int K, long long ldw) {
+bool sliced(int M, int K, long long ldw) {
     const long long k8 = ((long long)K + 7) & ~7ll;
-    return k8 > STREAM_WHOLE_K || ldw * 2 > (long long)STREAM_ROW_BYTES;
+    return (k8 > STREAM_WHOLE_K || ldw * 2 > (long long)STREAM_ROW_BYTES) && !octet(M, K, ldw);
 }
 
 // Half-SM CTAs (6 slots, two CTAs per SM) serve the whole-row launches whose x rows fit the small
@@ -1051,9 +1174,10 @@ static bool wide_x(int M, int K) {
 
 // x rows of one launch: as many as the x table holds (and, for a sliced problem, as many as the
 // scratch holds the tile sums of); 0 when not even one fits.
-static long long rows_that_fit(int N, int K, long long ldw) {
+static long long rows_that_fit(int M, int N, int K, long long ldw) {
     const long long k8 = ((long long)K + 7) & ~7ll;
-    const bool sl = sliced(K, ldw);
+    if (octet(M, K, ldw)) return (long long)STREAM_X_BYTES / (k8 * 2);
+    const bool sl = sliced(M, K, ldw);
     long long fit = (long long)(sl ? STREAM_X_WIDE_BYTES : STREAM_X_BYTES) / (k8 * 2);
     if (sl) {
         if ((N + 15) / 16 > TCOUNT_WORDS) return 0;
@@ -1068,14 +1192,14 @@ static long long rows_that_fit(int N, int K, long long ldw) {
 
 int stream_stages(int M, int N, int K, long long ldw) {
     if (!stream_launches(M, N, K, ldw)) return 0;
-    if (sliced(K, ldw)) return wide_x(M, K) ? SCfg<true, false, true>::STAGES : SCfg<true>::STAGES;
+    if (sliced(M, K, ldw)) return wide_x(M, K) ? SCfg<true, false, true>::STAGES : SCfg<true>::STAGES;
     const long long xelems = (long long)M * (((long long)K + 7) & ~7ll);
     return half_sm(false, xelems) ? SCfg<false, true>::STAGES : SCfg<false>::STAGES;
 }
 
 int stream_launches(int M, int N, int K, long long ldw) {
     if (M < 1 || M > STREAM_MAX_M || K < 1 || N < 1 || ldw < K) return 0;
-    const long long fit = rows_that_fit(N, K, ldw);
+    const long long fit = rows_that_fit(M, N, K, ldw);
     if (fit < 1) return 0;
     return (int)((M + fit - 1) / fit);
 }
@@ -1097,13 +1221,13 @@ int pack_group(const Group &all, int first, Group &g) {
     for (; i < all.count; ++i) {
         Problem p = all.prob[i];
         // a sliced problem uses the whole tile-sum scratch: it runs in a launch of its own
-        if (sliced(p.K, p.ldw) && g.count > 0) break;
-        if (g.count == 1 && sliced(g.prob[0].K, g.prob[0].ldw)) break;
+        if (sliced(all.M, p.K, p.ldw) && g.count > 0) break;
+        if (g.count == 1 && sliced(all.M, g.prob[0].K, g.prob[0].ldw)) break;
         int e = 0;
         while (e < g.nx && !(g.xsrc[e].x == p.x && g.xsrc[e].ldx == p.ldx && g.xsrc[e].K == p.K)) ++e;
         if (e == g.nx) {
             const int need = all.M * ((p.K + 7) & ~7);
-            if ((used + need) * 2 > (sliced(p.K, p.ldw) ? STREAM_X_WIDE_BYTES : STREAM_X_BYTES)) break;
+            if ((used + need) * 2 > (sliced(all.M, p.K, p.ldw) ? STREAM_X_WIDE_BYTES : STREAM_X_BYTES)) break;
             g.xsrc[g.nx++] = XSource{p.x, p.ldx, p.K, used};
             used += need;
         }
@@ -1179,15 +1303,16 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
 }
 
 unsigned grid_for(int M, int N, int K, long long ldw, int sm_count) {
-    if (!stream_launches(M, N, K, ldw)) return direct_grid(M, N, sm_count);
+    const int nl = stream_launches(M, N, K, ldw);
+    if (!nl) return direct_grid(M, N, sm_count);
     Group g = {};
     g.count = 1;
-    g.M = 1;
+    g.M = (M + nl - 1) / nl;   // x rows of the first launch
     g.prob[0].N = N;
     g.prob[0].K = K;
     g.prob[0].ldw = ldw;
     plan_units(g, sm_count);
-    const bool hf = half_sm(sliced(K, ldw), (long long)M * (((long long)K + 7) & ~7ll));
+    const bool hf = half_sm(sliced(g.M, K, ldw), (long long)g.M * (((long long)K + 7) & ~7ll));
     return stream_grid(hf, (long long)N * ldw * 2, g.units, sm_count);
 }
 

@@ -39,11 +39,19 @@ constexpr int STREAM_MAX_M = 8;         // x rows: the n8 dimension of the m16n8
 constexpr int STREAM_X_BYTES = 32768;   // shared-memory table of the launch's distinct x rows
 constexpr int STREAM_X_HALF_BYTES = 12288; // the x table of half-SM launches (two CTAs per SM)
 constexpr int STREAM_ROW_BYTES = 16384; // one copy slot
-// A unit of a problem with K <= STREAM_WHOLE_K is whole W rows (as many as fill a slot); above it a
-// unit is one K slice of STREAM_SLICE of a 16-row block, so the 16 W rows of every m16n8k16 MMA are
-// real rows however long K is. Each CTA takes a contiguous range of the block-major unit order and
-// finishes the blocks whose first slice it holds.
+// A unit of a problem with K <= STREAM_WHOLE_K is whole W rows (as many as fill a slot). Above it:
+// * octet units (K <= STREAM_OCTET_MAX_K, M <= STREAM_OCTET_MAX_M, the M x rows within the 32 KB
+//   table): one or two whole W rows, and every m16n8k16 MMA pairs 16 (W row, 256-K tile) rows of A
+//   with 8 consecutive x tiles as the columns of B, so a W element always meets its own x element
+//   and D[i][i % 8] is a 256-K tile sum. Units are independent: no tile sums cross CTAs.
+// * otherwise a unit is one K slice of STREAM_SLICE of a 16-row block, so the 16 W rows of every
+//   m16n8k16 MMA are real rows however long K is. Each CTA takes a contiguous range of the
+//   block-major unit order and finishes the blocks whose first slice it holds.
+// Both compute every tile sum with the same products in the same MMA slots and fold them in K
+// order, so a row's result is the same bits either way.
 constexpr int STREAM_WHOLE_K = 2048;
+constexpr int STREAM_OCTET_MAX_K = 8192;
+constexpr int STREAM_OCTET_MAX_M = 4;
 constexpr int STREAM_SLICE = 512;       // 16 rows x 512 FP16 = one slot; a multiple of the 256-K tile
 constexpr int STREAM_MAX_XTILES = 64;   // sliced launches: M x (256-K tiles) per block buffer
 // Wide sliced launches (x rows beyond 32 KB, e.g. M = 8 at K = 4096): 8 ring slots, a 64 KB x table
@@ -62,7 +70,7 @@ struct Problem {
     int x_off;                          // element offset of this problem's x rows in the x table
     int kslice;                         // 0: whole-row units; else K slice of the 16-row units
     int slices;                         // K slices of a sliced problem (units = blocks x slices)
-    int pad;
+    int octet;                          // 1: long-K whole-row units with the octet MMA mapping
 };
 
 // One distinct x (problems that share x and K share the entry): M rows of K, pitch ldx in
@@ -106,8 +114,9 @@ cudaError_t prepare();
 // launch, or more when the problems' distinct x rows exceed the x table (*launches gets the count).
 cudaError_t launch_group(Group &g, cudaStream_t stream, int sm_count, unsigned *grid_out, unsigned *launches);
 unsigned grid_for(int M, int N, int K, long long ldw, int sm_count);
-// True when a problem of this K streams in K slices (16-row units).
-bool sliced(int K, long long ldw);
+// True when a problem of this K streams in K slices (16-row units) for a batch of M x rows; false
+// for whole-row and octet units.
+bool sliced(int M, int K, long long ldw);
 
 }  // namespace gemv
 }  // namespace b2

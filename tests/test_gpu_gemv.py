@@ -47,13 +47,15 @@ def bits(t, cols):
     return t[:, :cols].cpu().numpy().view(np.uint16)
 
 
-@pytest.mark.parametrize("k", [1, 17, 576, 1000, 1536, 2048, 2056, 4096, 8192])
+@pytest.mark.parametrize("k", [1, 17, 576, 1000, 1536, 2048, 2056, 3000, 4096, 6000, 8192])
 def test_small_m_rows_are_batch_independent_and_within_tolerance(b2, gpu_fd, k):
-    """Rows of M=1, 2, 3 and 8 runs agree bit for bit (each x row's result does not depend on the
-    rest of the batch: M=8 at K=4096 is one wide launch with a 64 KB x table, at K=8192 two launches
-    of 4 rows), in both accumulation modes, with and without bias and HardSigmoid; all rows within
-    tolerance."""
-    n = 300
+    """Rows of M=1, 2, 3, 4 and 8 runs agree bit for bit (each x row's result does not depend on the
+    rest of the batch, nor on the unit kind that serves it: above K = 2048, M <= 4 runs long-K
+    whole-row (octet) units when the x rows fit 32 KB -- two W rows per unit up to K = 4096, one
+    above -- and the other batches 16-row K slices; M=8 at K=4096 is one wide sliced launch with a
+    64 KB x table, at K=8192 two launches of 4 rows), in both accumulation modes, with and without
+    bias and HardSigmoid; all rows within tolerance. N is odd, so a two-row unit ends with one row."""
+    n = 301
     x, w, b = uniform_case(8, n, k, 7000 + k)
     ldx, ldy = r8(k), r8(n)
     xd = dev(x, ldx, fill=float("nan"))          # pitch padding must never be read as data
@@ -62,8 +64,10 @@ def test_small_m_rows_are_batch_independent_and_within_tolerance(b2, gpu_fd, k):
             for bias in (b, None):
                 op = b2.Linear(gpu_fd, 1, k, n, w, bias, post=post, mode=b2.CO_CHAIN, acc=acc, compat=False)
                 info = op.info()
-                assert info.kernel == 1 and info.stages == (11 if k > 2048 else 6)   # M=1: half-SM ring
-                ys = {m: torch.zeros((m, ldy), dtype=torch.float16, device="cuda") for m in (1, 2, 3, 8)}
+                # M=1: half-SM ring while the x row fits its 12 KB table (whole-row and long-K octet
+                # units alike); K = 8192 (16 KB) runs full-SM CTAs with 12 slots
+                assert info.kernel == 1 and info.stages == (12 if k > 6144 else 6)
+                ys = {m: torch.zeros((m, ldy), dtype=torch.float16, device="cuda") for m in (1, 2, 3, 4, 8)}
                 torch.cuda.synchronize()
                 for m, y in ys.items():
                     op.run_device(m, xd.data_ptr(), ldx, y.data_ptr(), ldy)
@@ -71,7 +75,7 @@ def test_small_m_rows_are_batch_independent_and_within_tolerance(b2, gpu_fd, k):
                 assert b2.status(gpu_fd) == 0
                 what = f"k={k} acc={acc} post={post} bias={bias is not None}"
                 full = bits(ys[8], n)
-                for m in (1, 2, 3):
+                for m in (1, 2, 3, 4):
                     assert np.array_equal(full[:m], bits(ys[m], n)), f"{what} m={m}"
                 p = 1 if post == b2.CO_LINEAR_HSIG else 0
                 if acc == b2.ACC_TILE16:
@@ -142,6 +146,14 @@ def test_group_equals_individual_runs_bitwise(b2, gpu_fd, m):
                         [r8(items[i][1]) for i in streamed])
     b2.sync(gpu_fd)
     assert b2.counters()["launches"] - before == expect
+    if m <= 2:
+        # the K=4096 member streams whole rows (octet units) and joins the shared launch: the
+        # 576/1536/4096-wide inputs fit the 32 KB x table together
+        before = b2.counters()["launches"]
+        b2.group_run_device(ops, m, [x.data_ptr() for _, _, _, x in items], [x.shape[1] for _, _, _, x in items],
+                            [y.data_ptr() for y in grp], [r8(n) for _, n, _, _ in items])
+        b2.sync(gpu_fd)
+        assert b2.counters()["launches"] - before == 1
     for op in ops:
         op.destroy()
 
@@ -197,13 +209,16 @@ def test_lm_head_sized_decode_against_oracle(b2, gpu_fd):
 
 @pytest.mark.parametrize("n,k", [(8192, 4096), (16384, 2560), (4100, 11008), (2048, 16384)])
 def test_long_k_blocks_against_oracle(b2, gpu_fd, n, k):
-    """Long-K (sliced) streamed launches at decode sizes, where each CTA finishes most of its 16-row
-    blocks itself and reuses its shared tile-sum buffers (16384 x 2560: about seven blocks per CTA,
-    more than the four buffers), and the blocks at the ends of the CTAs' ranges are completed across
-    CTAs: tile-16 and FP32 results within tolerance of the oracle / FP64, rows of M = 1 and M = 4
-    identical, and repeated launches identical (the block counters return to zero)."""
+    """Long-K streamed launches at decode sizes. K <= 4096: M = 8 streams 16-row K slices (each CTA
+    finishes most of its blocks itself and reuses its shared tile-sum buffers -- 16384 x 2560 gives
+    about seven blocks per CTA, more than the four buffers -- and completes the blocks at the ends of
+    its range across CTAs), while M = 4 (two passes) and M = 1 stream whole rows as octet units; all
+    give the same bits for the same x row. K > 8192 is sliced at every M. Tile-16 and FP32 results
+    within tolerance of the oracle / FP64, repeated launches identical (the block counters return
+    to zero)."""
     rng = np.random.default_rng(n + k)
-    m = 4 if k <= 4096 else 1
+    ms = (8, 4, 1) if k <= 4096 else (1,)
+    m = ms[0]
     x = rng.uniform(-1, 1, (m, k)).astype(np.float16)
     w = rng.uniform(-1 / np.sqrt(k), 1 / np.sqrt(k), (n, k)).astype(np.float16)
     b = rng.uniform(-0.1, 0.1, n).astype(np.float16)
@@ -211,19 +226,21 @@ def test_long_k_blocks_against_oracle(b2, gpu_fd, n, k):
     for acc in (b2.ACC_TILE16, b2.ACC_FP32):
         op = b2.Linear(gpu_fd, 1, k, n, w, b, post=b2.CO_LINEAR_NONE, acc=acc, compat=False)
         info = op.info()
-        assert info.kernel == 1 and info.stages == 11
+        assert info.kernel == 1 and info.stages == (6 if k <= 4096 else 11)   # M=1: octet (half-SM) / sliced
         ldy = r8(n)
         ys = [torch.zeros((m, ldy), dtype=torch.float16, device="cuda") for _ in range(3)]
-        y1 = torch.zeros((1, ldy), dtype=torch.float16, device="cuda")
+        others = {mm: torch.zeros((mm, ldy), dtype=torch.float16, device="cuda") for mm in ms[1:]}
         torch.cuda.synchronize()
         for y in ys:
             op.run_device(m, xd.data_ptr(), k, y.data_ptr(), ldy)
-        op.run_device(1, xd.data_ptr(), k, y1.data_ptr(), ldy)
+        for mm, y in others.items():
+            op.run_device(mm, xd.data_ptr(), k, y.data_ptr(), ldy)
         b2.sync(gpu_fd)
         assert b2.status(gpu_fd) == 0
         assert torch.equal(ys[0].view(torch.int16), ys[1].view(torch.int16))
         assert torch.equal(ys[0].view(torch.int16), ys[2].view(torch.int16))
-        assert torch.equal(ys[0][:1].view(torch.int16), y1.view(torch.int16))
+        for mm, y in others.items():
+            assert torch.equal(ys[0][:mm].view(torch.int16), y.view(torch.int16)), f"n={n} k={k} m={mm}"
         if acc == b2.ACC_TILE16:
             ref = oracle.linear("tile16", x, w, b, post=0)["y16"]
         else:
