@@ -198,7 +198,7 @@ struct SCfg {
     static constexpr uint32_t X_OFFSET = STAGES * STAGE_BYTES;
     static constexpr uint32_t META_OFFSET = X_OFFSET + X_BYTES;
     static constexpr uint32_t BAR_OFFSET = META_OFFSET + STAGES * sizeof(Meta);
-    static constexpr uint32_t ABORT_OFFSET = BAR_OFFSET + 2 * STAGES * 8;
+    static constexpr uint32_t ABORT_OFFSET = BAR_OFFSET + 2 * STAGES * 8;   // [abort flag, x-table-ready flag]
     static constexpr uint32_t PROB_OFFSET = ABORT_OFFSET + 16;
     static constexpr uint32_t BUF_OFFSET = (PROB_OFFSET + PROBS * (uint32_t)sizeof(Problem) + 15u) & ~15u;
     static constexpr uint32_t CTL_OFFSET = BUF_OFFSET + (SL ? B_RING * BUF_FL * 4u : 0u);
@@ -388,9 +388,12 @@ __device__ __forceinline__ void produce(const Group &g, const Problem *prob, uin
     uint32_t ph = 0;
     bool done = !mine, armed = false;
     int q = slot, pi = 0;
+    const int hold = g.hold;
     uint64_t t0 = 0;
     for (uint32_t polls = 1;; ++polls) {
-        if (!done && mbar_test_wait(empty, ph ^ 1u)) {
+        // slots from `hold` on take their first unit once the consumers have the x table
+        const bool held = hold && q == slot && slot >= hold && abort_flag[1] == 0;
+        if (!done && !held && mbar_test_wait(empty, ph ^ 1u)) {
             const long long u = (long long)blockIdx.x + (long long)q * gridDim.x;   // round-robin units
             if (u < (long long)units) {
                 while (pi + 1 < count && u >= prob[pi + 1].unit_begin) ++pi;
@@ -902,7 +905,8 @@ __global__ void __launch_bounds__(SCfg<SL, HF, WX>::THREADS, SCfg<SL, HF, WX>::M
                 mbar_init(full0 + 8 * s, 1);
                 mbar_init(empty0 + 8 * s, 1);
             }
-            *abort_flag = 0;
+            abort_flag[0] = 0;
+            abort_flag[1] = 0;   // x table ready
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         }
         if (SL && lane < B_RING) {
@@ -923,7 +927,10 @@ __global__ void __launch_bounds__(SCfg<SL, HF, WX>::THREADS, SCfg<SL, HF, WX>::M
     asm volatile("bar.sync 2, %0;" ::"r"(C::THREADS) : "memory");   // barriers and problem table ready
     asm volatile("griddepcontrol.wait;" ::: "memory");              // the previous kernel is done
 
-    // The consumer warps fill the x table (x rows, zero past K) while the producer streams W.
+    // The consumer warps fill the x table (x rows, zero past K) while the producer streams W. Every
+    // 16-byte chunk of every source is issued before any is waited for (cp.async, the bytes past K
+    // zero-filled by the copy), so the fill costs one round trip however many inputs the launch has:
+    // these loads queue behind the W stream already in flight.
     {
         const int ct = threadIdx.x - 32, nct = C::STAGES * 32;
         for (int e = 0; e < g.nx; ++e) {
@@ -931,19 +938,16 @@ __global__ void __launch_bounds__(SCfg<SL, HF, WX>::THREADS, SCfg<SL, HF, WX>::M
             const int K8 = (xs.K + 7) & ~7, per_row = K8 / 8;
             for (int i = ct; i < g.M * per_row; i += nct) {
                 const int r = i / per_row, k = (i - r * per_row) * 8;
-                uint4 v = __ldg(reinterpret_cast<const uint4 *>(xs.x + (size_t)r * xs.ldx + k));
-                if (k + 8 > xs.K) {
-                    uint32_t *wv = reinterpret_cast<uint32_t *>(&v);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        if (k + 2 * j >= xs.K) wv[j] = 0u;
-                        else if (k + 2 * j + 1 >= xs.K) wv[j] &= 0x0000ffffu;
-                    }
-                }
-                *reinterpret_cast<uint4 *>(xtab + xs.off + (size_t)r * K8 + k) = v;
+                const uint32_t bytes = (uint32_t)min(8, xs.K - k) * 2u;   // k < K: at least one element
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                                 smem_u32(xtab + xs.off + (size_t)r * K8 + k)),
+                             "l"(xs.x + (size_t)r * xs.ldx + k), "r"(bytes)
+                             : "memory");
             }
         }
+        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
         asm volatile("bar.sync 1, %0;" ::"r"(nct) : "memory");
+        if (threadIdx.x == 32) abort_flag[1] = 1;   // releases the producer slots held back (see Group::hold)
     }
 
     // Consumer warp c owns slot c and takes its units in order (the producer fills slot c with the
@@ -1271,6 +1275,12 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
         for (int i = 0; i < g.count; ++i) wbytes += (long long)g.prob[i].N * g.prob[i].ldw * 2;
         const bool hf = half_sm(sl, xused);
         const unsigned grid = stream_grid(hf, wbytes, g.units, sm_count);
+        // Two half-SM CTAs per SM keep ~28 MB of weights in flight across the GPU, and loads queue
+        // behind them: the x rows the consumers need first would wait ~2-4 us. In those launches
+        // each producer fills half its ring, then the rest once its CTA has the x table (measured:
+        // LM head 12.7 -> 11.6 us, 63.8 MB grouped decode set 15.7 -> 14.4 us, 4096 x 4096 at K =
+        // 4096 9.3 -> 8.8 us; a 7 MB launch with one CTA per SM was slower with it).
+        g.hold = hf && grid > (unsigned)sm_count ? SCfg<false, true>::STAGES / 2 : 0;
         if (grid_out) *grid_out = grid;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
