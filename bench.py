@@ -27,6 +27,8 @@ scaling, one process per GPU).
   cfg1      the fused HardSigmoid at M=64, N=256, K=512 (the reference CLI's operator): device,
             CUDA-graph and end-to-end microseconds, beside the CPU oracle (C port, all threads)
             and the pure-Python form of the reference's file-gate oracle.
+  cube_entry co_linear_run_tiled at 4096^3 with 16 x 16 input cube views and 256 output cubes (the
+            GEMM reads and writes the cubes directly) beside b2_linear_run_device on row-major buffers.
   summary   the key figures of all sections, printed last so that a truncated log keeps them.
   gemm_tile16  the same 4096^3 Linear with the reference's per-256-K FP16 running sum (the
             co_linear_* default numerics), device-resident like `value`.
@@ -359,6 +361,11 @@ def main():
     if rank == 0 and world == 1:
         cfg1 = bench_cfg1(b2, fd, torch, stream, steps)
 
+    # ---------------------------------------------------------------- cube entry (rank 0, N=1 only)
+    cube = None
+    if rank == 0 and world == 1:
+        cube = bench_cube(b2, fd, torch, stream, steps)
+
     line = None
     if rank == 0:
         traffic = traffic_per_launch()
@@ -392,11 +399,13 @@ def main():
             line["gemv"] = gemv
         if shard:
             line["sharded"] = shard
+        if cube:
+            line["cube_entry"] = cube
         if cfg1:
             line["cfg1"] = cfg1
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_sample()
-        line["summary"] = summarize(world, kernel_tflops, e2e_ms, tile16, cfg1, shard, gemv, graph)
+        line["summary"] = summarize(world, kernel_tflops, e2e_ms, tile16, cfg1, shard, gemv, graph, cube)
     b2.close(fd)
     if world > 1:
         dist.barrier()
@@ -412,11 +421,13 @@ def _r(v, digits=4):
     return float(f"{v:.{digits}g}")
 
 
-def summarize(world, kernel_tflops, e2e_ms, tile16, cfg1, shard, gemv, graph):
+def summarize(world, kernel_tflops, e2e_ms, tile16, cfg1, shard, gemv, graph, cube=None):
     """The line's key figures in a few hundred bytes, printed as its last key."""
     out = {"n_gpus": world, "gemm_4096_fp32acc_tflops": _r(kernel_tflops), "e2e_ms": _r(e2e_ms)}
     if tile16:
         out["gemm_4096_tile16_tflops"] = _r(tile16["tflops"])
+    if cube:
+        out["cube_run_tiled_4096_ms"] = {"run_tiled": _r(cube["run_tiled_ms"]), "run_device": _r(cube["run_device_ms"])}
     if cfg1:
         out["cfg1_hsig_64x256x512_us"] = {"device": _r(cfg1["device_us"]), "graph": _r(cfg1["graph_us"]),
                                           "e2e": _r(cfg1["e2e_us"]), "cpu_c_port": _r(cfg1["cpu_c_port_us"]),
@@ -704,6 +715,71 @@ def bench_cfg1(b2, fd, torch, stream, steps):
             "device_tflops": flops / (graph * 1e-3) / 1e12, "worst_err_over_tol_vs_oracle": worst,
             "cpu_c_port_us": c_s * 1e6, "cpu_c_port_threads": threads, "cpu_oracle_literal_s": py_s,
             "cpu_oracle_literal": "pure-Python restatement of cli_gate.oracle (one core)"}
+
+
+def bench_cube(b2, fd, torch, stream, steps):
+    """co_linear_run_tiled at M = N = K = 4096 (the reference's cube entry used by its graph and
+    attention callers: research/custom-ops/src/linear_hardsigmoid.c:325-352): X as 16 x 16 C2=8 cube
+    views of 256 x 256 (co_tensor_matrix), Y as 16 x 16 output cubes, co_linear_create's default
+    numerics. The GEMM reads the input cubes through 3-D tensor maps and writes the output cubes
+    directly; the entry is synchronous (it also checks every caller buffer's guard). Beside it, the
+    same operator on row-major device buffers (b2_linear_run_device), back to back."""
+    import numpy as np
+    m = n = k = 4096
+    rng = np.random.default_rng(12)
+    w = (rng.standard_normal((n, k), np.float32) / 64).astype(np.float16)
+    x = rng.standard_normal((m, k), np.float32).astype(np.float16)
+    op = b2.Linear(fd, m, k, n, w, np.zeros(n, np.float16), post=b2.CO_LINEAR_NONE, mode=b2.CO_CHAIN)
+    t = b2.tensor_matrix(256, 256)
+    xbuf, ybuf = b2.Buffer(fd, 256 * t.bytes), b2.Buffer(fd, 256 * t.bytes)
+    xv = [xbuf.view(t, i * t.bytes) for i in range(256)]     # [m tile][k tile]
+    yv = [ybuf.view(t, i * t.bytes) for i in range(256)]     # [m tile][n tile]
+    for i, v in enumerate(xv):
+        mi, ki = divmod(i, 16)
+        b2.upload(v, np.ascontiguousarray(x[mi * 256:(mi + 1) * 256, ki * 256:(ki + 1) * 256]))
+    xa, ya = b2.views_array(xv), b2.views_array(yv)   # the caller's view arrays, built once
+    run = b2.lib().co_linear_run_tiled
+    for _ in range(3):
+        assert run(op.h, xa, len(xv), ya, len(yv)) == 0
+    reps = max(10, min(steps, 100))
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    before = b2.counters()["launches"]
+    es.record(stream)
+    for _ in range(reps):
+        run(op.h, xa, len(xv), ya, len(yv))
+    ee.record(stream)
+    ee.synchronize()
+    tiled_ms = es.elapsed_time(ee) / reps
+    launches = (b2.counters()["launches"] - before) / reps
+    # device-resident row-major run of the same operator (back to back, one stream)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty(m, n, device="cuda", dtype=torch.float16)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        op.run_device(m, xd.data_ptr(), k, yd.data_ptr(), n)
+    b2.sync(fd)
+    es.record(stream)
+    for _ in range(reps):
+        op.run_device(m, xd.data_ptr(), k, yd.data_ptr(), n)
+    ee.record(stream)
+    ee.synchronize()
+    dev_ms = es.elapsed_time(ee) / reps
+    if b2.status(fd):
+        raise RuntimeError("device status raised in the cube-entry run")
+    # the two entries give the same bytes
+    got = np.empty((m, n), np.float16)
+    for i, v in enumerate(yv):
+        mi, ni = divmod(i, 16)
+        got[mi * 256:(mi + 1) * 256, ni * 256:(ni + 1) * 256] = b2.download(v)
+    if not np.array_equal(got.view(np.uint16), yd.cpu().numpy().view(np.uint16)):
+        raise RuntimeError("cube entry and row-major entry differ")
+    op.destroy()
+    xbuf.free()
+    ybuf.free()
+    return {"m": m, "n": n, "k": k, "views_in": 256, "views_out": 256, "run_tiled_ms": tiled_ms,
+            "run_device_ms": dev_ms, "ratio": tiled_ms / dev_ms, "launches_per_call": launches,
+            "tflops": 2 * m * n * k / (tiled_ms * 1e-3) / 1e12,
+            "numerics": "per-256-K FP16 running sum (co_linear_create default)"}
 
 
 def bench_tile16(b2, fd, torch, stream, peak_tflops, steps):

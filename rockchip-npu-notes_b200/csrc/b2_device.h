@@ -146,6 +146,20 @@ int b2d_cube_to_rowmajor(b2_dev *, const b2k_cube_tile *tiles, unsigned count, v
 int b2d_rowmajor_to_cube(b2_dev *, const void *src, size_t ld, const b2k_cube_tile *tiles,
                          unsigned count);
 
+/* The fused Linear (a->fused, no residual or gate, m > B2D_GEMV_MAX_M) reading X straight from the
+ * caller's C2=8 cube views and writing the output cubes (padding zeroed): the gather/scatter-free
+ * form of the cube entries. in[mb * kviews + kt] holds rows [256 mb, +256) and K [kt * kview_k,
+ * + kview_k) of X (kviews = 1: all of K), its logical cols a multiple of 8; out[mt * ntiles + nt]
+ * is the 256 x 256 output tile (mt, nt). a->x and a->y are ignored. The views' tensor maps are
+ * encoded on the host and copied to a per-handle table before the launch. ROCKET_E_UNSUPPORTED when
+ * the shape or a view does not qualify (the caller then gathers and scatters). */
+#define B2D_CUBE_MAX_VIEWS 256u
+typedef struct {
+    const b2k_cube_tile *in; unsigned nin, kviews, kview_k;
+    const b2k_cube_tile *out; unsigned nout, ntiles;
+} b2k_cube_io;
+int b2d_linear_cube(b2_dev *, const b2k_linear *a, const b2k_cube_io *io, unsigned *launches);
+
 /* ---------------------------------------------------------------------- peer memory (CUDA IPC) */
 #define B2D_IPC_HANDLE_BYTES 64
 /* Exports a b2d_malloc'ed allocation for other processes on this node. */

@@ -29,6 +29,11 @@ struct b2_dev {
     unsigned *flags_dev;    // the same words as seen by kernels
     b2::gemv::Scratch gemv; // tile sums and block counters of long-K small-M launches
     __half *gate_table;     // SiLU / GELU gates of every FP16 input (common.cuh)
+    // cube entries: tensor maps of the input views and the output tile table (first use allocates)
+    void *cube_dev;         // device copy: [B2D_CUBE_MAX_VIEWS] CUtensorMap, then [..] CubeOut
+    void *cube_host;        // pinned staging of the same bytes (= what the device copy holds)
+    b2k_cube_tile *cube_key;   // [B2D_CUBE_MAX_VIEWS] the input view each device map describes
+    unsigned cube_maps, cube_outs;   // slots the device copy holds valid contents for
 };
 
 namespace {
@@ -132,6 +137,9 @@ void b2d_close(b2_dev *d) {
     cudaFree(d->gemv.tsum);
     cudaFree(d->gemv.tcount);
     cudaFree(d->gate_table);
+    if (d->cube_dev) cudaFree(d->cube_dev);
+    if (d->cube_host) cudaFreeHost(d->cube_host);
+    free(d->cube_key);
     delete d;
 }
 
@@ -382,6 +390,112 @@ int b2d_linear(b2_dev *d, const b2k_linear *a, unsigned *launches) {
         if (e != cudaSuccess) return rc_of(e);
         *launches += 1;
     }
+    return 0;
+}
+
+int b2d_linear_cube(b2_dev *d, const b2k_linear *a, const b2k_cube_io *io, unsigned *launches) {
+    *launches = 0;
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (!a || !io || !io->in || !io->out || !a->w || a->ldw % 8 || !aligned16(a->w) || a->ldw < a->k)
+        return ROCKET_E_SHAPE;
+    if (a->m <= B2D_GEMV_MAX_M || !a->fused || a->raw_only || a->res || a->gate || !io->kviews || !io->ntiles ||
+        io->nin > B2D_CUBE_MAX_VIEWS || io->nout > B2D_CUBE_MAX_VIEWS || io->nin % io->kviews ||
+        io->nout % io->ntiles || io->kview_k % b2::gemm::TILE_K)
+        return ROCKET_E_UNSUPPORTED;
+    constexpr size_t MAPS = B2D_CUBE_MAX_VIEWS * sizeof(CUtensorMap);
+    constexpr size_t OUTS = B2D_CUBE_MAX_VIEWS * sizeof(b2::gemm::CubeOut);
+    constexpr size_t BYTES = MAPS + OUTS + B2D_CUBE_MAX_VIEWS;   // + one octet flag per map
+    if (!d->cube_dev) {
+        if (cudaMalloc(&d->cube_dev, BYTES) != cudaSuccess) {
+            cudaGetLastError();
+            d->cube_dev = nullptr;
+            return ROCKET_E_NOMEM;
+        }
+    }
+    if (!d->cube_host) {
+        if (cudaHostAlloc(&d->cube_host, BYTES, cudaHostAllocDefault) != cudaSuccess) {
+            cudaGetLastError();
+            d->cube_host = nullptr;
+            return ROCKET_E_NOMEM;
+        }
+    }
+    if (!d->cube_key) {
+        d->cube_key = static_cast<b2k_cube_tile *>(calloc(B2D_CUBE_MAX_VIEWS, sizeof(b2k_cube_tile)));
+        if (!d->cube_key) return ROCKET_E_NOMEM;
+    }
+    // The tables of the previous call stay on the device: a map or an output entry is re-encoded and
+    // the tables copied again only when a view differs (callers typically reuse their views, and
+    // encoding 256 maps costs more host time than the GEMM).
+    CUtensorMap *maps = static_cast<CUtensorMap *>(d->cube_host);
+    b2::gemm::CubeOut *outs = reinterpret_cast<b2::gemm::CubeOut *>(static_cast<char *>(d->cube_host) + MAPS);
+    unsigned char *octs = static_cast<unsigned char *>(d->cube_host) + MAPS + OUTS;
+    bool same_in = io->nin <= d->cube_maps, same_out = io->nout <= d->cube_outs;
+    for (unsigned i = 0; same_in && i < io->nin; ++i) {
+        const b2k_cube_tile &t = io->in[i], &k = d->cube_key[i];
+        same_in = t.ptr == k.ptr && t.rows == k.rows && t.cols == k.cols && t.physical_rows == k.physical_rows;
+    }
+    for (unsigned i = 0; same_out && i < io->nout; ++i) {
+        const b2k_cube_tile &t = io->out[i];
+        const b2::gemm::CubeOut &o = outs[i];
+        same_out = o.ptr == t.ptr && o.prow == (int)t.physical_rows && o.rows == (int)t.rows && o.cols == (int)t.cols &&
+                   o.pcols == (int)t.physical_cols;
+    }
+    if (!same_in || !same_out) {
+        // the staging is rewritten only once the previous cube launch's copy of it has completed
+        if (cudaStreamSynchronize(d->stream) != cudaSuccess) return ROCKET_E_DEVICE;
+        d->cube_maps = d->cube_outs = 0;   // the device copy is stale until the copies below are queued
+    }
+    if (!same_in) {
+        for (unsigned i = 0; i < io->nin; ++i) {
+            const b2k_cube_tile &t = io->in[i];
+            int oct = 0;
+            if (t.cols % 8 || !b2::gemm::make_cube_map(&maps[i], t.ptr, t.rows, t.physical_rows, t.cols, &oct))
+                return ROCKET_E_UNSUPPORTED;
+            octs[i] = (unsigned char)oct;
+            d->cube_key[i] = t;
+        }
+    }
+    if (!same_out) {
+        for (unsigned i = 0; i < io->nout; ++i) {
+            const b2k_cube_tile &t = io->out[i];
+            if (!aligned16(t.ptr) || t.physical_rows < t.rows || t.physical_cols < t.cols || t.physical_cols % 8)
+                return ROCKET_E_UNSUPPORTED;
+            outs[i] = b2::gemm::CubeOut{static_cast<__half *>(t.ptr), (int)t.physical_rows, (int)t.rows,
+                                        (int)t.cols, (int)t.physical_cols, {0, 0}};
+        }
+    }
+    if (!same_in || !same_out) {
+        // both tables again (the other one was left stale above)
+        cudaError_t e = cudaMemcpyAsync(d->cube_dev, d->cube_host, io->nin * sizeof(CUtensorMap),
+                                        cudaMemcpyHostToDevice, d->stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(static_cast<char *>(d->cube_dev) + MAPS + OUTS, octs, io->nin, cudaMemcpyHostToDevice,
+                                d->stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(static_cast<char *>(d->cube_dev) + MAPS, outs, io->nout * sizeof(b2::gemm::CubeOut),
+                                cudaMemcpyHostToDevice, d->stream);
+        if (e != cudaSuccess) return rc_of(e);
+        d->cube_maps = io->nin;
+        d->cube_outs = io->nout;
+    }
+    cudaError_t e;
+    b2::gemm::Params p = {};
+    p.M = (int)a->m; p.N = (int)a->n; p.K = (int)a->k;
+    p.bias = static_cast<const __half *>(a->bias);
+    p.out_mode = b2::gemm::OUT_FINAL;
+    p.post = a->post;
+    p.fold = a->acc == 0 ? 1 : 0;
+    p.flags = d->flags_dev;
+    p.a_maps = static_cast<const CUtensorMap *>(d->cube_dev);
+    p.a_octets = static_cast<const unsigned char *>(d->cube_dev) + MAPS + OUTS;
+    p.a_kviews = (int)io->kviews;
+    p.a_kview_k = (int)io->kview_k;
+    p.y_cube = reinterpret_cast<const b2::gemm::CubeOut *>(static_cast<const char *>(d->cube_dev) + MAPS);
+    p.y_cube_nt = (int)io->ntiles;
+    b2::gemm::Shape s = {nullptr, 0, a->w, a->ldw};
+    e = b2::gemm::launch(s, p, d->stream, d->ordinal, d->sm_count, nullptr);
+    if (e != cudaSuccess) return rc_of(e);
+    *launches = 1;
     return 0;
 }
 

@@ -108,6 +108,30 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
             : "memory");
     }
 }
+// One 3-D box of a cube view's map (8 channels x 128 rows x 8 channel groups) into shared memory.
+template <int CG>
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1,
+                                            int c2) {
+    if constexpr (CG == 2) {
+        asm volatile(
+            "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+            " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+            "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+            : "memory");
+    } else {
+        asm volatile(
+            "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+            " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+            "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+            : "memory");
+    }
+}
+// A tensor map in global memory that the host rewrote since the last launch: the tensormap proxy
+// must not use a copy of its old contents.
+__device__ __forceinline__ void tmap_acquire(const CUtensorMap *map) {
+    asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(reinterpret_cast<uint64_t>(map))
+                 : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -209,6 +233,15 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
+
+// Shared-memory matrix descriptor of a cube stage: K-major without swizzle, [8 channel groups][128
+// rows][8] FP16, i.e. 8-row x 16-byte core matrices 128 bytes apart along M (SBO) and 2048 bytes
+// apart along K (LBO); version 1, base offset 0. One K = 16 step advances the start by 4096 bytes.
+__device__ __forceinline__ uint64_t cube_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(2048 >> 4) << 16) | ((uint64_t)(128 >> 4) << 32) |
+           ((uint64_t)1 << 46);
+}
+constexpr uint32_t CUBE_K16_STEP = 4096 >> 4;   // descriptor units (16 bytes) per K = 16 step
 
 __device__ __forceinline__ float load_bias(const __half *bias, int col, int n) {
     return (bias && col < n) ? __half2float(bias[col]) : 0.0f;
@@ -404,6 +437,34 @@ __device__ __forceinline__ void release_acc(int lane, uint32_t tempty_leader, ui
 // M and columns past n_out are clipped by the tensor map). Otherwise each thread stores its row.
 __device__ __forceinline__ void store_out(const Params &p, const CUtensorMap *tmap_y, uint32_t stage, int lane,
                                           int row, bool row_ok, int x, int n_out, const uint32_t (&pk)[16]) {
+    if (p.y_cube) {
+        // The tile's output cube: this thread's row, four 16-byte atoms (32 columns); consecutive lanes
+        // are consecutive rows, so each atom store of the warp is 512 contiguous bytes. Padding rows
+        // and columns of the cube receive zeros (the caller's cube must not keep stale values there).
+        const CubeOut o = p.y_cube[(row >> 8) * p.y_cube_nt + (x >> 8)];
+        const int r = row & 255, c0 = x & 255;
+        if (r >= o.prow) return;
+        const bool live = r < o.rows;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int a = (c0 >> 3) + q, keep = o.cols - 8 * a;   // channels of atom a inside the tile
+            if (8 * a >= o.pcols) break;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (live && keep > 0) {
+                v = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+                if (keep < 8) {
+                    uint32_t *w = reinterpret_cast<uint32_t *>(&v);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (2 * j >= keep) w[j] = 0u;
+                        else if (2 * j + 1 >= keep) w[j] &= 0x0000ffffu;
+                    }
+                }
+            }
+            *reinterpret_cast<uint4 *>(o.ptr + ((size_t)a * o.prow + r) * 8) = v;
+        }
+        return;
+    }
     if (p.tma_y) {
         if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // box free again
         __syncwarp();
@@ -727,7 +788,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        prefetch_tmap(&tmap_a);
+        if (!p.a_maps) prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
         if (p.tma_y) prefetch_tmap(&tmap_y);
     }
@@ -747,6 +808,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             // ------------------------------------------------------------------ TMA producer
             uint32_t issued = 0;
             bool ok = true;
+            const CUtensorMap *a_map_seen = nullptr;
+            int a_oct = 0;
             for (int tile = cluster_id; ok && tile < p.num_tiles; tile += num_clusters) {
                 int mb, nb;
                 tile_coords(tile, p, mb, nb);
@@ -757,7 +820,22 @@ __global__ void __launch_bounds__(THREADS, 1)
                     uint32_t full_bar = full0 + 8 * s;
                     if constexpr (CG == 2) full_bar = map_to_rank(full_bar, 0);
                     if (rank == 0) mbar_arrive_expect_tx(full0 + 8 * s, C::STAGE_BYTES * CG);
-                    tma_load_2d<CG>(smem_u32(sA + s * C::A_BYTES), &tmap_a, full_bar, kb * BK, row_a);
+                    if (p.a_maps) {
+                        // X from the caller's cube view of this row band and K range (box rows past the
+                        // view's rows and channel groups past its K arrive as zeros)
+                        const int k = kb * BK;
+                        const size_t view = (size_t)(row_a >> 8) * p.a_kviews + k / p.a_kview_k;
+                        const CUtensorMap *am = p.a_maps + view;
+                        if (am != a_map_seen) {
+                            tmap_acquire(am);
+                            a_map_seen = am;
+                            a_oct = p.a_octets[view];
+                        }
+                        tma_load_3d<CG>(smem_u32(sA + s * C::A_BYTES), am, full_bar, 0,
+                                        a_oct ? (row_a & 255) >> 3 : row_a & 255, (k % p.a_kview_k) / 8);
+                    } else {
+                        tma_load_2d<CG>(smem_u32(sA + s * C::A_BYTES), &tmap_a, full_bar, kb * BK, row_a);
+                    }
                     tma_load_2d<CG>(smem_u32(sB + s * C::B_BYTES), &tmap_b, full_bar, kb * BK, row_b);
                     ++issued;
                 }
@@ -774,6 +852,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             // ------------------------------------------------------------------ MMA issuer
             uint32_t consumed = 0, acc_used = 0;
             bool ok = true;
+            const bool cube_a = p.a_maps != nullptr;
             for (int tile = cluster_id; ok && tile < p.num_tiles; tile += num_clusters) {
                 for (int c = 0; ok && c < nchunks; ++c) {
                     const uint32_t acc = acc_used & 1u, acc_ph = (acc_used >> 1) & 1u;
@@ -786,11 +865,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const uint32_t s = consumed % C::STAGES, ph = (consumed / C::STAGES) & 1u;
                         if (!wait_phase(full0 + 8 * s, ph, abort_flag, p.flags)) { ok = false; break; }
                         tc_fence_after();
-                        const uint64_t adesc = sw128_desc(smem_u32(sA + s * C::A_BYTES));
+                        const uint64_t adesc = cube_a ? cube_desc(smem_u32(sA + s * C::A_BYTES))
+                                                      : sw128_desc(smem_u32(sA + s * C::A_BYTES));
                         const uint64_t bdesc = sw128_desc(smem_u32(sB + s * C::B_BYTES));
+                        const uint32_t astep = cube_a ? CUBE_K16_STEP : 2u;
 #pragma unroll
-                        for (int k = 0; k < BK / 16; ++k)   // +32 bytes along K = +2 in the desc
-                            umma_f16<CG>(d_tmem, adesc + 2 * k, bdesc + 2 * k, C::IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+                        for (int k = 0; k < BK / 16; ++k)   // swizzled: +32 bytes along K = +2 in the desc
+                            umma_f16<CG>(d_tmem, adesc + astep * k, bdesc + 2 * k, C::IDESC,
+                                         (kb > kb0 || k > 0) ? 1u : 0u);
                         umma_commit<CG>(empty0 + 8 * s);
                         ++consumed;
                     }
@@ -853,6 +935,20 @@ static bool make_map(CUtensorMap *map, const void *ptr, uint64_t inner, uint64_t
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+
+bool make_cube_map(CUtensorMap *map, const void *ptr, unsigned rows, unsigned prow, unsigned cols, int *octets) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc || !rows || prow < rows || !cols || cols % 8 || (reinterpret_cast<uintptr_t>(ptr) & 15)) return false;
+    const bool oct = rows % 8 == 0;
+    cuuint64_t dims[3] = {oct ? 64u : 8u, oct ? rows / 8 : rows, cols / 8};
+    cuuint64_t strides[2] = {oct ? 128u : 16u, (cuuint64_t)prow * 16};
+    cuuint32_t box[3] = {oct ? 64u : 8u, oct ? 16u : 128u, 8};
+    cuuint32_t estr[3] = {1, 1, 1};
+    *octets = oct ? 1 : 0;
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(ptr), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 template <int CG, int TN, int MODE>
 static cudaError_t set_smem_attr() {
@@ -1004,8 +1100,12 @@ static cudaError_t launch_tile(const Shape &s, Params p, cudaStream_t stream, in
     using C = Cfg<CG, TN>;
     if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
     CUtensorMap ta, tb;
-    if (!make_map(&ta, s.x, (uint64_t)p.K, (uint64_t)p.M, s.ldx, 128) ||
+    memset(&ta, 0, sizeof(ta));   // unused when X comes from cube views (p.a_maps)
+    if ((!p.a_maps && !make_map(&ta, s.x, (uint64_t)p.K, (uint64_t)p.M, s.ldx, 128)) ||
         !make_map(&tb, s.w, (uint64_t)p.K, (uint64_t)p.N, s.ldw, C::B_ROWS))
+        return cudaErrorInvalidValue;
+    if ((p.a_maps || p.y_cube) && (p.out_mode != OUT_FINAL || p.gate || p.res || p.route_rows ||
+                                   (p.a_maps && (p.a_kviews < 1 || p.a_kview_k < BK || p.a_kview_k % BK))))
         return cudaErrorInvalidValue;
     p.num_m_blocks = (p.M + C::BM - 1) / C::BM;
     p.num_n_blocks = (p.N + TN - 1) / TN;

@@ -1,5 +1,6 @@
 // gemm_sm100.h -- parameters and host launcher of the tcgen05 GEMM (gemm_sm100.cu).
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -14,6 +15,15 @@ enum OutMode : int {
 };
 
 constexpr int ROUTE_MAX = 8;   // ranks a routed raw output can address
+
+// Output tile of the cube store (the device-cube entries): the caller's C2=8 cube holding rows x cols
+// of the 256 x 256 output tile (mt, nt), element (r, c) at ptr + ((c / 8) * prow + r) * 8 + c % 8;
+// rows [rows, prow) and columns [cols, pcols) of the cube are padding and receive zeros.
+struct CubeOut {
+    __half *ptr;
+    int prow, rows, cols, pcols;
+    int pad[2];
+};
 
 struct Params {
     int M, N, K;
@@ -48,6 +58,17 @@ struct Params {
     const __half *bias2;
     const __half *gate_table;    // the gate of every FP16 input (common.cuh GATE_TABLE_ENTRIES)
     int tma_y;                   // FP16 output stored through TMA tile stores (set by the launcher)
+    // Cube operands (the device-cube entries; OUT_FINAL only). With a_maps, X comes from the caller's
+    // C2=8 cube views: a_maps (global memory, 64-byte aligned) holds one 3-D tensor map per view
+    // (make_cube_map), view (row / 256) * a_kviews + k / a_kview_k holding rows [256 (row / 256), +256)
+    // and K [k - k % a_kview_k, + a_kview_k) of X; shared memory receives [8 channel groups][128
+    // rows][8] without swizzle. With y_cube (global memory, [M bands of 256][y_cube_nt]), each output
+    // tile goes to its cube, padding included, and y is not written.
+    const CUtensorMap *a_maps;
+    const unsigned char *a_octets;   // [views] 1: the map addresses rows in octets (make_cube_map)
+    int a_kviews, a_kview_k;
+    const CubeOut *y_cube;
+    int y_cube_nt;
 };
 
 struct Shape {
@@ -65,6 +86,13 @@ cudaError_t launch(const Shape &s, Params p, cudaStream_t stream, int device, in
 // A specific variant: cg CTAs per cluster (1 = 128x256 tiles, 2 = 256x256 tiles per CTA pair).
 cudaError_t launch_variant(int cg, const Shape &s, const Params &p, cudaStream_t stream, int device,
                            int sm_count, unsigned *grid_out);
+// 3-D tensor map of a C2=8 FP16 cube view for Params::a_maps: rows x cols logical (cols % 8 == 0),
+// prow physical rows, no swizzle, zeros outside the logical extent. When rows % 8 == 0 the map is
+// (64 = 8 rows x 8 channels, rows / 8 row octets, cols / 8 groups) with box 64 x 16 x 8, so every
+// request is 128 contiguous bytes (*octets = 1); otherwise (8 channels, rows, groups) with box
+// 8 x 128 x 8 (16-byte requests). Both land [8 groups][128 rows][8] in shared memory. False when
+// the view cannot be described.
+bool make_cube_map(CUtensorMap *map, const void *ptr, unsigned rows, unsigned prow, unsigned cols, int *octets);
 // Runs the launchers' one-time device setup (tensor-map encoder lookup, shared-memory limits,
 // co-resident cluster counts) now, so that a later launch issues no such call (a launch recorded
 // into a CUDA graph must not).

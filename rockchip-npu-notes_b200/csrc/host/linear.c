@@ -221,10 +221,41 @@ static int compatible(const co_view *v, const co_tensor *want, int fd) {
            a->bytes == want->bytes;
 }
 
-/* Address-range overlap, also across separate co_buffer wrappers of the same allocation. */
-static int overlap(const co_view *a, const co_view *b) {
-    uintptr_t pa = (uintptr_t)view_ptr(a), pb = (uintptr_t)view_ptr(b);
-    return pa < pb + b->tensor.bytes && pb < pa + a->tensor.bytes;
+/* Aliasing rule of the cube entries: no output view may share a byte with an input view or another
+ * output view (inputs may share bytes with each other); address ranges are compared, so separate
+ * co_buffer wrappers of one allocation are caught too. The ranges are sorted by start and swept
+ * once, keeping the furthest end of every range and of the output ranges seen so far: a range
+ * overlaps an earlier one exactly when it starts before that earlier range's end. */
+typedef struct {
+    uintptr_t start, end;
+    int output;
+} view_range;
+
+static int by_start(const void *a, const void *b) {
+    uintptr_t x = ((const view_range *)a)->start, y = ((const view_range *)b)->start;
+    return x < y ? -1 : x > y;
+}
+
+static int outputs_alias(const co_view *x, unsigned nx, const co_view *y, unsigned ny, int *nomem) {
+    view_range *r = malloc(sizeof(*r) * (nx + ny));
+    *nomem = !r;
+    if (!r) return 0;
+    for (unsigned i = 0; i < nx + ny; i++) {
+        const co_view *v = i < nx ? &x[i] : &y[i - nx];
+        r[i].start = (uintptr_t)view_ptr(v);
+        r[i].end = r[i].start + v->tensor.bytes;
+        r[i].output = i >= nx;
+    }
+    qsort(r, nx + ny, sizeof(*r), by_start);
+    uintptr_t end_all = 0, end_out = 0;
+    int alias = 0;
+    for (unsigned i = 0; i < nx + ny && !alias; i++) {
+        alias = r[i].start < (r[i].output ? end_all : end_out);
+        if (r[i].end > end_all) end_all = r[i].end;
+        if (r[i].output && r[i].end > end_out) end_out = r[i].end;
+    }
+    free(r);
+    return alias;
 }
 
 static unsigned tile_extent(unsigned total, unsigned i) {
@@ -288,21 +319,45 @@ static int guard_views(b2_dev *d, const co_view *a, unsigned na, const co_view *
     return 0;
 }
 
-/* Shared tail of the cube entries: gather -> GEMM -> scatter -> guard check -> status. */
-static int run_cube_tiles(co_linear_hsig *c, const b2k_cube_tile *in, unsigned nin,
-                          const b2k_cube_tile *out, unsigned nout, const co_view *xv, unsigned nx,
-                          const co_view *yv, unsigned ny) {
+/* Shared tail of the cube entries: the GEMM straight from the input cubes into the output cubes
+ * (b2d_linear_cube) where the operator and the views allow it, else gather -> GEMM -> scatter; then
+ * the guard check and the status. in[] holds kviews views per 256-row band, each kview_k columns. */
+static int run_cube_tiles(co_linear_hsig *c, const b2k_cube_tile *in, unsigned nin, unsigned kviews,
+                          unsigned kview_k, const b2k_cube_tile *out, unsigned nout, const co_view *xv,
+                          unsigned nx, const co_view *yv, unsigned ny) {
     b2_dev *d = b2h_dev(c->fd);
     unsigned launches = 0, l = 0;
     int rc = b2d_sync(d);
     if (rc) return rc;
     uint32_t prior = b2d_status(d, 1);
-    rc = gather(d, in, nin, c->x, c->ldx, &launches);
-    if (!rc) {
-        rc = launch_linear(c, c->plan.m, c->x, c->ldx, c->y, c->ldy, &l);
-        launches += l;
+    /* direct: the fused arm of a GEMM-sized operator, every input view a whole number of 8-channel
+     * atoms (a partial atom's unused channels would be read as data) */
+    int direct = c->mode == CO_CHAIN && c->plan.m > B2D_GEMV_MAX_M && nin <= B2D_CUBE_MAX_VIEWS &&
+                 nout <= B2D_CUBE_MAX_VIEWS;
+    for (unsigned i = 0; direct && i < nin; i++) direct = in[i].cols % 8 == 0;
+    int fallback = !direct;
+    if (direct) {
+        if (b2h_fault(B2_FAULT_LAUNCH)) {
+            rc = ROCKET_E_DEVICE;
+        } else {
+            b2k_linear a = {.m = c->plan.m, .n = c->plan.n, .k = c->plan.k, .w = c->w, .ldw = c->ldw,
+                            .bias = c->bias, .post = c->post == CO_LINEAR_HSIG, .acc = (int)c->acc,
+                            .fused = 1};
+            b2k_cube_io io = {in, nin, kviews, kview_k, out, nout, c->plan.ntiles};
+            rc = b2d_linear_cube(d, &a, &io, &l);
+            launches += l;
+            fallback = rc == ROCKET_E_UNSUPPORTED;
+            if (fallback) rc = 0;
+        }
     }
-    if (!rc) rc = scatter(d, c->y, c->ldy, out, nout, &launches);
+    if (fallback) {
+        rc = gather(d, in, nin, c->x, c->ldx, &launches);
+        if (!rc) {
+            rc = launch_linear(c, c->plan.m, c->x, c->ldx, c->y, c->ldy, &l);
+            launches += l;
+        }
+        if (!rc) rc = scatter(d, c->y, c->ldy, out, nout, &launches);
+    }
     if (!rc) rc = guard_views(d, xv, nx, yv, ny, &launches);
     int sync_rc = b2d_sync(d);
     if (!rc) rc = sync_rc;
@@ -327,14 +382,15 @@ int co_linear_hsig_run_tiles(co_linear_hsig *c, const co_view *x, unsigned nx, c
         if (co_tensor_matrix(&want, tile_extent(c->plan.m, i / nt), tile_extent(c->plan.n, i % nt), CO_F16) ||
             !compatible(&y[i], &want, c->fd))
             return ROCKET_E_SHAPE;
-        for (unsigned j = 0; j < nx; j++) if (overlap(&x[j], &y[i])) return ROCKET_E_SHAPE;
-        for (unsigned j = 0; j < i; j++) if (overlap(&y[j], &y[i])) return ROCKET_E_SHAPE;
     }
+    int nomem = 0;
+    if (outputs_alias(x, nx, y, ny, &nomem)) return ROCKET_E_SHAPE;
+    if (nomem) return ROCKET_E_NOMEM;
     b2k_cube_tile *in = malloc(sizeof(*in) * nx), *out = malloc(sizeof(*out) * ny);
     if (!in || !out) { free(in); free(out); return ROCKET_E_NOMEM; }
     for (unsigned mi = 0; mi < nx; mi++) in[mi] = cube_tile(&x[mi], mi * 256, 0);
     for (unsigned i = 0; i < ny; i++) out[i] = cube_tile(&y[i], (i / nt) * 256, (i % nt) * 256);
-    int rc = run_cube_tiles(c, in, nx, out, ny, x, nx, y, ny);
+    int rc = run_cube_tiles(c, in, nx, 1, b2h_round_up(k, 64), out, ny, x, nx, y, ny);
     free(in);
     free(out);
     return rc;
@@ -361,14 +417,15 @@ int co_linear_run_tiled(co_linear *c, const co_view *x, unsigned nx, const co_vi
         if (co_tensor_matrix(&want, tile_extent(c->plan.m, i / nt), tile_extent(c->plan.n, i % nt), CO_F16) ||
             !compatible(&y[i], &want, c->fd))
             return ROCKET_E_SHAPE;
-        for (unsigned j = 0; j < nx; j++) if (overlap(&x[j], &y[i])) return ROCKET_E_SHAPE;
-        for (unsigned j = 0; j < i; j++) if (overlap(&y[j], &y[i])) return ROCKET_E_SHAPE;
     }
+    int nomem = 0;
+    if (outputs_alias(x, nx, y, ny, &nomem)) return ROCKET_E_SHAPE;
+    if (nomem) return ROCKET_E_NOMEM;
     b2k_cube_tile *in = malloc(sizeof(*in) * nx), *out = malloc(sizeof(*out) * ny);
     if (!in || !out) { free(in); free(out); return ROCKET_E_NOMEM; }
     for (unsigned i = 0; i < nx; i++) in[i] = cube_tile(&x[i], (i / kt) * 256, (i % kt) * CO_K_TILE);
     for (unsigned i = 0; i < ny; i++) out[i] = cube_tile(&y[i], (i / nt) * 256, (i % nt) * 256);
-    int rc = run_cube_tiles(c, in, nx, out, ny, x, nx, y, ny);
+    int rc = run_cube_tiles(c, in, nx, kt, CO_K_TILE, out, ny, x, nx, y, ny);
     free(in);
     free(out);
     return rc;

@@ -207,6 +207,45 @@ static void test_cube_entry_and_guard(int fd) {
     CHECK(co_download(&vy, y) == 0, "download");
     CHECK(memcmp(y, ref, (size_t)m * n * 2) == 0, "cube entry equals the reference arithmetic");
     CHECK(co_guard_check(&by) == 0, "guard intact");
+    /* a refused launch on the direct cube path: ROCKET_E_DEVICE, then the next run succeeds */
+    b2_fault_inject(B2_FAULT_LAUNCH, 1);
+    CHECK(co_linear_hsig_run_cube(op, vx, vy) == ROCKET_E_DEVICE, "cube launch fault");
+    CHECK(co_linear_hsig_run_cube(op, vx, vy) == 0, "cube runs again after the fault");
+    /* K = 100 leaves a partial 8-channel atom: the gather -> GEMM -> scatter form, same arithmetic */
+    {
+        const unsigned k2 = 100;
+        uint16_t *x2 = alloc16((size_t)m * k2), *w2 = alloc16((size_t)n * k2), *ref2 = alloc16((size_t)m * n);
+        fill(x2, (size_t)m * k2, 1.0);
+        fill(w2, (size_t)n * k2, 0.1);
+        CHECK(oracle_linear(TILE16_EXACT, m, k2, n, x2, w2, b, 1, ref2, NULL, NULL, 1) == 0, "oracle cube k=100");
+        co_linear_hsig *op2 = NULL;
+        CHECK(co_linear_hsig_create(fd, m, k2, n, (const _Float16 *)w2, (const _Float16 *)b, CO_CHAIN, &op2) == 0,
+              "create k=100");
+        co_tensor tx2;
+        co_buffer bx2;
+        co_view vx2;
+        CHECK(co_tensor_input(&tx2, m, k2) == 0 && co_buffer_alloc(fd, tx2.bytes, &bx2) == 0 &&
+                  co_view_init(&vx2, &bx2, 0, &tx2) == 0 && co_upload_f16(&vx2, (const _Float16 *)x2) == 0,
+              "k=100 input view");
+        CHECK(co_linear_hsig_run_cube(op2, vx2, vy) == 0, "run cube k=100");
+        CHECK(co_download(&vy, y) == 0 && memcmp(y, ref2, (size_t)m * n * 2) == 0,
+              "ragged-K cube entry equals the reference arithmetic");
+        co_buffer_free(&bx2);
+        co_linear_hsig_destroy(op2);
+        free(x2); free(w2); free(ref2);
+    }
+    /* aliasing: an output sharing bytes with the input is refused before any launch; inputs may
+     * share bytes with each other (run_tiled: two K-tile views of one matrix buffer) */
+    {
+        co_view bad = vy;
+        bad.buffer = &bx;
+        bad.offset = 0;
+        co_tensor tyy;
+        CHECK(co_tensor_matrix(&tyy, m, n, CO_F16) == 0, "alias descriptor");
+        bad.tensor = tyy;
+        CHECK(bx.payload >= tyy.bytes, "alias view fits");
+        CHECK(co_linear_hsig_run_cube(op, vx, bad) == ROCKET_E_SHAPE, "output over the input refused");
+    }
     /* a byte of the output buffer's slack is damaged: the run reports it */
     ((unsigned char *)by.bo.ptr)[by.payload + 5] = 1;
     CHECK(co_linear_hsig_run_cube(op, vx, vy) == ROCKET_E_DEVICE, "damaged slack -> DEVICE");

@@ -280,6 +280,41 @@ int b2d_rowmajor_to_cube(b2_dev *d, const void *src, size_t ld, const b2k_cube_t
 }
 
 static float noalloc_scratch[B2D_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+/* The direct cube GEMM: the same gather -> fused Linear -> scatter on the CPU, with the device's
+ * eligibility rules, so the host layer's choice between the two forms is tested without a GPU. */
+int b2d_linear_cube(b2_dev *d, const b2k_linear *a, const b2k_cube_io *io, unsigned *launches) {
+    *launches = 0;
+    if (!d || !a || !io || !io->in || !io->out) return ROCKET_E_SHAPE;
+    if (a->m <= B2D_GEMV_MAX_M || !a->fused || a->raw_only || a->res || a->gate || !io->kviews || !io->ntiles ||
+        io->nin > B2D_CUBE_MAX_VIEWS || io->nout > B2D_CUBE_MAX_VIEWS || io->nin % io->kviews ||
+        io->nout % io->ntiles || io->kview_k % 64)
+        return ROCKET_E_UNSUPPORTED;
+    for (unsigned i = 0; i < io->nin; i++)
+        if (io->in[i].cols % 8) return ROCKET_E_UNSUPPORTED;
+    const size_t ldx = (a->k + 7) / 8 * 8, ldy = (a->n + 7) / 8 * 8;
+    uint16_t *x = calloc((size_t)a->m * ldx, 2), *y = calloc((size_t)a->m * ldy, 2);
+    int rc = x && y ? 0 : ROCKET_E_NOMEM;
+    for (unsigned i = 0; !rc && i < io->nin; i += B2K_MAX_CUBE_TILES) {
+        unsigned n = io->nin - i < B2K_MAX_CUBE_TILES ? io->nin - i : B2K_MAX_CUBE_TILES;
+        rc = b2d_cube_to_rowmajor(d, io->in + i, n, x, ldx);
+    }
+    b2k_linear f = *a;
+    f.x = x;
+    f.ldx = ldx;
+    f.y = y;
+    f.ldy = ldy;
+    unsigned l = 0;
+    if (!rc) rc = b2d_linear(d, &f, &l);
+    for (unsigned i = 0; !rc && i < io->nout; i += B2K_MAX_CUBE_TILES) {
+        unsigned n = io->nout - i < B2K_MAX_CUBE_TILES ? io->nout - i : B2K_MAX_CUBE_TILES;
+        rc = b2d_rowmajor_to_cube(d, y, ldy, io->out + i, n);
+    }
+    free(x);
+    free(y);
+    if (!rc) *launches = 1;
+    return rc;
+}
+
 int b2d_noalloc_scratch(b2_dev *d, float **ptr, size_t *bytes) {
     if (!d) return ROCKET_E_DEVICE;
     *ptr = noalloc_scratch;

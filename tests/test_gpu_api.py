@@ -25,6 +25,15 @@ def uniform_case(m, n, k, seed):
     return x, w, b
 
 
+def cuda_runtime():
+    """cuda-python's runtime bindings (raw device copies for the padding checks), or None."""
+    try:
+        from cuda.bindings import runtime
+        return runtime
+    except Exception:
+        return None
+
+
 def tile_extent(total, i):
     return min(256, total - 256 * i)
 
@@ -66,7 +75,11 @@ def assemble(b2, views, info, m, n):
     return y
 
 
-@pytest.mark.parametrize("m,k,n", [(13, 37, 45), (257, 257, 257), (513, 33, 289)])
+# K a multiple of 8 with M > 8 in CO_CHAIN: the GEMM reads the input cubes and writes the output
+# cubes directly (3-D tensor maps, no gather/scatter); other shapes and CO_SEPARATE gather and
+# scatter. Both forms must give the host entry's bytes.
+@pytest.mark.parametrize("m,k,n", [(13, 37, 45), (257, 257, 257), (513, 33, 289), (40, 96, 72), (257, 264, 257),
+                                   (513, 512, 289), (100, 256, 300)])
 def test_run_tiles_matches_host_run_and_refuses_bad_views(b2, gpu_fd, m, k, n):
     x, w, b = uniform_case(m, n, k, m + k + n)
     for mode in (b2.CO_SEPARATE, b2.CO_CHAIN):
@@ -105,7 +118,7 @@ def test_run_tiles_matches_host_run_and_refuses_bad_views(b2, gpu_fd, m, k, n):
         op.destroy()
 
 
-@pytest.mark.parametrize("m,k,n", [(29, 513, 45), (300, 1000, 300)])
+@pytest.mark.parametrize("m,k,n", [(29, 513, 45), (300, 1000, 300), (129, 768, 513), (1024, 1024, 1024)])
 def test_run_tiled_k_tile_inputs(b2, gpu_fd, m, k, n):
     x, w, b = uniform_case(m, n, k, 11)
     op = b2.Linear(gpu_fd, m, k, n, w, b, post=b2.CO_LINEAR_NONE)
@@ -116,6 +129,24 @@ def test_run_tiled_k_tile_inputs(b2, gpu_fd, m, k, n):
     assert op.run_tiled(xv, yv) == 0
     y = assemble(b2, yv, info, m, n)
     assert np.array_equal(y.view(np.uint16), host.view(np.uint16))
+    # again with the same views (the direct form reuses its tensor maps), after filling every byte of
+    # the output cubes, padding included, with 0x47: the results and the zero padding come back
+    rt = cuda_runtime()
+    if rt is not None:
+        b2.sync(gpu_fd)
+        for v in yv:
+            assert rt.cudaMemset(v.buffer.contents.bo.ptr + v.offset, 0x47, v.tensor.bytes)[0] == 0
+        assert rt.cudaDeviceSynchronize()[0] == 0
+    assert op.run_tiled(xv, yv) == 0
+    assert np.array_equal(assemble(b2, yv, info, m, n).view(np.uint16), host.view(np.uint16))
+    if rt is not None:
+        for v in yv:
+            t = v.tensor
+            raw = np.empty(t.bytes // 2, np.uint16)
+            assert rt.cudaMemcpy(raw.ctypes.data, v.buffer.contents.bo.ptr + v.offset, t.bytes, 2)[0] == 0
+            cube = raw.reshape(t.physical_cols // 8, t.physical_rows, 8)          # [atom][row][channel]
+            rowmajor = cube.transpose(1, 0, 2).reshape(t.physical_rows, t.physical_cols)
+            assert not rowmajor[t.rows:, :].any() and not rowmajor[:, t.cols:].any(), "cube padding not zeroed"
     op.destroy()
 
 
