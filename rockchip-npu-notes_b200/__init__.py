@@ -243,6 +243,28 @@ SIGNATURES = {
     "b2_graph_launch": (_I, [_P]),
     "b2_graph_status": (_I, [_P]),
     "b2_graph_get_info": (_I, [_P, ctypes.POINTER(B2GraphInfo)]),
+    # rk_plan.h (descriptor and report structs as opaque pointers; tests/c/rk_plan_test.c drives them)
+    "rk_abi_version": (_U, []),
+    "rk_target_check": (_I, [_P]),
+    "rk_target_validate_text": (_I, [ctypes.c_char_p, _Z, ctypes.c_char_p, _P]),
+    "rk_plan_create": (_I, [_P, ctypes.POINTER(_P), _P]),
+    "rk_plan_destroy": (None, [_P]),
+    "rk_workspace_create": (_I, [_I, _P, _P, _U, ctypes.POINTER(_P), _P]),
+    "rk_workspace_create_shared": (_I, [_I, _P, _P, _U, _P, _U, ctypes.POINTER(_P), _P]),
+    "rk_workspace_run": (_I, [_P, _P, _U, _P, _U, _P, _P]),
+    "rk_workspace_run_group": (_I, [_P, _P, _U, _P, _P]),
+    "rk_workspace_run_ex": (_I, [_P, _P, _U, _P, _U, _P, _P]),
+    "rk_workspace_destroy": (_I, [_P, _P]),
+    "rk_workspace_set_persistent_upload": (_I, [_P, _U, _P]),
+    "rk_workspace_update_upload_region": (_I, [_P, _U, _P, _U, _U, _U, _U, _U, _U, _P]),
+    "rk_workspace_clear_upload_destination": (_I, [_P, _U, _P]),
+    "rk_workspace_get_cache_info": (_I, [_P, _P, _P]),
+    "rk_workspace_task_cbuf": (_I, [_P, _U, _P, _U, _P, _P]),
+    "rk_shared_constant_get_or_create": (_I, [_I, _P, _U, _P, ctypes.c_char_p, ctypes.POINTER(_P), _P, _P]),
+    "rk_shared_constant_retain": (None, [_P]),
+    "rk_shared_constant_release": (None, [_P]),
+    "rk_shared_constant_bytes": (ctypes.c_uint64, [_P]),
+    "rk_shared_constant_live": (_U, []),
 }
 KSPLIT_BLOB_BYTES = 96
 

@@ -207,6 +207,59 @@ int b2d_guard_init(b2_dev *, void *base, size_t payload, size_t slack, size_t gu
 int b2d_guard_check(b2_dev *, void *const *bases, const size_t *payloads, unsigned count,
                     size_t slack, size_t guard);
 
+/* ---------------------------------------------------------------------- plan (RKPlan) tiles
+ * A device tile of a plan view: FP16 at `ptr` (16-byte aligned) in one of the three layouts
+ * (values of enum rk_layout): CUBE [pcols/8][prows][8], WEIGHT [prows/16][pcols/32][16][32],
+ * LINEAR [pcols] (prows 1). */
+enum { B2K_RK_CUBE = 1, B2K_RK_WEIGHT = 2, B2K_RK_LINEAR = 3 };
+typedef struct {
+    void *ptr;
+    unsigned layout, rows, cols, physical_rows, physical_cols;
+} b2k_rk_tile;
+
+/* Upload packing: the destination logical rectangle [r0, r0+rows) x [c0, c0+cols) of `dst`
+ * receives, for its element (r0+i, c0+j),
+ *   MATRIX   src[(transpose ? j : i) * ld + (transpose ? i : j)]
+ *   SCALAR   src[0]
+ *   CHANNEL  src[j]
+ * and, with `clear`, every other physical element of the tile becomes 0. src is device FP16. */
+enum { B2K_RK_SRC_MATRIX = 0, B2K_RK_SRC_SCALAR = 1, B2K_RK_SRC_CHANNEL = 2 };
+typedef struct {
+    b2k_rk_tile dst;
+    unsigned r0, c0, rows, cols;
+    unsigned clear, mode, transpose;
+    const void *src;
+    size_t ld;
+} b2k_rk_pack;
+#define B2K_RK_MAX_PACK 40u     /* items per b2d_rk_pack launch (kernel parameter space) */
+int b2d_rk_pack(b2_dev *, const b2k_rk_pack *items, unsigned count);
+
+/* One device task (op = an rk_template_id value) over the tiles' whole physical extents:
+ *   contraction ops (MM, MM_ACC, EW_*): s(r, c) = sum over q < x.physical_cols, in order, of
+ *     double(x[r][q]) * double(w[c][q]) (w = the identity operand for EW_*), then
+ *     MM fp16(s); MM_ACC fp16(s + aux); EW_ADD fp16(s + aux); EW_MUL fp16(s * aux);
+ *     EW_MAX fp16(fmax(s, aux)); EW_ADD_RELU fp16(fmax(s + aux, 0)), for r < y.physical_rows,
+ *     c < y.physical_cols (aux has y's geometry);
+ *   LUT ops: y[e] = fp16(f(double(x[e]))) for each physical element (x and y same geometry) with
+ *     f = 1/(1+exp(-v)), clamp(v/6+0.5, 0, 1), 0.5(1+erf(v/sqrt 2)) or 1/sqrt(max(v, 0.125)).
+ * Every fp16() is one round-to-nearest-even of the double. ROCKET_E_SHAPE for an unknown op or
+ * tiles whose extents do not fit together. */
+typedef struct {
+    unsigned op;
+    b2k_rk_tile x, w, aux, y;
+} b2k_rk_task;
+int b2d_rk_task(b2_dev *, const b2k_rk_task *task);
+
+/* Download unpacking: the logical rows x cols of `src` into row-major device FP16 at dst with a
+ * pitch of ld elements. */
+typedef struct {
+    b2k_rk_tile src;
+    void *dst;
+    size_t ld;
+} b2k_rk_unpack;
+#define B2K_RK_MAX_UNPACK 64u
+int b2d_rk_unpack(b2_dev *, const b2k_rk_unpack *items, unsigned count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,6 +17,7 @@
 #include "gemm_sm100.h"
 #include "gemv.h"
 #include "graph_kernels.h"
+#include "plan_kernels.h"
 #include "ksplit.h"
 #include "rocket_b200.h"
 
@@ -742,6 +743,92 @@ int b2d_guard_check(b2_dev *d, void *const *bases, const size_t *payloads, unsig
     }
     g.count = count;
     return rc_of(b2::aux::guard_check(g, slack, guard, d->flags_dev, d->stream));
+}
+
+// ----------------------------------------------------------------------------- plan (RKPlan) tiles
+}  // extern "C"
+
+namespace {
+
+// The geometry rules every plan view satisfies (the plan verifier enforces them first; the kernels
+// index by them, so they are checked again before any launch).
+bool rk_tile_ok(const b2k_rk_tile &t) {
+    if (!t.ptr || (reinterpret_cast<uintptr_t>(t.ptr) & 15) || !t.rows || !t.cols || t.rows > t.physical_rows ||
+        t.cols > t.physical_cols || t.physical_cols > 65520u || t.physical_rows > 4096u)
+        return false;
+    if (t.layout == B2K_RK_LINEAR) return t.physical_rows == 1;
+    if (t.layout == B2K_RK_WEIGHT) return t.physical_rows % 32 == 0 && t.physical_cols % 32 == 0;
+    return t.layout == B2K_RK_CUBE && t.physical_rows % 4 == 0 && t.physical_cols % 32 == 0 &&
+           t.physical_rows <= 256;
+}
+
+bool rk_same_geometry(const b2k_rk_tile &a, const b2k_rk_tile &b) {
+    return a.layout == b.layout && a.physical_rows == b.physical_rows && a.physical_cols == b.physical_cols;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b2d_rk_pack(b2_dev *d, const b2k_rk_pack *items, unsigned count) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (count && !items) return ROCKET_E_SHAPE;
+    for (unsigned base = 0; base < count; base += B2K_RK_MAX_PACK) {
+        b2::rkplan::PackTable t;
+        memset(&t, 0, sizeof(t));
+        size_t max_vectors = 0;
+        for (unsigned i = base; i < count && i - base < B2K_RK_MAX_PACK; ++i) {
+            const b2k_rk_pack &it = items[i];
+            if (!rk_tile_ok(it.dst) || it.mode > B2K_RK_SRC_CHANNEL || (it.rows && it.cols && !it.src) ||
+                (size_t)it.r0 + it.rows > it.dst.physical_rows || (size_t)it.c0 + it.cols > it.dst.physical_cols ||
+                (it.mode == B2K_RK_SRC_MATRIX && it.rows && it.cols && it.ld < (it.transpose ? it.rows : it.cols)))
+                return ROCKET_E_SHAPE;
+            t.item[t.count++] = it;
+            const size_t v = ((size_t)it.dst.physical_rows * it.dst.physical_cols + 7) / 8;
+            if (v > max_vectors) max_vectors = v;
+        }
+        const int rc = rc_of(b2::rkplan::pack(t, max_vectors, d->stream, d->sm_count));
+        if (rc) return rc;
+    }
+    return 0;
+}
+
+int b2d_rk_task(b2_dev *d, const b2k_rk_task *t) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (!t || !rk_tile_ok(t->x) || !rk_tile_ok(t->y)) return ROCKET_E_SHAPE;
+    const unsigned op = t->op;
+    if ((op >= 5 && op <= 7) || op == 10) {
+        if (!rk_same_geometry(t->x, t->y)) return ROCKET_E_SHAPE;
+    } else if (op >= 1 && op <= 9) {
+        if (t->x.layout != B2K_RK_CUBE || !rk_tile_ok(t->w) || t->w.layout != B2K_RK_WEIGHT ||
+            t->y.layout != B2K_RK_CUBE || t->w.physical_cols != t->x.physical_cols ||
+            t->w.physical_rows < t->y.physical_cols || t->y.physical_rows > t->x.physical_rows)
+            return ROCKET_E_SHAPE;
+        if (op != 1 && (!rk_tile_ok(t->aux) || !rk_same_geometry(t->aux, t->y))) return ROCKET_E_SHAPE;
+    } else {
+        return ROCKET_E_SHAPE;
+    }
+    return rc_of(b2::rkplan::task(*t, d->stream, d->sm_count));
+}
+
+int b2d_rk_unpack(b2_dev *d, const b2k_rk_unpack *items, unsigned count) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (count && !items) return ROCKET_E_SHAPE;
+    for (unsigned base = 0; base < count; base += B2K_RK_MAX_UNPACK) {
+        b2::rkplan::UnpackTable t;
+        memset(&t, 0, sizeof(t));
+        size_t max_elements = 0;
+        for (unsigned i = base; i < count && i - base < B2K_RK_MAX_UNPACK; ++i) {
+            const b2k_rk_unpack &it = items[i];
+            if (!rk_tile_ok(it.src) || !it.dst || it.ld < it.src.cols) return ROCKET_E_SHAPE;
+            t.item[t.count++] = it;
+            const size_t n = (size_t)it.src.rows * it.src.cols;
+            if (n > max_elements) max_elements = n;
+        }
+        const int rc = rc_of(b2::rkplan::unpack(t, max_elements, d->stream, d->sm_count));
+        if (rc) return rc;
+    }
+    return 0;
 }
 
 // ----------------------------------------------------------------------------- graph node kernels

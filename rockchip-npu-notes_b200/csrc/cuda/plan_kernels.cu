@@ -1,0 +1,209 @@
+// plan_kernels.cu -- the plan (RKPlan) runtime's device work on sm_100a.
+//
+// A plan is a schedule of small tiles (at most 256 x 256, K at most 256 for a matmul) in the
+// reference's NPU layouts. Three kernels run it on B200:
+//   pack     every per-run upload of the schedule in one launch: the caller's FP16 windows (copied
+//            to HBM once per binding) are packed into the destination views' physical layouts,
+//            padding zeroed (research/custom-ops/src/rk_plan_runtime.c:244-339).
+//   task     one device task: the NPU program's arithmetic as the reference's host model of the NPU
+//            states it (research/custom-ops/tests/mock/npu_mock.c:392-537): a matmul-shaped pass
+//            s(r, c) = sum over q of x[r][q] * w[c][q] accumulated in double in q order (every
+//            FP16 product is exact in double, so an FMA equals the separate multiply and add), the
+//            template's epilogue in double, one round-to-nearest-even to FP16 (cvt.rn.f16.f64);
+//            LUT templates evaluate their function in double per element and round once.
+//   unpack   every download in one launch: the views' logical elements into row-major staging
+//            placed at the publish offsets of each output binding.
+// The tiles are small and latency-bound; the double-precision contraction keeps the results
+// bit-identical to the reference's model instead of fast (the Linear path itself runs on the
+// tcgen05 GEMM, not here).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "plan_kernels.h"
+
+namespace b2 {
+namespace rkplan {
+
+constexpr int THREADS = 256;
+
+__device__ __forceinline__ size_t tile_index(const b2k_rk_tile &t, unsigned r, unsigned c) {
+    if (t.layout == B2K_RK_LINEAR) return (size_t)r * t.physical_cols + c;
+    if (t.layout == B2K_RK_WEIGHT)
+        return (((size_t)(r / 16) * (t.physical_cols / 32) + c / 32) * 16 + r % 16) * 32 + c % 32;
+    return ((size_t)(c / 8) * t.physical_rows + r) * 8 + c % 8;
+}
+
+__device__ __forceinline__ double load_f64(const b2k_rk_tile &t, unsigned r, unsigned c) {
+    const unsigned short h = static_cast<const unsigned short *>(t.ptr)[tile_index(t, r, c)];
+    return (double)__half2float(__ushort_as_half(h));
+}
+
+__device__ __forceinline__ unsigned short round_f16(double v) {
+    unsigned short h;
+    asm("cvt.rn.f16.f64 %0, %1;" : "=h"(h) : "d"(v));
+    return h;
+}
+
+// Physical vector v (8 consecutive physical elements) of a tile -> its row and first column.
+// Every layout keeps 8 consecutive physical elements in one row at consecutive columns.
+__device__ __forceinline__ void vector_origin(const b2k_rk_tile &t, size_t v, unsigned &r, unsigned &c) {
+    if (t.layout == B2K_RK_LINEAR) {
+        r = 0;
+        c = (unsigned)(v * 8);
+    } else if (t.layout == B2K_RK_WEIGHT) {
+        const size_t ct = t.physical_cols / 32;
+        const size_t block = v / 64;                  // one 16 x 32 block holds 64 vectors
+        r = (unsigned)((block / ct) * 16 + (v / 4) % 16);
+        c = (unsigned)((block % ct) * 32 + (v % 4) * 8);
+    } else {
+        r = (unsigned)(v % t.physical_rows);
+        c = (unsigned)((v / t.physical_rows) * 8);
+    }
+}
+
+// ----------------------------------------------------------------------------------- pack
+__global__ void __launch_bounds__(THREADS) pack_kernel(const __grid_constant__ PackTable t) {
+    const b2k_rk_pack &it = t.item[blockIdx.y];
+    const b2k_rk_tile &d = it.dst;
+    const size_t elements = (size_t)d.physical_rows * d.physical_cols;
+    const size_t vectors = (elements + 7) / 8;
+    const unsigned short *src = static_cast<const unsigned short *>(it.src);
+    unsigned short *dst = static_cast<unsigned short *>(d.ptr);
+    for (size_t v = (size_t)blockIdx.x * THREADS + threadIdx.x; v < vectors; v += (size_t)gridDim.x * THREADS) {
+        unsigned r, c;
+        vector_origin(d, v, r, c);
+        const bool row_in = r >= it.r0 && r - it.r0 < it.rows;
+        const bool any_in = row_in && c + 8 > it.c0 && c < it.c0 + it.cols;
+        if (!any_in && !it.clear) continue;
+        unsigned short out[8];
+        const bool full = v * 8 + 8 <= elements;
+        if (!it.clear && full) {
+            const uint4 old = reinterpret_cast<const uint4 *>(dst)[v];
+            memcpy(out, &old, 16);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) out[k] = 0;
+        }
+        if (any_in) {
+            const unsigned i = r - it.r0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const unsigned cc = c + k;
+                if (cc < it.c0 || cc - it.c0 >= it.cols) continue;
+                const unsigned j = cc - it.c0;
+                size_t at;
+                if (it.mode == B2K_RK_SRC_SCALAR) at = 0;
+                else if (it.mode == B2K_RK_SRC_CHANNEL) at = j;
+                else at = it.transpose ? (size_t)j * it.ld + i : (size_t)i * it.ld + j;
+                out[k] = src[at];
+            }
+        }
+        if (full) {
+            uint4 u;
+            memcpy(&u, out, 16);
+            reinterpret_cast<uint4 *>(dst)[v] = u;
+        } else {
+            for (size_t k = 0; v * 8 + k < elements; ++k)
+                if (it.clear || (row_in && c + k >= it.c0 && c + k - it.c0 < it.cols)) dst[v * 8 + k] = out[k];
+        }
+    }
+}
+
+// ----------------------------------------------------------------------------------- tasks
+constexpr int TR = 8, TC = 32, TK = 32;     // block tile: 8 output rows x 32 output columns
+
+__global__ void __launch_bounds__(THREADS) contract_kernel(const __grid_constant__ b2k_rk_task t) {
+    __shared__ double xs[TR][TK];
+    __shared__ double ws[TC][TK + 1];
+    const unsigned tx = threadIdx.x % TC, ty = threadIdx.x / TC;
+    const unsigned r0 = blockIdx.y * TR, c0 = blockIdx.x * TC;
+    const unsigned r = r0 + ty, c = c0 + tx;
+    const unsigned K = t.x.physical_cols;
+    double s = 0.0;
+    for (unsigned q0 = 0; q0 < K; q0 += TK) {
+        xs[ty][tx] = r < t.x.physical_rows ? load_f64(t.x, r, q0 + tx) : 0.0;
+#pragma unroll
+        for (int i = 0; i < TC / TR; ++i) {
+            const unsigned wr = c0 + ty + TR * i;
+            ws[ty + TR * i][tx] = wr < t.w.physical_rows ? load_f64(t.w, wr, q0 + tx) : 0.0;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < TK; ++q) s = __fma_rn(xs[ty][q], ws[tx][q], s);
+        __syncthreads();
+    }
+    if (r >= t.y.physical_rows || c >= t.y.physical_cols) return;
+    double v = s;
+    if (t.op != 1) {                                          // every op but MM reads aux
+        const double b = load_f64(t.aux, r, c);
+        switch (t.op) {
+        case 2: case 3: v = __dadd_rn(s, b); break;          // MM_ACC, EW_ADD
+        case 4: v = __dmul_rn(s, b); break;                   // EW_MUL
+        case 8: v = fmax(s, b); break;                        // EW_MAX
+        default: v = fmax(__dadd_rn(s, b), 0.0); break;       // EW_ADD_RELU
+        }
+    }
+    static_cast<unsigned short *>(t.y.ptr)[tile_index(t.y, r, c)] = round_f16(v);
+}
+
+__device__ __forceinline__ double lut(unsigned op, double v) {
+    switch (op) {
+    case 5: return __ddiv_rn(1.0, __dadd_rn(1.0, exp(-v)));                          // sigmoid
+    case 6: return fmin(1.0, fmax(0.0, __dadd_rn(__ddiv_rn(v, 6.0), 0.5)));         // hardsigmoid
+    case 7: return __dmul_rn(0.5, __dadd_rn(1.0, erf(__ddiv_rn(v, 1.4142135623730951))));  // GELU gate
+    default: return __ddiv_rn(1.0, __dsqrt_rn(fmax(0.125, v)));                      // rsqrt
+    }
+}
+
+// x and y share one geometry, so physical element e of x maps to physical element e of y.
+__global__ void __launch_bounds__(THREADS) lut_kernel(const __grid_constant__ b2k_rk_task t) {
+    const size_t n = (size_t)t.y.physical_rows * t.y.physical_cols;
+    const unsigned short *x = static_cast<const unsigned short *>(t.x.ptr);
+    unsigned short *y = static_cast<unsigned short *>(t.y.ptr);
+    for (size_t e = (size_t)blockIdx.x * THREADS + threadIdx.x; e < n; e += (size_t)gridDim.x * THREADS)
+        y[e] = round_f16(lut(t.op, (double)__half2float(__ushort_as_half(x[e]))));
+}
+
+// ----------------------------------------------------------------------------------- unpack
+__global__ void __launch_bounds__(THREADS) unpack_kernel(const __grid_constant__ UnpackTable t) {
+    const b2k_rk_unpack &it = t.item[blockIdx.y];
+    const size_t n = (size_t)it.src.rows * it.src.cols;
+    const unsigned short *src = static_cast<const unsigned short *>(it.src.ptr);
+    unsigned short *dst = static_cast<unsigned short *>(it.dst);
+    for (size_t e = (size_t)blockIdx.x * THREADS + threadIdx.x; e < n; e += (size_t)gridDim.x * THREADS) {
+        const unsigned r = (unsigned)(e / it.src.cols), c = (unsigned)(e % it.src.cols);
+        dst[(size_t)r * it.ld + c] = src[tile_index(it.src, r, c)];
+    }
+}
+
+static unsigned blocks_for(size_t work, int sm_count) {
+    const size_t b = (work + THREADS - 1) / THREADS;
+    const size_t cap = (size_t)(sm_count > 0 ? sm_count : 148) * 4;
+    return (unsigned)(b < 1 ? 1 : (b < cap ? b : cap));
+}
+
+cudaError_t pack(const PackTable &t, size_t max_vectors, cudaStream_t s, int sm_count) {
+    if (!t.count) return cudaSuccess;
+    pack_kernel<<<dim3(blocks_for(max_vectors, sm_count), t.count), THREADS, 0, s>>>(t);
+    return cudaGetLastError();
+}
+
+cudaError_t task(const b2k_rk_task &t, cudaStream_t s, int sm_count) {
+    if ((t.op >= 5 && t.op <= 7) || t.op == 10) {
+        lut_kernel<<<blocks_for((size_t)t.y.physical_rows * t.y.physical_cols, sm_count), THREADS, 0, s>>>(t);
+    } else {
+        const dim3 grid((t.y.physical_cols + TC - 1) / TC, (t.y.physical_rows + TR - 1) / TR);
+        contract_kernel<<<grid, THREADS, 0, s>>>(t);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t unpack(const UnpackTable &t, size_t max_elements, cudaStream_t s, int sm_count) {
+    if (!t.count) return cudaSuccess;
+    unpack_kernel<<<dim3(blocks_for(max_elements, sm_count), t.count), THREADS, 0, s>>>(t);
+    return cudaGetLastError();
+}
+
+}  // namespace rkplan
+}  // namespace b2

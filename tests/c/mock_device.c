@@ -444,3 +444,55 @@ int b2d_capture_end(b2_dev *d, b2_exec **out, unsigned *kernels) {
 }
 int b2d_exec_launch(b2_dev *d, b2_exec *x) { return ROCKET_E_SHAPE; }
 void b2d_exec_destroy(b2_exec *x) { (void)x; }
+
+/* ---------------------------------------------------------------------- plan (RKPlan) tiles
+ * The oracle's restatement (oracle/rkplan_oracle.c) on host memory. mock_rk_inject plays the
+ * reference mock's injection knobs (research/custom-ops/tests/mock/npu_mock.c: rk_mock_inject_nan,
+ * the guard corruption): 1 writes NaN into element 0 of every task output, 2 overwrites the first
+ * slack byte behind every task output's tile. */
+typedef struct {
+    uint16_t *p;
+    unsigned layout, rows, cols, prows, pcols;
+} rk_oracle_tile;
+int rk_oracle_task(int op, const rk_oracle_tile *x, const rk_oracle_tile *w, const rk_oracle_tile *aux,
+                   rk_oracle_tile *y);
+void rk_oracle_pack(rk_oracle_tile *dst, unsigned r0, unsigned c0, unsigned rows, unsigned cols, int clear, int mode,
+                    int transpose, const uint16_t *src, size_t ld);
+void rk_oracle_unpack(const rk_oracle_tile *src, uint16_t *dst, size_t ld);
+
+int mock_rk_inject = 0;
+unsigned mock_rk_tasks = 0;   /* tasks run since start */
+
+static rk_oracle_tile mock_tile(const b2k_rk_tile *t) {
+    rk_oracle_tile o = {(uint16_t *)t->ptr, t->layout, t->rows, t->cols, t->physical_rows, t->physical_cols};
+    return o;
+}
+
+int b2d_rk_pack(b2_dev *d, const b2k_rk_pack *items, unsigned count) {
+    if (!d || (count && !items)) return ROCKET_E_SHAPE;
+    for (unsigned i = 0; i < count; i++) {
+        rk_oracle_tile t = mock_tile(&items[i].dst);
+        rk_oracle_pack(&t, items[i].r0, items[i].c0, items[i].rows, items[i].cols, (int)items[i].clear,
+                       (int)items[i].mode, (int)items[i].transpose, (const uint16_t *)items[i].src, items[i].ld);
+    }
+    return 0;
+}
+
+int b2d_rk_task(b2_dev *d, const b2k_rk_task *t) {
+    if (!d || !t) return ROCKET_E_SHAPE;
+    rk_oracle_tile x = mock_tile(&t->x), w = mock_tile(&t->w), aux = mock_tile(&t->aux), y = mock_tile(&t->y);
+    if (rk_oracle_task((int)t->op, &x, &w, &aux, &y)) return ROCKET_E_SHAPE;
+    mock_rk_tasks++;
+    if (mock_rk_inject == 1) y.p[0] = 0x7e00;
+    if (mock_rk_inject == 2) ((unsigned char *)y.p)[(size_t)y.prows * y.pcols * 2] ^= 0x5a;
+    return 0;
+}
+
+int b2d_rk_unpack(b2_dev *d, const b2k_rk_unpack *items, unsigned count) {
+    if (!d || (count && !items)) return ROCKET_E_SHAPE;
+    for (unsigned i = 0; i < count; i++) {
+        rk_oracle_tile s = mock_tile(&items[i].src);
+        rk_oracle_unpack(&s, (uint16_t *)items[i].dst, items[i].ld);
+    }
+    return 0;
+}

@@ -17,10 +17,10 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def declared_functions():
     names = set()
-    for h in ("rocket_b200.h", "custom_ops.h", "b2_linear.h", "co_graph.h"):
+    for h in ("rocket_b200.h", "custom_ops.h", "b2_linear.h", "co_graph.h", "rk_plan.h"):
         src = open(os.path.join(ROOT, "include", h)).read()
         src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-        for m in re.finditer(r"\b((?:co|rocket|b2)_[a-z0-9_]+)\s*\(", src):
+        for m in re.finditer(r"\b((?:co|rocket|b2|rk)_[a-z0-9_]+)\s*\(", src):
             names.add(m.group(1))
     return names
 

@@ -81,7 +81,7 @@ def _mock_cli(tmp_path):
     sources = [os.path.join(host, f) for f in ("cli.c", "rocket.c", "tensor.c", "plan.c", "linear.c", "ksplit.c",
                                                 "graph.c")]
     sources += [os.path.join(ROOT, "tests", "c", "mock_device.c"), os.path.join(ROOT, "oracle", "linear_oracle.c"),
-                os.path.join(ROOT, "oracle", "graph_oracle.c")]
+                os.path.join(ROOT, "oracle", "graph_oracle.c"), os.path.join(ROOT, "oracle", "rkplan_oracle.c")]
     exe = tmp_path / "linear_hardsigmoid_mock"
     inc = ["-I", os.path.join(ROOT, "include"), "-I", os.path.join(ROOT, "rockchip-npu-notes_b200", "csrc"), "-I", host]
     strict = subprocess.run([cc, "-std=gnu11", "-O2", "-Wall", "-Wextra", "-Wno-unused-parameter", "-Werror",

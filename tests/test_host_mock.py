@@ -24,7 +24,8 @@ def _build_and_run(tmp_path, test_source, banner):
         pytest.skip("gcc not available")
     sources = [os.path.join(HOST, f) for f in ("rocket.c", "tensor.c", "plan.c", "linear.c", "ksplit.c", "graph.c")]
     sources += [os.path.join(ROOT, "tests", "c", "mock_device.c"), os.path.join(ROOT, "tests", "c", test_source),
-                os.path.join(ROOT, "oracle", "linear_oracle.c"), os.path.join(ROOT, "oracle", "graph_oracle.c")]
+                os.path.join(ROOT, "oracle", "linear_oracle.c"), os.path.join(ROOT, "oracle", "graph_oracle.c"),
+                os.path.join(ROOT, "oracle", "rkplan_oracle.c")]
     exe = tmp_path / test_source.replace(".c", "")
     cmd = [cc, "-std=gnu11", "-O1", "-Wall", "-Werror=implicit-function-declaration",
            "-I", os.path.join(ROOT, "include"), "-I", os.path.join(ROOT, "rockchip-npu-notes_b200", "csrc"),
