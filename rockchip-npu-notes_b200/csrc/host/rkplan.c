@@ -18,10 +18,11 @@
  *
  * The run (rk_plan_runtime.c:1580-2150): binding checks (count, shape, finiteness of every input,
  * host-range overlap) before any device work; one host-to-device copy per input binding into HBM
- * staging; then, on the device handle's stream, one pack launch for every per-run upload, one
- * launch per task in action order and one unpack launch for every download (replayed as one CUDA
- * graph when the handle supports capture), the slack/guard check of every slot, one
- * device-to-host copy of the outputs; only when every downloaded element is finite and every
+ * staging; then, on the device handle's stream and in action order, one pack launch per run of
+ * consecutive uploads, one launch per task and one unpack launch per run of consecutive downloads
+ * (slots may be shared by buffers with disjoint live ranges, so each transfer runs at its own
+ * position), replayed as one CUDA graph when the handle supports capture, the slack/guard check
+ * of every slot, one device-to-host copy of the outputs; only when every downloaded element is finite and every
  * guard is intact are the caller's output buffers written. Constant uploads run once, at
  * workspace creation.
  */
@@ -960,8 +961,10 @@ struct rk_workspace {
     uint32_t npacks;
     b2k_rk_task *tasks;              /* device tasks in action order */
     uint32_t ntasks;
-    b2k_rk_unpack *unpacks;
+    b2k_rk_unpack *unpacks;          /* downloads in action order */
     uint32_t nunpacks;
+    struct rk_step { uint32_t kind, first, count; } *steps;   /* the run, in action order */
+    uint32_t nsteps;
     void **guard_base;               /* allocated slots for the guard check */
     size_t *guard_payload;
     uint32_t nguard;
@@ -1059,31 +1062,52 @@ static int is_constant_upload(const rk_plan *p, const rk_action_desc *a) {
     return a->kind == RK_ACTION_UPLOAD && p->values[a->source_binding].role == RK_ROLE_CONSTANT;
 }
 
-/* Per-run device schedule: the non-constant, non-persistent uploads (and which inputs they read). */
-static void build_packs(rk_workspace *ws) {
+/* The per-run device schedule, in action order: a run of consecutive per-run uploads (neither
+ * constant nor persistent) is one pack launch, each task one launch, a run of consecutive
+ * downloads one unpack launch. Order matters: a plan may map buffers with disjoint live ranges to
+ * one slot, so an upload or download may only run at its own position. */
+enum { STEP_PACK = 0, STEP_TASK = 1, STEP_UNPACK = 2 };
+
+static void build_schedule(rk_workspace *ws) {
     const rk_plan *p = ws->plan;
-    ws->npacks = 0;
+    uint32_t task = 0, unpack = 0;
+    ws->npacks = ws->nsteps = 0;
     ws->upload_calls = ws->upload_bytes = 0;
     memset(ws->in_needed, 0, p->d.nvalues);
     for (uint32_t i = 0; i < p->d.nactions; i++) {
         const rk_action_desc *a = &p->actions[i];
-        if (a->kind != RK_ACTION_UPLOAD || is_constant_upload(p, a) || ws->persistent[i]) continue;
-        ws->packs[ws->npacks++] = pack_of(ws, a, (const char *)ws->in_dev + ws->in_off[a->source_binding]);
-        ws->in_needed[a->source_binding] = 1;
-        ws->upload_calls++;
-        ws->upload_bytes += p->views[a->outputs[0]].tensor.bytes;
+        struct rk_step *last = ws->nsteps ? &ws->steps[ws->nsteps - 1] : NULL;
+        if (a->kind == RK_ACTION_UPLOAD) {
+            if (is_constant_upload(p, a) || ws->persistent[i]) continue;
+            if (!last || last->kind != STEP_PACK) ws->steps[ws->nsteps++] = (struct rk_step){STEP_PACK, ws->npacks, 0};
+            ws->steps[ws->nsteps - 1].count++;
+            ws->packs[ws->npacks++] = pack_of(ws, a, (const char *)ws->in_dev + ws->in_off[a->source_binding]);
+            ws->in_needed[a->source_binding] = 1;
+            ws->upload_calls++;
+            ws->upload_bytes += p->views[a->outputs[0]].tensor.bytes;
+        } else if (a->kind == RK_ACTION_NPU_TASK) {
+            ws->steps[ws->nsteps++] = (struct rk_step){STEP_TASK, task++, 1};
+        } else if (a->kind == RK_ACTION_DOWNLOAD) {
+            if (!last || last->kind != STEP_UNPACK) ws->steps[ws->nsteps++] = (struct rk_step){STEP_UNPACK, unpack, 0};
+            ws->steps[ws->nsteps - 1].count++;
+            unpack++;
+        }
     }
 }
 
-/* pack -> tasks -> guard check -> unpack, on the handle's stream. */
+/* The steps, then the guard check of every slot, on the handle's stream. */
 static int issue_schedule(rk_workspace *ws) {
-    int rc = b2d_rk_pack(ws->dev, ws->packs, ws->npacks);
-    for (uint32_t i = 0; i < ws->ntasks && !rc; i++) rc = b2d_rk_task(ws->dev, &ws->tasks[i]);
+    int rc = 0;
+    for (uint32_t i = 0; i < ws->nsteps && !rc; i++) {
+        const struct rk_step *st = &ws->steps[i];
+        if (st->kind == STEP_PACK) rc = b2d_rk_pack(ws->dev, ws->packs + st->first, st->count);
+        else if (st->kind == STEP_TASK) rc = b2d_rk_task(ws->dev, &ws->tasks[st->first]);
+        else rc = b2d_rk_unpack(ws->dev, ws->unpacks + st->first, st->count);
+    }
     for (uint32_t g = 0; g < ws->nguard && !rc; g += B2K_MAX_CUBE_TILES) {
         const uint32_t n = ws->nguard - g < B2K_MAX_CUBE_TILES ? ws->nguard - g : B2K_MAX_CUBE_TILES;
         rc = b2d_guard_check(ws->dev, ws->guard_base + g, ws->guard_payload + g, n, CO_SLACK, CO_GUARD);
     }
-    if (!rc) rc = b2d_rk_unpack(ws->dev, ws->unpacks, ws->nunpacks);
     return rc;
 }
 
@@ -1112,7 +1136,8 @@ static void workspace_free(rk_workspace *ws) {
     b2h_free(ws->fd, ws->scratch_dev, ws->scratch_bytes);
     b2d_host_free(ws->out_host);
     free(ws->slots); free(ws->tiles); free(ws->in_off); free(ws->in_needed); free(ws->out_off);
-    free(ws->packs); free(ws->tasks); free(ws->unpacks); free(ws->guard_base); free(ws->guard_payload);
+    free(ws->packs); free(ws->tasks); free(ws->unpacks); free(ws->steps); free(ws->guard_base);
+    free(ws->guard_payload);
     free(ws->persistent);
     plan_free(ws->plan);
     free(ws);
@@ -1201,11 +1226,12 @@ static int workspace_create_impl(int fd, const rk_plan *plan, const rk_binding *
     ws->packs = calloc(na, sizeof(b2k_rk_pack));
     ws->tasks = calloc(na, sizeof(b2k_rk_task));
     ws->unpacks = calloc(na, sizeof(b2k_rk_unpack));
+    ws->steps = calloc(na, sizeof(*ws->steps));
     ws->guard_base = calloc(nb, sizeof(void *));
     ws->guard_payload = calloc(nb, sizeof(size_t));
     ws->persistent = calloc(na, 1);
     if (!ws->slots || !ws->tiles || !ws->in_off || !ws->in_needed || !ws->out_off || !ws->packs || !ws->tasks ||
-        !ws->unpacks || !ws->guard_base || !ws->guard_payload || !ws->persistent) {
+        !ws->unpacks || !ws->steps || !ws->guard_base || !ws->guard_payload || !ws->persistent) {
         workspace_free(ws);
         return WS_FAIL("workspace_create", RK_E_NOMEM, "out of memory");
     }
@@ -1290,7 +1316,7 @@ static int workspace_create_impl(int fd, const rk_plan *plan, const rk_binding *
         }
     }
     for (uint32_t s = 0; s < p->d.nsubmits; s++) ws->task_count += p->submits[s].ntask_ids;
-    build_packs(ws);
+    build_schedule(ws);
     rc = upload_constants(ws, constants, nconstants, diag);
     if (rc) {
         workspace_free(ws);
@@ -1667,7 +1693,7 @@ int rk_workspace_set_persistent_upload(rk_workspace *ws, uint32_t action_id, rk_
         rc = STATE_FAIL(RK_E_SCHEMA, "persistent state requires a single-output upload action", action_id);
     else if (!ws->persistent[action_id]) {
         ws->persistent[action_id] = 1;
-        build_packs(ws);
+        build_schedule(ws);
         rc = capture_schedule(ws);
         if (rc) {
             atomic_store(&ws->poisoned, 1);

@@ -17,6 +17,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 #include "b2_linear.h"
 #include "rk_plan.h"
@@ -384,6 +385,26 @@ static void multitile_case(int fd) {
     EXPECT(rk_workspace_run(ws, inputs, 1, outputs, 1, &report, &diag) == 0);
     EXPECT(!memcmp(y, ref, (size_t)MM * NN * 2));
 
+    /* latency of one synchronous run (host copies in, the device schedule, the copy out, the
+     * checks and the publish), printed for the record */
+    {
+#ifdef RK_TEST_MOCK
+        enum { RUNS = 3 };
+#else
+        enum { RUNS = 200 };
+#endif
+        struct timespec t0, t1;
+        double wait = 0;
+        clock_gettime(CLOCK_MONOTONIC, &t0);
+        for (int i = 0; i < RUNS; i++) {
+            EXPECT(rk_workspace_run(ws, inputs, 1, outputs, 1, &report, &diag) == 0);
+            wait += report.submit_wait_us;
+        }
+        clock_gettime(CLOCK_MONOTONIC, &t1);
+        const double us = ((double)(t1.tv_sec - t0.tv_sec) * 1e6 + (double)(t1.tv_nsec - t0.tv_nsec) / 1e3) / RUNS;
+        printf("rk_plan multitile [257x256]x[256x32]: %.1f us per run, %.1f us device schedule + copy out\n", us,
+               wait / RUNS);
+    }
     /* binding checks */
     rk_binding wrong = outputs[0];
     wrong.shape[0] = 256;
