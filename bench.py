@@ -366,6 +366,11 @@ def main():
     if rank == 0 and world == 1:
         cube = bench_cube(b2, fd, torch, stream, steps)
 
+    # ---------------------------------------------------------------- plan ABI (rank 0, N=1 only)
+    rkp = None
+    if rank == 0 and world == 1:
+        rkp = bench_rk_plan(b2, fd, steps)
+
     line = None
     if rank == 0:
         traffic = traffic_per_launch()
@@ -403,9 +408,11 @@ def main():
             line["cube_entry"] = cube
         if cfg1:
             line["cfg1"] = cfg1
+        if rkp:
+            line["rk_plan"] = rkp
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_sample()
-        line["summary"] = summarize(world, kernel_tflops, e2e_ms, tile16, cfg1, shard, gemv, graph, cube)
+        line["summary"] = summarize(world, kernel_tflops, e2e_ms, tile16, cfg1, shard, gemv, graph, cube, rkp)
     b2.close(fd)
     if world > 1:
         dist.barrier()
@@ -421,7 +428,7 @@ def _r(v, digits=4):
     return float(f"{v:.{digits}g}")
 
 
-def summarize(world, kernel_tflops, e2e_ms, tile16, cfg1, shard, gemv, graph, cube=None):
+def summarize(world, kernel_tflops, e2e_ms, tile16, cfg1, shard, gemv, graph, cube=None, rkp=None):
     """The line's key figures in a few hundred bytes, printed as its last key."""
     out = {"n_gpus": world, "gemm_4096_fp32acc_tflops": _r(kernel_tflops), "e2e_ms": _r(e2e_ms)}
     if tile16:
@@ -432,6 +439,8 @@ def summarize(world, kernel_tflops, e2e_ms, tile16, cfg1, shard, gemv, graph, cu
         out["cfg1_hsig_64x256x512_us"] = {"device": _r(cfg1["device_us"]), "graph": _r(cfg1["graph_us"]),
                                           "e2e": _r(cfg1["e2e_us"]), "cpu_c_port": _r(cfg1["cpu_c_port_us"]),
                                           "cpu_literal_s": _r(cfg1["cpu_oracle_literal_s"])}
+    if rkp:
+        out["rk_plan_hsig_64x256x512_e2e_us"] = _r(rkp["e2e_us"])
     if shard:
         cp = shard["column_parallel"]
         out["cfg5_8192x16384x16384_column_parallel"] = {"ms": _r(cp["ms_per_step"]),
@@ -715,6 +724,52 @@ def bench_cfg1(b2, fd, torch, stream, steps):
             "device_tflops": flops / (graph * 1e-3) / 1e12, "worst_err_over_tol_vs_oracle": worst,
             "cpu_c_port_us": c_s * 1e6, "cpu_c_port_threads": threads, "cpu_oracle_literal_s": py_s,
             "cpu_oracle_literal": "pure-Python restatement of cli_gate.oracle (one core)"}
+
+
+def bench_rk_plan(b2, fd, steps):
+    """The config-1 shape through the plan/workspace ABI: the Linear + HardSigmoid plan the reference's
+    own planner writes for M=64, N=256, K=512 (tests/golden/rk_plans.json, chain mode: two K-tile
+    uploads, two weight uploads packed once, MM + MM_ACC + a HardSigmoid LUT task, one download),
+    run end to end with rk_workspace_run from host arrays (copies in, the recorded CUDA graph of the
+    schedule, copy out, finiteness and guard checks, publish). The plan has no bias, so its output is
+    compared byte for byte with co_linear_hsig_run at b = 0 (the same tile-16 arithmetic)."""
+    import importlib
+    import numpy as np
+    rk = importlib.import_module("rockchip-npu-notes_b200.rkplan")
+    name = "linear_hardsigmoid_64x512x256/chain"
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden", "rk_plans.json")) as f:
+        entry = json.load(f)[name]
+    m, n, k = 64, 256, 512
+    rng = np.random.default_rng(0)
+    x = rng.uniform(-1, 1, (m, k)).astype(np.float16)
+    w = rng.uniform(-1 / np.sqrt(k), 1 / np.sqrt(k), (n, k)).astype(np.float16)
+    y = np.zeros((m, n), np.float16)
+    ids = {bd["name"]: bd["id"] for bd in entry["bindings"]}
+    L = rk.declare(b2.lib())
+    plan = rk.Plan(L, entry)
+    ws = rk.Workspace(L, fd, plan, {ids["B"]: w})
+    prepared = ws.prepare({ids["A"]: x}, {ids["A1"]: y})
+    for _ in range(20):
+        report = ws.run(prepared)
+    reps = max(50, min(steps, 2000))
+    wait = 0.0
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        report = ws.run(prepared)
+        wait += report.submit_wait_us
+    e2e_us = (time.perf_counter() - t0) / reps * 1e6
+    tasks, submits = report.task_count, report.submit_count
+    ws.destroy()
+    plan.destroy()
+    op = b2.Linear(fd, m, k, n, w, np.zeros(n, np.float16), post=b2.CO_LINEAR_HSIG, mode=b2.CO_CHAIN,
+                   acc=b2.ACC_TILE16, compat=True)
+    y_op = op.run(x)
+    op.destroy()
+    if not np.array_equal(y.view(np.uint16), np.asarray(y_op, np.float16).view(np.uint16)):
+        raise RuntimeError("plan-ABI output differs from co_linear_hsig_run at b = 0")
+    return {"plan": name, "source": "the reference planner's descriptors (tests/golden/rk_plans.json)",
+            "tasks": tasks, "submits": submits, "e2e_us": e2e_us, "device_schedule_and_copy_out_us": wait / reps,
+            "equals_co_linear_hsig_run": True}
 
 
 def bench_cube(b2, fd, torch, stream, steps):

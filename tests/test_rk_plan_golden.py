@@ -13,6 +13,7 @@ Each test rebuilds the structs from that JSON (ctypes mirrors of include/rk_plan
   * on a B200: the same runs give the same bytes as the CPU seam.
 """
 import ctypes
+import importlib
 import json
 import os
 import shutil
@@ -26,137 +27,7 @@ HOST = os.path.join(ROOT, "rockchip-npu-notes_b200", "csrc", "host")
 INC = ["-I", os.path.join(ROOT, "include"), "-I", os.path.join(ROOT, "rockchip-npu-notes_b200", "csrc"), "-I", HOST]
 PLANS = json.load(open(os.path.join(ROOT, "tests", "golden", "rk_plans.json")))
 
-u32, u64, i32 = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int32
-_PU32 = ctypes.POINTER(u32)
-
-
-class Tensor(ctypes.Structure):
-    _fields_ = [("abi_version", u32), ("struct_size", u32), ("dtype", u32), ("layout", u32), ("rows", u32),
-                ("cols", u32), ("physical_rows", u32), ("physical_cols", u32), ("atom", u32), ("reserved", u32),
-                ("bytes", u64)]
-
-
-class Value(ctypes.Structure):
-    _fields_ = [("abi_version", u32), ("struct_size", u32), ("id", u32), ("role", u32), ("dtype", u32), ("rank", u32),
-                ("shape", u32 * 2), ("nbytes", u64), ("name", ctypes.c_char_p), ("name_len", u32),
-                ("reserved", u32)]
-
-
-class Buffer(ctypes.Structure):
-    _fields_ = [(n, u32) for n in ("abi_version", "struct_size", "id", "role", "slot_id", "alignment", "layout_id",
-                                   "padding_state", "lifetime_first", "lifetime_last")] + [("offset", u64),
-                                                                                            ("capacity", u64)]
-
-
-class View(ctypes.Structure):
-    _fields_ = [("abi_version", u32), ("struct_size", u32), ("id", u32), ("buffer_id", u32), ("offset_bytes", u64),
-                ("valid_region", u32 * 4), ("tensor", Tensor)]
-
-
-class Action(ctypes.Structure):
-    _fields_ = [(n, u32) for n in ("abi_version", "struct_size", "id", "kind", "template_id", "ninputs", "noutputs",
-                                   "ndeps", "source_binding", "source_row_offset", "source_col_offset",
-                                   "source_row_stride", "source_k0", "source_k_index", "source_k_count", "flags",
-                                   "act_kind")] + [("inputs", _PU32), ("outputs", _PU32), ("deps", _PU32),
-                                                   ("origin", ctypes.c_char * 64)]
-
-
-class Submit(ctypes.Structure):
-    _fields_ = [(n, u32) for n in ("abi_version", "struct_size", "id", "mode", "core_policy", "ntask_ids",
-                                   "ndeps")] + [("task_ids", _PU32), ("deps", _PU32)]
-
-
-class Publish(ctypes.Structure):
-    _fields_ = [(n, u32) for n in ("abi_version", "struct_size", "binding_id", "view_id", "dst_row_offset",
-                                   "dst_col_offset", "rows", "cols")]
-
-
-class PlanDesc(ctypes.Structure):
-    _fields_ = [("abi_version", u32), ("struct_size", u32), ("schema_version", u32), ("flags", u32),
-                ("profile_hash", u64), ("source_hash", u64),
-                ("values", ctypes.POINTER(Value)), ("nvalues", u32), ("reserved0", u32),
-                ("buffers", ctypes.POINTER(Buffer)), ("nbuffers", u32), ("reserved1", u32),
-                ("views", ctypes.POINTER(View)), ("nviews", u32), ("reserved2", u32),
-                ("actions", ctypes.POINTER(Action)), ("nactions", u32), ("reserved3", u32),
-                ("submits", ctypes.POINTER(Submit)), ("nsubmits", u32), ("reserved4", u32),
-                ("publish", ctypes.POINTER(Publish)), ("npublish", u32), ("reserved5", u32),
-                ("device_budget_bytes", u64), ("host_budget_bytes", u64), ("claimed_device_bytes", u64),
-                ("claimed_host_bytes", u64), ("runtime_abi_version", u32), ("reserved6", u32)]
-
-
-class Binding(ctypes.Structure):
-    _fields_ = [("abi_version", u32), ("struct_size", u32), ("id", u32), ("dtype", u32), ("rank", u32),
-                ("shape", u32 * 2), ("data", ctypes.c_void_p), ("nbytes", u64)]
-
-
-class Diag(ctypes.Structure):
-    _fields_ = [("abi_version", u32), ("struct_size", u32), ("code", i32), ("native_status", i32),
-                ("action_id", u32), ("has_action", u32), ("stage", ctypes.c_char * 32),
-                ("message", ctypes.c_char * 512), ("source", ctypes.c_char * 128), ("profile", ctypes.c_char * 64)]
-
-
-class RunReport(ctypes.Structure):
-    _fields_ = [(n, u32) for n in ("abi_version", "struct_size", "task_count", "submit_count", "fail_action_id",
-                                   "numeric_mode")] + [(n, u64) for n in ("upload_calls", "upload_bytes",
-                                                                          "download_calls", "download_bytes")] + \
-               [(n, ctypes.c_double) for n in ("pack_us", "emit_us", "submit_wait_us", "output_sync_us")]
-
-
-def _fill(struct, row, skip=()):
-    for name, ctype in struct._fields_:
-        if name in skip or name not in row:
-            continue
-        v = row[name]
-        if isinstance(v, list):
-            arr = getattr(struct, name)
-            for i, x in enumerate(v):
-                arr[i] = x
-        elif isinstance(v, dict):
-            _fill(getattr(struct, name), v)
-        elif isinstance(v, str):
-            setattr(struct, name, v.encode())
-        else:
-            setattr(struct, name, v)
-
-
-def build_desc(entry):
-    """The plan descriptor of one JSON entry; returns (desc, keepalive)."""
-    keep = []
-
-    def arr(ctype, rows, skip=(), extra=None):
-        a = (ctype * max(len(rows), 1))()
-        for i, row in enumerate(rows):
-            _fill(a[i], row, skip)
-            if extra:
-                extra(a[i], row)
-        keep.append(a)
-        return a
-
-    def ids(values):
-        a = (u32 * max(len(values), 1))(*values)
-        keep.append(a)
-        return ctypes.cast(a, _PU32) if values else None
-
-    def value_extra(v, row):
-        name = ctypes.create_string_buffer(row["name"].encode())
-        keep.append(name)
-        v.name = ctypes.cast(name, ctypes.c_char_p)
-
-    def action_extra(a, row):
-        a.inputs, a.outputs, a.deps = ids(row["inputs"]), ids(row["outputs"]), ids(row["deps"])
-
-    def submit_extra(s, row):
-        s.task_ids, s.deps = ids(row["task_ids"]), ids(row["deps"])
-
-    d = PlanDesc()
-    _fill(d, entry, skip=("values", "buffers", "views", "actions", "submits", "publish"))
-    d.values = arr(Value, entry["values"], skip=("name",), extra=value_extra)
-    d.buffers = arr(Buffer, entry["buffers"])
-    d.views = arr(View, entry["views"])
-    d.actions = arr(Action, entry["actions"], skip=("inputs", "outputs", "deps"), extra=action_extra)
-    d.submits = arr(Submit, entry["submits"], skip=("task_ids", "deps"), extra=submit_extra)
-    d.publish = arr(Publish, entry["publish"])
-    return d, keep
+rk = importlib.import_module("rockchip-npu-notes_b200.rkplan")
 
 
 def f16(x):
@@ -179,7 +50,7 @@ def silu16(z):
 
 def case_data(name, entry):
     """Seeded inputs and constants of a case, and the expected outputs by binding name."""
-    rng = np.random.default_rng(abs(hash(name.split("/")[0])) % (2 ** 32) if False else 7)
+    rng = np.random.default_rng(7)
     shapes = {b["name"]: tuple(b["shape"]) for b in entry["bindings"]}
     data = {}
     for b in entry["bindings"]:
@@ -214,56 +85,25 @@ def case_data(name, entry):
 
 
 def run_case(L, fd, name, entry):
-    """rk_plan_create + workspace + one run on library L; returns the outputs by binding name."""
-    desc, keep = build_desc(entry)
-    diag = Diag()
-    plan = ctypes.c_void_p()
-    rc = L.rk_plan_create(ctypes.byref(desc), ctypes.byref(plan), ctypes.byref(diag))
-    assert rc == 0, (name, rc, diag.message)
+    """rk_plan_create + workspace + one run on library L; returns (outputs, expected) by binding name."""
     data, want = case_data(name, entry)
-
-    def binding(b, array):
-        x = Binding()
-        x.abi_version, x.struct_size, x.id, x.dtype = 1, ctypes.sizeof(Binding), b["id"], 0
-        x.rank = 2
-        x.shape[0], x.shape[1] = b["shape"]
-        x.data, x.nbytes = array.ctypes.data, array.nbytes
-        return x
-
-    by_role = {r: [b for b in sorted(entry["bindings"], key=lambda b: b["id"]) if b["role"] == r]
-               for r in ("input", "constant", "output")}
-    outs = {b["name"]: np.zeros(b["shape"], np.float16) for b in by_role["output"]}
-    consts = (Binding * max(len(by_role["constant"]), 1))(*[binding(b, data[b["name"]]) for b in by_role["constant"]])
-    ins = (Binding * max(len(by_role["input"]), 1))(*[binding(b, data[b["name"]]) for b in by_role["input"]])
-    outb = (Binding * len(by_role["output"]))(*[binding(b, outs[b["name"]]) for b in by_role["output"]])
-    ws = ctypes.c_void_p()
+    ids = {b["name"]: b["id"] for b in entry["bindings"]}
+    roles = {b["name"]: b["role"] for b in entry["bindings"]}
+    outs = {b["name"]: np.zeros(b["shape"], np.float16) for b in entry["bindings"] if b["role"] == "output"}
+    plan = rk.Plan(L, entry)
+    ws = None
     try:
-        rc = L.rk_workspace_create(fd, plan, consts, len(by_role["constant"]), ctypes.byref(ws), ctypes.byref(diag))
-        assert rc == 0, (name, rc, diag.message)
-        report = RunReport()
-        rc = L.rk_workspace_run(ws, ins, len(by_role["input"]), outb, len(by_role["output"]), ctypes.byref(report),
-                                ctypes.byref(diag))
-        assert rc == 0, (name, rc, diag.message)
+        ws = rk.Workspace(L, fd, plan, {ids[n]: a for n, a in data.items() if roles[n] == "constant"})
+        prepared = ws.prepare({ids[n]: a for n, a in data.items() if roles[n] == "input"},
+                              {ids[n]: a for n, a in outs.items()})
+        report = ws.run(prepared)
         assert report.download_calls == len(entry["publish"])
         assert report.task_count == sum(len(s["task_ids"]) for s in entry["submits"])
     finally:
-        if ws.value:
-            assert L.rk_workspace_destroy(ws, ctypes.byref(diag)) == 0
-        L.rk_plan_destroy(plan)
+        if ws is not None:
+            ws.destroy()
+        plan.destroy()
     return outs, want
-
-
-def _declare(L):
-    L.rocket_open.restype = ctypes.c_int
-    for fn in ("rk_plan_create", "rk_workspace_create", "rk_workspace_run", "rk_workspace_destroy"):
-        getattr(L, fn).restype = ctypes.c_int
-    L.rk_plan_destroy.argtypes = [ctypes.c_void_p]
-    L.rk_workspace_destroy.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
-    L.rk_workspace_create.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, u32, ctypes.c_void_p,
-                                      ctypes.c_void_p]
-    L.rk_workspace_run.argtypes = [ctypes.c_void_p, ctypes.c_void_p, u32, ctypes.c_void_p, u32, ctypes.c_void_p,
-                                   ctypes.c_void_p]
-    return L
 
 
 def mock_library(tmp_path):
@@ -280,7 +120,7 @@ def mock_library(tmp_path):
                             "-lpthread", "-lm", "-o", so], capture_output=True, text=True)
     assert build.returncode == 0, build.stderr
     os.environ.setdefault("B2_MOCK_DEVICES", "1")
-    return _declare(ctypes.CDLL(so))
+    return rk.declare(ctypes.CDLL(so))
 
 
 def test_struct_sizes_match_the_reference_ctypes(tmp_path):
@@ -302,10 +142,7 @@ def test_struct_sizes_match_the_reference_ctypes(tmp_path):
            "rk_tensor_desc": e["views"][0]["tensor"]["struct_size"], "rk_action_desc": e["actions"][0]["struct_size"],
            "rk_submit_desc": e["submits"][0]["struct_size"], "rk_publish_desc": e["publish"][0]["struct_size"]}
     assert got == sizes
-    mirrors = {"rk_plan_desc": PlanDesc, "rk_value_desc": Value, "rk_buffer_desc": Buffer, "rk_view_desc": View,
-               "rk_tensor_desc": Tensor, "rk_action_desc": Action, "rk_submit_desc": Submit,
-               "rk_publish_desc": Publish}
-    assert {n: ctypes.sizeof(m) for n, m in mirrors.items()} == sizes
+    assert {n: ctypes.sizeof(rk.MIRRORS[n]) for n in names} == sizes
 
 
 @pytest.mark.parametrize("name", sorted(PLANS))
@@ -324,7 +161,7 @@ def test_reference_plans_on_cpu_seam(tmp_path, name):
 @pytest.mark.gpu
 def test_reference_plans_on_gpu_match_cpu_seam(b2, tmp_path):
     M = mock_library(tmp_path)
-    G = _declare(ctypes.CDLL(b2.LIB_PATH))
+    G = rk.declare(ctypes.CDLL(b2.LIB_PATH))
     mfd, gfd = M.rocket_open(), G.rocket_open()
     assert mfd >= 0 and gfd >= 0
     try:
