@@ -87,25 +87,54 @@ static unsigned operands(const co_graph_node *n, unsigned refs[4]) {
     return 1;
 }
 
-/* reference co_graph.c:29-41 */
-static int visit(const co_graph_desc *d, unsigned id, unsigned char *state, co_graph_plan *p) {
-    if (id >= d->count) return ROCKET_E_SHAPE;
-    if (state[id] == 1) return ROCKET_E_SHAPE;
-    if (state[id] == 2) return 0;
-    const co_graph_node *n = &d->nodes[id];
+/* The per-node checks made when the walk first reaches a node (reference co_graph.c:29-41): an op
+ * past ATTENTION is unsupported; flags other than ALLOW_NEG_INF, flags on a non-INPUT node and a
+ * mask count above one are shape errors. */
+static int node_ok(const co_graph_node *n) {
     if ((unsigned)n->op > (unsigned)CO_GRAPH_ATTENTION) return ROCKET_E_UNSUPPORTED;
-    if (n->flags & ~CO_GRAPH_ALLOW_NEG_INF) return ROCKET_E_SHAPE;
-    if (n->flags && n->op != CO_GRAPH_INPUT) return ROCKET_E_SHAPE;
-    if (n->op == CO_GRAPH_ATTENTION && n->has_mask > 1) return ROCKET_E_SHAPE;
-    state[id] = 1;
-    unsigned refs[4], nr = operands(n, refs);
-    for (unsigned i = 0; i < nr; i++) {
-        int rc = visit(d, refs[i], state, p);
-        if (rc) return rc;
-    }
-    state[id] = 2;
-    p->order[p->steps++] = id;
+    if ((n->flags & ~CO_GRAPH_ALLOW_NEG_INF) || (n->flags && n->op != CO_GRAPH_INPUT)) return ROCKET_E_SHAPE;
+    return n->op == CO_GRAPH_ATTENTION && n->has_mask > 1 ? ROCKET_E_SHAPE : 0;
+}
+
+enum { NODE_UNSEEN = 0, NODE_OPEN = 1, NODE_PLACED = 2 };
+struct walk_frame {
+    unsigned id, next, nrefs, refs[4];
+};
+
+/* Opens node `id` on the walk stack, unless it is already placed. Reaching an open node again
+ * closes a cycle; an id past the graph is not a node: both ROCKET_E_SHAPE. */
+static int open_node(const co_graph_desc *d, unsigned id, unsigned char *state, struct walk_frame *stack,
+                     unsigned *depth) {
+    if (id >= d->count || state[id] == NODE_OPEN) return ROCKET_E_SHAPE;
+    if (state[id] == NODE_PLACED) return 0;
+    const int rc = node_ok(&d->nodes[id]);
+    if (rc) return rc;
+    state[id] = NODE_OPEN;
+    struct walk_frame *f = &stack[(*depth)++];
+    f->id = id;
+    f->next = 0;
+    f->nrefs = operands(&d->nodes[id], f->refs);
     return 0;
+}
+
+/* Places `root` and everything it reads into p->order, operands before their consumer and in operand
+ * order (a depth-first post-order, walked with an explicit stack: each node is open at most once, so
+ * the stack never holds more than the graph's nodes). */
+static int place(const co_graph_desc *d, unsigned root, unsigned char *state, co_graph_plan *p) {
+    struct walk_frame stack[MAXN];
+    unsigned depth = 0;
+    int rc = open_node(d, root, state, stack, &depth);
+    while (!rc && depth) {
+        struct walk_frame *top = &stack[depth - 1];
+        if (top->next < top->nrefs) {
+            rc = open_node(d, top->refs[top->next++], state, stack, &depth);
+            continue;
+        }
+        state[top->id] = NODE_PLACED;
+        p->order[p->steps++] = top->id;
+        depth--;
+    }
+    return rc;
 }
 
 static int tensor_size(unsigned rows, unsigned cols, size_t *bytes, unsigned *tiles) {
@@ -194,7 +223,7 @@ static int analyze(const co_graph_desc *d, const unsigned *outputs, unsigned nou
         for (unsigned j = 0; j < i; j++)
             if (outputs[j] == outputs[i]) return ROCKET_E_SHAPE;
         p.outputs[i] = outputs[i];
-        int rc = visit(d, outputs[i], state, &p);
+        int rc = place(d, outputs[i], state, &p);
         if (rc) return rc;
     }
     for (unsigned step = 0; step < p.steps; step++) {

@@ -17,8 +17,8 @@
  * those plans are accepted; CBUF reuse flags keep their structural check and have no effect.
  *
  * The run (rk_plan_runtime.c:1580-2150): binding checks (count, shape, finiteness of every input,
- * host-range overlap) before any device work; one host-to-device copy per input binding into HBM
- * staging; then, on the device handle's stream and in action order, one pack launch per run of
+ * host-range overlap) before any device work; the input bindings through pinned staging as one
+ * host-to-device copy into HBM; then, on the device handle's stream and in action order, one pack launch per run of
  * consecutive uploads, one launch per task and one unpack launch per run of consecutive downloads
  * (slots may be shared by buffers with disjoint live ranges, so each transfer runs at its own
  * position), replayed as one CUDA graph when the handle supports capture, the slack/guard check
@@ -950,7 +950,7 @@ struct rk_workspace {
     rk_plan *plan;                   /* the workspace's own copy */
     co_buffer *slots;                /* [nbuffers]: one HBM allocation per used slot id */
     b2k_rk_tile *tiles;              /* [nviews] */
-    void *in_dev;                    /* HBM copy of the input bindings, per-value offsets */
+    void *in_dev, *in_host;          /* the input bindings in HBM and their pinned host staging */
     size_t in_bytes;
     uint64_t *in_off;                /* [nvalues] */
     unsigned char *in_needed;        /* [nvalues]: a per-run upload reads this input */
@@ -1135,6 +1135,7 @@ static void workspace_free(rk_workspace *ws) {
     b2h_free(ws->fd, ws->out_dev, ws->out_bytes);
     b2h_free(ws->fd, ws->scratch_dev, ws->scratch_bytes);
     b2d_host_free(ws->out_host);
+    b2d_host_free(ws->in_host);
     free(ws->slots); free(ws->tiles); free(ws->in_off); free(ws->in_needed); free(ws->out_off);
     free(ws->packs); free(ws->tasks); free(ws->unpacks); free(ws->steps); free(ws->guard_base);
     free(ws->guard_payload);
@@ -1276,7 +1277,10 @@ static int workspace_create_impl(int fd, const rk_plan *plan, const rk_binding *
             ws->nconstants++;
         }
     }
-    if (ws->in_bytes) rc = b2h_malloc(fd, ws->in_bytes, &ws->in_dev);
+    if (ws->in_bytes) {
+        rc = b2h_malloc(fd, ws->in_bytes, &ws->in_dev);
+        if (!rc && !(ws->in_host = b2d_host_alloc(ws->in_bytes))) rc = ROCKET_E_NOMEM;
+    }
     if (!rc) rc = b2h_malloc(fd, ws->out_bytes, &ws->out_dev);
     if (!rc && !(ws->out_host = b2d_host_alloc(ws->out_bytes))) rc = ROCKET_E_NOMEM;
     if (rc) {
@@ -1426,12 +1430,16 @@ static int run_once(rk_workspace *ws, const rk_binding *in, uint32_t nin, void *
     const rk_plan *p = ws->plan;
     double t0 = now_us();
     int rc = 0;
-    for (uint32_t i = 0; i < p->d.nvalues && !rc; i++) {
+    /* the inputs the schedule reads, through pinned staging, as one asynchronous copy (the previous
+     * run's copy finished at its sync) */
+    size_t end = 0;
+    for (uint32_t i = 0; i < p->d.nvalues; i++) {
         if (!ws->in_needed[i]) continue;
         const rk_binding *b = find_binding(in, nin, i);
-        rc = b2d_copy_2d(ws->dev, (char *)ws->in_dev + ws->in_off[i], b->nbytes, b->data, b->nbytes, b->nbytes, 1,
-                         B2D_H2D);
+        memcpy((char *)ws->in_host + ws->in_off[i], b->data, b->nbytes);
+        if (ws->in_off[i] + b->nbytes > end) end = ws->in_off[i] + b->nbytes;
     }
+    if (end) rc = b2d_copy_2d(ws->dev, ws->in_dev, end, ws->in_host, end, end, 1, B2D_H2D);
     double t1 = now_us();
     st->pack_us += t1 - t0;
     if (!rc) rc = ws->exec ? b2d_exec_launch(ws->dev, ws->exec) : issue_schedule(ws);
