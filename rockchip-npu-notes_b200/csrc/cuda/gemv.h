@@ -86,7 +86,7 @@ struct Group {
     XSource xsrc[GROUP_MAX];
     int count, M, units, nx;
     int map3;                           // wmap is 3-D (one copy per 16-row x 512-K unit), else 2-D 64 x 16 boxes
-    int hold;                           // whole-row launches: slots a producer fills before the x table is ready (0: all)
+    int hold;                           // whole-row launches: slots a producer fills before the x loads are issued (0: all)
     unsigned *flags;
     Scratch scratch;
 };
