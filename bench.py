@@ -369,7 +369,10 @@ def main():
     # ---------------------------------------------------------------- plan ABI (rank 0, N=1 only)
     rkp = None
     if rank == 0 and world == 1:
-        rkp = bench_rk_plan(b2, fd, steps)
+        try:
+            rkp = bench_rk_plan(b2, fd, steps)
+        except Exception as e:   # a secondary surface: report it, keep the line
+            rkp = {"error": f"{type(e).__name__}: {e}"}
 
     line = None
     if rank == 0:
@@ -440,7 +443,7 @@ def summarize(world, kernel_tflops, e2e_ms, tile16, cfg1, shard, gemv, graph, cu
                                           "e2e": _r(cfg1["e2e_us"]), "cpu_c_port": _r(cfg1["cpu_c_port_us"]),
                                           "cpu_literal_s": _r(cfg1["cpu_oracle_literal_s"])}
     if rkp:
-        out["rk_plan_hsig_64x256x512_e2e_us"] = _r(rkp["e2e_us"])
+        out["rk_plan_hsig_64x256x512_e2e_us"] = _r(rkp["e2e_us"]) if "e2e_us" in rkp else rkp.get("error")
     if shard:
         cp = shard["column_parallel"]
         out["cfg5_8192x16384x16384_column_parallel"] = {"ms": _r(cp["ms_per_step"]),
@@ -731,8 +734,10 @@ def bench_rk_plan(b2, fd, steps):
     own planner writes for M=64, N=256, K=512 (tests/golden/rk_plans.json, chain mode: two K-tile
     uploads, two weight uploads packed once, MM + MM_ACC + a HardSigmoid LUT task, one download),
     run end to end with rk_workspace_run from host arrays (copies in, the recorded CUDA graph of the
-    schedule, copy out, finiteness and guard checks, publish). The plan has no bias, so its output is
-    compared byte for byte with co_linear_hsig_run at b = 0 (the same tile-16 arithmetic)."""
+    schedule, copy out, finiteness and guard checks, publish). The plan has no bias; its output is
+    checked against co_linear_hsig_run at b = 0 within the 2e-3 + 2e-3|ref| tolerance (the plan sums
+    each 256-K tile exactly, the operator on the tensor cores in FP32, so an element may differ by
+    one FP16 rounding)."""
     import importlib
     import numpy as np
     rk = importlib.import_module("rockchip-npu-notes_b200.rkplan")
@@ -765,11 +770,14 @@ def bench_rk_plan(b2, fd, steps):
                    acc=b2.ACC_TILE16, compat=True)
     y_op = op.run(x)
     op.destroy()
-    if not np.array_equal(y.view(np.uint16), np.asarray(y_op, np.float16).view(np.uint16)):
-        raise RuntimeError("plan-ABI output differs from co_linear_hsig_run at b = 0")
+    a, r = y.astype(np.float64), np.asarray(y_op, np.float64)
+    if not np.all(np.abs(a - r) <= 2e-3 + 2e-3 * np.abs(r)):
+        raise RuntimeError("plan-ABI output outside tolerance of co_linear_hsig_run at b = 0")
+    same = float(np.mean(y.view(np.uint16) == np.asarray(y_op, np.float16).view(np.uint16)))
     return {"plan": name, "source": "the reference planner's descriptors (tests/golden/rk_plans.json)",
             "tasks": tasks, "submits": submits, "e2e_us": e2e_us, "device_schedule_and_copy_out_us": wait / reps,
-            "equals_co_linear_hsig_run": True}
+            "vs_co_linear_hsig_run": {"within_tolerance": True, "bit_identical_fraction": same,
+                                      "max_abs_diff": float(np.max(np.abs(a - r)))}}
 
 
 def bench_cube(b2, fd, torch, stream, steps):
