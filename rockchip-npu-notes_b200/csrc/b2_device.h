@@ -242,8 +242,8 @@ int b2d_rk_pack(b2_dev *, const b2k_rk_pack *items, unsigned count);
  *     c < y.physical_cols (aux has y's geometry);
  *   LUT ops: y[e] = fp16(f(double(x[e]))) for each physical element (x and y same geometry) with
  *     f = 1/(1+exp(-v)), clamp(v/6+0.5, 0, 1), 0.5(1+erf(v/sqrt 2)) or 1/sqrt(max(v, 0.125)).
- * Every fp16() is one round-to-nearest-even of the double. ROCKET_E_SHAPE for an unknown op or
- * tiles whose extents do not fit together. */
+ * Every fp16() is one round-to-nearest-even of the double. ROCKET_E_SHAPE for an unknown op, a
+ * contraction over more than 256 physical columns, or tiles whose extents do not fit together. */
 typedef struct {
     unsigned op;
     b2k_rk_tile x, w, aux, y;

@@ -125,6 +125,7 @@ int b2d_open(int ordinal, b2_dev **out) {
         return ROCKET_E_NOMEM;
     }
     d->gate_table = static_cast<__half *>(gt);
+    if (b2::rkplan::prepare() != cudaSuccess) cudaGetLastError();   // plan tasks then report the launch error
     *out = d;
     return 0;
 }
@@ -801,7 +802,7 @@ int b2d_rk_task(b2_dev *d, const b2k_rk_task *t) {
         if (!rk_same_geometry(t->x, t->y)) return ROCKET_E_SHAPE;
     } else if (op >= 1 && op <= 9) {
         if (t->x.layout != B2K_RK_CUBE || !rk_tile_ok(t->w) || t->w.layout != B2K_RK_WEIGHT ||
-            t->y.layout != B2K_RK_CUBE || t->w.physical_cols != t->x.physical_cols ||
+            t->y.layout != B2K_RK_CUBE || t->x.physical_cols > 256 || t->w.physical_cols != t->x.physical_cols ||
             t->w.physical_rows < t->y.physical_cols || t->y.physical_rows > t->x.physical_rows)
             return ROCKET_E_SHAPE;
         if (op != 1 && (!rk_tile_ok(t->aux) || !rk_same_geometry(t->aux, t->y))) return ROCKET_E_SHAPE;

@@ -14,8 +14,8 @@
 //   unpack   every download in one launch: the views' logical elements into row-major staging
 //            placed at the publish offsets of each output binding.
 // The tiles are small and latency-bound; the double-precision contraction keeps the results
-// bit-identical to the reference's model instead of fast (the Linear path itself runs on the
-// tcgen05 GEMM, not here).
+// bit-identical to the reference's model (the Linear path itself runs on the tcgen05 GEMM, not
+// here).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -111,29 +111,57 @@ __global__ void __launch_bounds__(THREADS) pack_kernel(const __grid_constant__ P
 }
 
 // ----------------------------------------------------------------------------------- tasks
-constexpr int TR = 8, TC = 32, TK = 32;     // block tile: 8 output rows x 32 output columns
+// A block computes 8 output rows x 32 output columns. K (x's physical columns) is at most 256 for
+// every contraction template, so the block stages its 8 x rows and 32 W rows over the whole of K in
+// shared memory in one load phase, converted to double once there, and each thread then runs its
+// element's sum in q order with nothing but the FMA on the dependency chain.
+// The W rows are padded by one double so the 32 threads of a warp, reading W rows tx at one q, fall
+// on different banks; the x row is a broadcast.
+constexpr int TR = 8, TC = 32, KMAX = 256, WPITCH = KMAX + 1, CTHREADS = TR * TC;
+constexpr size_t CONTRACT_SMEM = (size_t)(TR * KMAX + TC * WPITCH) * sizeof(double);
 
-__global__ void __launch_bounds__(THREADS) contract_kernel(const __grid_constant__ b2k_rk_task t) {
-    __shared__ double xs[TR][TK];
-    __shared__ double ws[TC][TK + 1];
+__global__ void __launch_bounds__(CTHREADS) contract_kernel(const __grid_constant__ b2k_rk_task t) {
+    extern __shared__ double sm[];
+    double *xs = sm;                  // [TR][KMAX]
+    double *ws = sm + TR * KMAX;      // [TC][WPITCH]
     const unsigned tx = threadIdx.x % TC, ty = threadIdx.x / TC;
     const unsigned r0 = blockIdx.y * TR, c0 = blockIdx.x * TC;
-    const unsigned r = r0 + ty, c = c0 + tx;
     const unsigned K = t.x.physical_cols;
-    double s = 0.0;
-    for (unsigned q0 = 0; q0 < K; q0 += TK) {
-        xs[ty][tx] = r < t.x.physical_rows ? load_f64(t.x, r, q0 + tx) : 0.0;
+    const unsigned short *xg = static_cast<const unsigned short *>(t.x.ptr);
+    const unsigned short *wg = static_cast<const unsigned short *>(t.w.ptr);
+    // Thread (ty, tx) stages x row ty and W rows ty + 8 i (i < 4) at q = tx + 32 j: all 40 loads
+    // are issued before any is used, so the phase costs one memory round trip.
+    constexpr int J = KMAX / 32;
+    unsigned short xv[J], wv[TC / TR][J];
+    const unsigned r = r0 + ty;
 #pragma unroll
-        for (int i = 0; i < TC / TR; ++i) {
-            const unsigned wr = c0 + ty + TR * i;
-            ws[ty + TR * i][tx] = wr < t.w.physical_rows ? load_f64(t.w, wr, q0 + tx) : 0.0;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int q = 0; q < TK; ++q) s = __fma_rn(xs[ty][q], ws[tx][q], s);
-        __syncthreads();
+    for (int j = 0; j < J; ++j) {
+        const unsigned q = tx + 32 * j;
+        xv[j] = (r < t.x.physical_rows && q < K) ? xg[tile_index(t.x, r, q)] : (unsigned short)0;
     }
+#pragma unroll
+    for (int i = 0; i < TC / TR; ++i) {
+        const unsigned c = c0 + ty + TR * i;
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            const unsigned q = tx + 32 * j;
+            wv[i][j] = (c < t.w.physical_rows && q < K) ? wg[tile_index(t.w, c, q)] : (unsigned short)0;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) xs[ty * KMAX + tx + 32 * j] = (double)__half2float(__ushort_as_half(xv[j]));
+#pragma unroll
+    for (int i = 0; i < TC / TR; ++i)
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+            ws[(ty + TR * i) * WPITCH + tx + 32 * j] = (double)__half2float(__ushort_as_half(wv[i][j]));
+    __syncthreads();
+    const unsigned c = c0 + tx;
     if (r >= t.y.physical_rows || c >= t.y.physical_cols) return;
+    const double *xr = xs + ty * KMAX, *wr = ws + tx * WPITCH;
+    double s = 0.0;
+#pragma unroll 16
+    for (unsigned q = 0; q < K; ++q) s = __fma_rn(xr[q], wr[q], s);
     double v = s;
     if (t.op != 1) {                                          // every op but MM reads aux
         const double b = load_f64(t.aux, r, c);
@@ -183,6 +211,10 @@ static unsigned blocks_for(size_t work, int sm_count) {
     return (unsigned)(b < 1 ? 1 : (b < cap ? b : cap));
 }
 
+cudaError_t prepare() {
+    return cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CONTRACT_SMEM);
+}
+
 cudaError_t pack(const PackTable &t, size_t max_vectors, cudaStream_t s, int sm_count) {
     if (!t.count) return cudaSuccess;
     pack_kernel<<<dim3(blocks_for(max_vectors, sm_count), t.count), THREADS, 0, s>>>(t);
@@ -194,7 +226,7 @@ cudaError_t task(const b2k_rk_task &t, cudaStream_t s, int sm_count) {
         lut_kernel<<<blocks_for((size_t)t.y.physical_rows * t.y.physical_cols, sm_count), THREADS, 0, s>>>(t);
     } else {
         const dim3 grid((t.y.physical_cols + TC - 1) / TC, (t.y.physical_rows + TR - 1) / TR);
-        contract_kernel<<<grid, THREADS, 0, s>>>(t);
+        contract_kernel<<<grid, CTHREADS, CONTRACT_SMEM, s>>>(t);
     }
     return cudaGetLastError();
 }

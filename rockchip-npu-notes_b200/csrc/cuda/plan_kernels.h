@@ -18,6 +18,9 @@ struct UnpackTable {
     unsigned count;
 };
 
+// The contraction kernel's shared-memory opt-in (over 48 KB) on the current device: done when a device
+// handle opens, outside any stream capture.
+cudaError_t prepare();
 cudaError_t pack(const PackTable &t, size_t max_vectors, cudaStream_t s, int sm_count);
 cudaError_t task(const b2k_rk_task &t, cudaStream_t s, int sm_count);
 cudaError_t unpack(const UnpackTable &t, size_t max_elements, cudaStream_t s, int sm_count);
