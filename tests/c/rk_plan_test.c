@@ -45,17 +45,17 @@ static int mentions(const char *message, const char *needle) { return !needle ||
 typedef struct {
     rk_value_desc values[8];
     uint32_t nvalues;
-    rk_buffer_desc buffers[48];
+    rk_buffer_desc buffers[64];
     uint32_t nbuffers;
-    rk_view_desc views[48];
+    rk_view_desc views[64];
     uint32_t nviews;
-    rk_action_desc actions[64];
+    rk_action_desc actions[128];
     uint32_t nactions;
-    uint32_t ins[64][3], outs[64][1], deps[64][4];
+    uint32_t ins[128][3], outs[128][1], deps[128][4];
     rk_submit_desc submits[32];
     uint32_t nsubmits;
     uint32_t tasks[32][16];
-    rk_publish_desc publish[16];
+    rk_publish_desc publish[64];
     uint32_t npublish;
     const char *names[8];
 } pb;
@@ -319,7 +319,7 @@ static void multitile_case(int fd) {
     bad.npublish = 1;
     EXPECT_CODE(rk_plan_create(&bad, &badplan, &diag), RK_E_SHAPE, "cover the output binding");
     /* the two output tiles are live at the same time: they cannot share a slot */
-    rk_buffer_desc shared[48];
+    rk_buffer_desc shared[64];
     memcpy(shared, b.buffers, sizeof(shared));
     shared[4].slot_id = shared[3].slot_id;
     bad = desc;
@@ -510,7 +510,7 @@ static void kacc_case(int fd) {
         return;
     }
     /* the accumulator's prior and output may not share a slot */
-    rk_buffer_desc shared[48];
+    rk_buffer_desc shared[64];
     memcpy(shared, b.buffers, sizeof(shared));
     shared[5].slot_id = shared[4].slot_id;
     rk_plan_desc bad = desc;
@@ -818,8 +818,80 @@ static void rejection_cases(void) {
     EXPECT_CODE(rk_target_validate_text("x", 1, "y", &diag), RK_E_UNSUPPORTED, NULL);
 }
 
+/* ------------------------------------------------------------------------------ many uploads */
+/* 50 uploads of 12-row slices of one input (more than one pack launch holds), a sigmoid task on
+ * the first slice and 50 downloads back into one output (the reference's many-upload case,
+ * rk_plan_host_test.c:1493-1695, in its own form). */
+static void many_uploads_case(int fd) {
+    enum { TILES = 50, TR = 12, C = 32 };
+    static pb b;
+    memset(&b, 0, sizeof(b));
+    const uint32_t A = pb_value(&b, RK_ROLE_INPUT, 2, TILES * TR, C, "A");
+    const uint32_t Y = pb_value(&b, RK_ROLE_OUTPUT, 2, TILES * TR, C, "Y");
+    uint32_t v[TILES], u[TILES];
+    for (int i = 0; i < TILES; i++) v[i] = pb_view(&b, RK_LAYOUT_CUBE_F16, TR, C, RK_ROLE_INPUT_SLICE);
+    const uint32_t vs = pb_view(&b, RK_LAYOUT_CUBE_F16, TR, C, RK_ROLE_SCRATCH);
+    for (int i = 0; i < TILES; i++) u[i] = pb_upload(&b, A, v[i], (uint32_t)(TR * i), 0, 0);
+    const uint32_t t = pb_task(&b, RK_TEMPLATE_LUT_SIGMOID_F16, (uint32_t[]){v[0]}, 1, vs, (uint32_t[]){u[0]}, 1);
+    pb_submit(&b, t, 1);
+    pb_download(&b, Y, vs, t, 0, 0);
+    for (int i = 1; i < TILES; i++) pb_download(&b, Y, v[i], u[i], (uint32_t)(TR * i), 0);
+    rk_plan_desc desc = pb_desc(&b);
+    rk_diag diag;
+    rk_plan *plan = NULL;
+    EXPECT(rk_plan_create(&desc, &plan, &diag) == 0);
+    if (!plan) {
+        fprintf(stderr, "  many uploads create: %s\n", diag.message);
+        return;
+    }
+    static _Float16 a[TILES * TR * C], y[TILES * TR * C], ref[TILES * TR * C];
+    for (int i = 0; i < TILES * TR * C; i++) a[i] = (_Float16)((double)pattern((unsigned)i, 29) * 9.0);
+    for (int i = 0; i < TILES * TR * C; i++)
+        ref[i] = i < TR * C ? (_Float16)(1.0 / (1.0 + exp(-(double)a[i]))) : a[i];
+    rk_workspace *ws = NULL;
+    EXPECT(rk_workspace_create(fd, plan, NULL, 0, &ws, &diag) == 0);
+    if (ws) {
+        rk_binding in[] = {binding(&b.values[A], a)}, out[] = {binding(&b.values[Y], y)};
+        rk_run_report report;
+        EXPECT(rk_workspace_run(ws, in, 1, out, 1, &report, &diag) == 0);
+        EXPECT(report.upload_calls == TILES && report.download_calls == TILES && report.task_count == 1);
+        EXPECT(!memcmp(y, ref, sizeof(y)));
+        EXPECT(rk_workspace_destroy(ws, &diag) == 0);
+    }
+    rk_plan_destroy(plan);
+}
+
+/* A writer that touches a buffer does not cover a wider reader: 12 uploaded rows under a 13-row
+ * view of the same buffer are refused (the reference's partial-coverage case,
+ * rk_plan_host_test.c:379-540). */
+static void partial_coverage_case(void) {
+    static pb b;
+    memset(&b, 0, sizeof(b));
+    const uint32_t A = pb_value(&b, RK_ROLE_INPUT, 2, 13, 32, "A");
+    const uint32_t Y = pb_value(&b, RK_ROLE_OUTPUT, 2, 13, 32, "Y");
+    const uint32_t up = pb_view(&b, RK_LAYOUT_CUBE_F16, 12, 32, RK_ROLE_INPUT_SLICE);
+    /* a 13-row reader over the uploaded view's buffer (physical rows 16 against 12) */
+    const uint32_t rd = b.nviews++;
+    b.views[rd] = b.views[up];
+    b.views[rd].id = rd;
+    b.views[rd].tensor = tensor(RK_LAYOUT_CUBE_F16, 13, 32);
+    b.views[rd].valid_region[1] = 13;
+    b.buffers[b.views[up].buffer_id].capacity = b.views[rd].tensor.bytes;
+    const uint32_t out = pb_view(&b, RK_LAYOUT_CUBE_F16, 13, 32, RK_ROLE_SCRATCH);
+    const uint32_t u = pb_upload(&b, A, up, 0, 0, 0);
+    const uint32_t t = pb_task(&b, RK_TEMPLATE_LUT_HARDSIGMOID_F16, (uint32_t[]){rd}, 1, out, (uint32_t[]){u}, 1);
+    pb_submit(&b, t, 1);
+    pb_download(&b, Y, out, t, 0, 0);
+    rk_plan_desc desc = pb_desc(&b);
+    rk_diag diag;
+    rk_plan *plan = (rk_plan *)1;
+    EXPECT_CODE(rk_plan_create(&desc, &plan, &diag), RK_E_SHAPE, "no write before this read");
+    EXPECT(plan == NULL);
+}
+
 int main(void) {
     rejection_cases();
+    partial_coverage_case();
     const int fd = rocket_open();
     if (fd < 0) {
         printf("rk_plan_test: no device (%d); %u checks, %u failures\n", fd, checks, failures);
@@ -830,6 +902,7 @@ int main(void) {
     multitile_case(fd);
     kacc_case(fd);
     ew_case(fd);
+    many_uploads_case(fd);
     rocket_close(fd);
     printf("rk_plan_test: %u checks, %u failures\n", checks, failures);
     return failures ? 1 : 0;
