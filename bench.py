@@ -208,6 +208,7 @@ def main():
     ap.add_argument("--graph-m", type=int, nargs="*", default=[4096, 8, 1], help="graph FFN row counts")
     ap.add_argument("--tile16-only", action="store_true", help="only the tile-16 GEMM section (diagnostics)")
     ap.add_argument("--rk-plan-only", action="store_true", help="only the plan-ABI section (diagnostics)")
+    ap.add_argument("--cfg1-only", action="store_true", help="only the config-1 section (diagnostics)")
     ap.add_argument("--linear-shape", type=int, nargs="+", metavar="M N K",
                     help="time tile-16 Linears of these shapes only, given as M N K triples (diagnostics)")
     args = ap.parse_args()
@@ -247,6 +248,10 @@ def main():
         return
     if args.rk_plan_only:   # diagnostics (profiling the plan-ABI section): no headline line
         print(json.dumps({"rk_plan": bench_rk_plan(b2, fd, args.steps)}), flush=True)
+        b2.close(fd)
+        return
+    if args.cfg1_only:   # diagnostics (profiling the config-1 operator): no headline line
+        print(json.dumps({"cfg1": bench_cfg1(b2, fd, torch, stream, args.steps)}), flush=True)
         b2.close(fd)
         return
     if args.graph_only:   # diagnostics (profiling the graph section): no headline line

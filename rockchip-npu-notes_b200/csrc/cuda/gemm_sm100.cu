@@ -53,7 +53,8 @@ constexpr int THREADS = 128 + EPI_WARPS * 32;
 constexpr uint32_t SMEM_LIMIT = 232448;              // dynamic shared memory per CTA on sm_100
 constexpr int TILE_N = 256;                          // output columns per tile
 
-// Tile configuration: CG CTAs per cluster (1 or 2) and TN output columns per tile (128 or 256).
+// Tile configuration: CG CTAs per cluster (1 or 2) and TN output columns per tile (64, 128 or 256;
+// the 2-SM pair always 256).
 template <int CG, int TN>
 struct Cfg {
     static constexpr int BM = 128 * CG;                 // output rows per tile (per CTA: 128)
@@ -997,9 +998,23 @@ static int clusters_for(int cg, int sm_count) {
     return cg == 2 ? resident_clusters<2, TILE_N>(sm_count) : resident_clusters<1, TILE_N>(sm_count);
 }
 
-// Tiles are TILE_N = 256 columns wide: narrower tiles need more operand traffic per FLOP and
-// measured 0.55-0.65x the throughput on B200. Picks the CTA group with fewer persistent waves,
-// preferring the 2-SM pair (less shared-memory traffic per FLOP); 2-SM tiles need M > 128.
+// Column width of a 1-SM launch's tiles. TILE_N = 256 wherever the 256-wide tiles fill the GPU:
+// narrower tiles need more operand traffic per FLOP and measured 0.55-0.65x the throughput there.
+// A launch whose 256-wide tiles occupy at most a quarter (half) of the SMs takes 64- (128-) wide
+// tiles instead: each CTA then stages a quarter (half) of the W rows and finishes a quarter (half)
+// of the columns, so a latency-bound launch (M = 64, N = 256: one CTA) spreads over more SMs. The
+// per-element arithmetic does not depend on the tile width. The gated epilogue pairs 32-column
+// pieces inside a tile and keeps 256; cube operands and routed stores keep 256 as well.
+static int choose_tn(int cg, int M, int N, int sm_count, const Params *p) {
+    if (cg != 1 || (p && (p->gate || p->a_maps || p->y_cube || p->route_rows))) return TILE_N;
+    const long long tiles = (long long)((M + 127) / 128) * ((N + TILE_N - 1) / TILE_N);
+    if (4 * tiles <= sm_count) return 64;
+    if (2 * tiles <= sm_count) return 128;
+    return TILE_N;
+}
+
+// Picks the CTA group with fewer persistent waves of 256-wide tiles, preferring the 2-SM pair (less
+// shared-memory traffic per FLOP); 2-SM tiles need M > 128.
 static int choose_cg(int M, int N, int sm_count) {
     if (M <= 128) return 1;
     long long waves[3];
@@ -1011,10 +1026,14 @@ static int choose_cg(int M, int N, int sm_count) {
     return waves[1] < waves[2] ? 1 : 2;
 }
 
-unsigned grid_for_variant(int cg, int M, int N, int sm_count) {
-    const long long tiles = (long long)((M + 128 * cg - 1) / (128 * cg)) * ((N + TILE_N - 1) / TILE_N);
+static unsigned grid_for_tile(int cg, int tn, int M, int N, int sm_count) {
+    const long long tiles = (long long)((M + 128 * cg - 1) / (128 * cg)) * ((N + tn - 1) / tn);
     const long long clusters = clusters_for(cg, sm_count);
     return (unsigned)((tiles < clusters ? tiles : clusters) * cg);
+}
+
+unsigned grid_for_variant(int cg, int M, int N, int sm_count) {
+    return grid_for_tile(cg, choose_tn(cg, M, N, sm_count, nullptr), M, N, sm_count);
 }
 
 unsigned grid_for(int M, int N, int sm_count) {
@@ -1023,9 +1042,11 @@ unsigned grid_for(int M, int N, int sm_count) {
 
 void config_for(int M, int N, int sm_count, unsigned *tile_m, unsigned *tile_n, unsigned *stages) {
     const int cg = choose_cg(M, N, sm_count);
+    const int tn = choose_tn(cg, M, N, sm_count, nullptr);
     *tile_m = 128u * cg;
-    *tile_n = (unsigned)TILE_N;
-    *stages = cg == 2 ? Cfg<2, TILE_N>::STAGES : Cfg<1, TILE_N>::STAGES;
+    *tile_n = (unsigned)tn;
+    *stages = cg == 2 ? Cfg<2, TILE_N>::STAGES
+                      : (tn == 64 ? Cfg<1, 64>::STAGES : tn == 128 ? Cfg<1, 128>::STAGES : Cfg<1, TILE_N>::STAGES);
 }
 
 template <int CG, int TN, int MODE>
@@ -1039,23 +1060,27 @@ static cudaError_t ensure_attr(int device) {
     return cudaSuccess;
 }
 
+// The shared-memory opt-in of every kernel a variant launches (narrow tiles have no gated form).
 template <int CG, int TN>
 static cudaError_t prepare_variant(int device, int sm_count) {
     resident_clusters<CG, TN>(sm_count);
     cudaError_t e = cudaSuccess;
     for (cudaError_t r : {ensure_attr<CG, TN, EPI_FP32>(device), ensure_attr<CG, TN, EPI_TILE16>(device),
-                          ensure_attr<CG, TN, EPI_RAW16>(device), ensure_attr<CG, TN, EPI_RAW32>(device),
-                          ensure_attr<CG, TN, EPI_GATED>(device)})
+                          ensure_attr<CG, TN, EPI_RAW16>(device), ensure_attr<CG, TN, EPI_RAW32>(device)})
         if (r != cudaSuccess) e = r;
+    if constexpr (TN == TILE_N)
+        if (ensure_attr<CG, TN, EPI_GATED>(device) != cudaSuccess) e = cudaErrorInvalidValue;
     return e;
 }
 
 cudaError_t prepare(int device, int sm_count) {
     if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
     if (!encode_fn()) return cudaErrorNotSupported;
-    const cudaError_t e1 = prepare_variant<1, TILE_N>(device, sm_count);
-    const cudaError_t e2 = prepare_variant<2, TILE_N>(device, sm_count);
-    return e1 != cudaSuccess ? e1 : e2;
+    cudaError_t e = cudaSuccess;
+    for (cudaError_t r : {prepare_variant<1, TILE_N>(device, sm_count), prepare_variant<2, TILE_N>(device, sm_count),
+                          prepare_variant<1, 64>(device, sm_count), prepare_variant<1, 128>(device, sm_count)})
+        if (r != cudaSuccess && e == cudaSuccess) e = r;
+    return e;
 }
 
 // Output tensor map of the TMA tile stores: FP16 [rows, ld] of which `cols` are valid, 32 x 32 boxes,
@@ -1114,13 +1139,16 @@ static cudaError_t launch_tile(const Shape &s, Params p, cudaStream_t stream, in
     p.kb_per_chunk = p.fold ? 256 / BK : p.num_kb;
     // Bands of 8 m-blocks keep a wave's X and W blocks L2-resident once X outgrows the L2.
     p.group_m = (p.num_m_blocks >= 16 && p.num_n_blocks >= 16 && (long long)p.M * p.K >= (64ll << 20)) ? 8 : 0;
-    const unsigned grid = grid_for_variant(CG, p.M, p.N, sm_count);
+    const unsigned grid = grid_for_tile(CG, TN, p.M, p.N, sm_count);
     if (grid_out) *grid_out = grid;
     if (p.out_mode == OUT_RAW32) return launch_mode<CG, TN, EPI_RAW32>(ta, tb, p, grid, stream, device);
     if (p.out_mode == OUT_RAW16) return launch_mode<CG, TN, EPI_RAW16>(ta, tb, p, grid, stream, device);
     if (p.gate) {
-        if (!p.fold || p.res || p.post || p.N != 2 * ((p.gate_n + 31) / 32 * 32)) return cudaErrorInvalidValue;
-        return launch_mode<CG, TN, EPI_GATED>(ta, tb, p, grid, stream, device);
+        if constexpr (TN != TILE_N) return cudaErrorInvalidValue;   // 32-column pairs need the 256-wide tile
+        else {
+            if (!p.fold || p.res || p.post || p.N != 2 * ((p.gate_n + 31) / 32 * 32)) return cudaErrorInvalidValue;
+            return launch_mode<CG, TN, EPI_GATED>(ta, tb, p, grid, stream, device);
+        }
     }
     if (p.fold) return launch_mode<CG, TN, EPI_TILE16>(ta, tb, p, grid, stream, device);
     return launch_mode<CG, TN, EPI_FP32>(ta, tb, p, grid, stream, device);
@@ -1129,8 +1157,11 @@ static cudaError_t launch_tile(const Shape &s, Params p, cudaStream_t stream, in
 cudaError_t launch_variant(int cg, const Shape &s, const Params &p, cudaStream_t stream, int device,
                            int sm_count, unsigned *grid_out) {
     if (cg == 2) return launch_tile<2, TILE_N>(s, p, stream, device, sm_count, grid_out);
-    if (cg == 1) return launch_tile<1, TILE_N>(s, p, stream, device, sm_count, grid_out);
-    return cudaErrorInvalidValue;
+    if (cg != 1) return cudaErrorInvalidValue;
+    const int tn = choose_tn(1, p.M, p.N, sm_count, &p);
+    if (tn == 64) return launch_tile<1, 64>(s, p, stream, device, sm_count, grid_out);
+    if (tn == 128) return launch_tile<1, 128>(s, p, stream, device, sm_count, grid_out);
+    return launch_tile<1, TILE_N>(s, p, stream, device, sm_count, grid_out);
 }
 
 cudaError_t launch(const Shape &s, Params p, cudaStream_t stream, int device, int sm_count,
