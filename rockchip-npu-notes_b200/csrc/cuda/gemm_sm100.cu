@@ -1014,9 +1014,13 @@ static int choose_tn(int cg, int M, int N, int sm_count, const Params *p) {
 }
 
 // Picks the CTA group with fewer persistent waves of 256-wide tiles, preferring the 2-SM pair (less
-// shared-memory traffic per FLOP); 2-SM tiles need M > 128.
+// shared-memory traffic per FLOP); 2-SM tiles need M > 128. A launch whose 1-SM 256-wide tiles fill
+// at most half of the SMs runs narrow 1-SM tiles instead (choose_tn): two or four times the CTAs of
+// the 1-SM form, each with a half or a quarter of the MMA work (measured against the pair: 512 x 4096
+// x 4096 tile-16 41.3 -> 34.9 us, 1000 x 1000 x 4096 41.0 -> 31.1 us, outputs bit-identical).
 static int choose_cg(int M, int N, int sm_count) {
     if (M <= 128) return 1;
+    if (2 * (long long)((M + 127) / 128) * ((N + TILE_N - 1) / TILE_N) <= sm_count) return 1;
     long long waves[3];
     for (int cg = 1; cg <= 2; ++cg) {
         const long long tiles = (long long)((M + 128 * cg - 1) / (128 * cg)) * ((N + TILE_N - 1) / TILE_N);
