@@ -48,6 +48,15 @@ enum { B2D_H2D = 0, B2D_D2H = 1, B2D_D2D = 2 };
 /* Pitched copy of `rows` rows of `width` bytes, asynchronous on the handle's stream. */
 int b2d_copy_2d(b2_dev *, void *dst, size_t dpitch, const void *src, size_t spitch,
                 size_t width, size_t rows, int kind);
+/* The same copy on the handle's side stream, ordered after all work issued so far on the handle's
+ * stream, then recorded under side event `ev` (< B2D_SIDE_EVENTS): an input copy in row bands that
+ * kernels on the handle's stream consume band by band (b2d_wait_side). Without a side stream the
+ * copy goes to the handle's stream. */
+#define B2D_SIDE_EVENTS 8u
+int b2d_copy_side(b2_dev *, void *dst, size_t dpitch, const void *src, size_t spitch,
+                  size_t width, size_t rows, int kind, unsigned ev);
+/* Work issued on the handle's stream after this call waits for the copy recorded under `ev`. */
+int b2d_wait_side(b2_dev *, unsigned ev);
 int b2d_memset(b2_dev *, void *ptr, int value, size_t bytes);
 /* Waits for the handle's stream; ROCKET_E_DEVICE if CUDA reported an error. */
 int b2d_sync(b2_dev *);

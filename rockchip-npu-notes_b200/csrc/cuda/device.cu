@@ -35,6 +35,10 @@ struct b2_dev {
     void *cube_host;        // pinned staging of the same bytes (= what the device copy holds)
     b2k_cube_tile *cube_key;   // [B2D_CUBE_MAX_VIEWS] the input view each device map describes
     unsigned cube_maps, cube_outs;   // slots the device copy holds valid contents for
+    // side stream of banded input copies (first use creates it; none if creation failed)
+    cudaStream_t side;
+    cudaEvent_t fork, side_ev[B2D_SIDE_EVENTS];
+    bool side_tried;
 };
 
 namespace {
@@ -134,6 +138,12 @@ void b2d_close(b2_dev *d) {
     if (!d) return;
     set_device(d);
     cudaStreamSynchronize(d->stream);
+    if (d->side) {
+        cudaStreamSynchronize(d->side);
+        cudaStreamDestroy(d->side);
+        cudaEventDestroy(d->fork);
+        for (unsigned i = 0; i < B2D_SIDE_EVENTS; ++i) cudaEventDestroy(d->side_ev[i]);
+    }
     cudaStreamDestroy(d->own);
     cudaFreeHost(d->flags);
     cudaFree(d->gemv.tsum);
@@ -201,6 +211,54 @@ int b2d_copy_2d(b2_dev *d, void *dst, size_t dpitch, const void *src, size_t spi
     if (dpitch == width && spitch == width) e = cudaMemcpyAsync(dst, src, width * rows, k, d->stream);
     else e = cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, k, d->stream);
     return rc_of(e);
+}
+
+// The side stream and its events, created on first use; false (and no side stream) if any creation
+// failed, in which case banded copies run on the handle's stream.
+static bool side_ready(b2_dev *d) {
+    if (d->side || d->side_tried) return d->side != nullptr;
+    d->side_tried = true;
+    cudaStream_t s = nullptr;
+    cudaEvent_t ev[B2D_SIDE_EVENTS + 1] = {};
+    bool ok = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess;
+    unsigned made = 0;
+    for (; ok && made <= B2D_SIDE_EVENTS; ++made)
+        ok = cudaEventCreateWithFlags(&ev[made], cudaEventDisableTiming) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        for (unsigned i = 0; i < made; ++i)
+            if (ev[i]) cudaEventDestroy(ev[i]);
+        if (s) cudaStreamDestroy(s);
+        return false;
+    }
+    d->side = s;
+    d->fork = ev[B2D_SIDE_EVENTS];
+    for (unsigned i = 0; i < B2D_SIDE_EVENTS; ++i) d->side_ev[i] = ev[i];
+    return true;
+}
+
+int b2d_copy_side(b2_dev *d, void *dst, size_t dpitch, const void *src, size_t spitch, size_t width, size_t rows,
+                  int kind, unsigned ev) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (ev >= B2D_SIDE_EVENTS) return ROCKET_E_SHAPE;
+    if (!side_ready(d)) return b2d_copy_2d(d, dst, dpitch, src, spitch, width, rows, kind);
+    const cudaMemcpyKind k = kind == B2D_H2D ? cudaMemcpyHostToDevice
+                             : kind == B2D_D2H ? cudaMemcpyDeviceToHost
+                                               : cudaMemcpyDeviceToDevice;
+    cudaError_t e = cudaEventRecord(d->fork, d->stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(d->side, d->fork, 0);
+    if (e == cudaSuccess && rows && width)
+        e = (dpitch == width && spitch == width) ? cudaMemcpyAsync(dst, src, width * rows, k, d->side)
+                                                 : cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, k, d->side);
+    if (e == cudaSuccess) e = cudaEventRecord(d->side_ev[ev], d->side);
+    return rc_of(e);
+}
+
+int b2d_wait_side(b2_dev *d, unsigned ev) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (ev >= B2D_SIDE_EVENTS) return ROCKET_E_SHAPE;
+    if (!d->side) return 0;   // the copies went to the handle's stream
+    return rc_of(cudaStreamWaitEvent(d->stream, d->side_ev[ev], 0));
 }
 
 int b2d_memset(b2_dev *d, void *ptr, int value, size_t bytes) {

@@ -160,6 +160,48 @@ static void test_ragged_and_fp32(int fd) {
     free(x); free(w); free(ref); free(y);
 }
 
+/* Large host-buffer runs copy X in row bands on a side stream (2 bands at 1100 rows, 8 at 4096; X of
+ * 8 MiB or more):
+ * the result equals the reference arithmetic and the unbanded CO_SEPARATE run, and a non-finite
+ * element in the first or the last band is refused with Y untouched. */
+static void test_banded_host_run(int fd) {
+    static const unsigned shapes[2][3] = {{1100, 4096, 16}, {4096, 1024, 8}};
+    for (int s = 0; s < 2; s++) {
+        const unsigned m = shapes[s][0], k = shapes[s][1], n = shapes[s][2];
+        uint16_t *x = alloc16((size_t)m * k), *w = alloc16((size_t)n * k), *b = alloc16(n);
+        uint16_t *ref = alloc16((size_t)m * n), *y1 = alloc16((size_t)m * n), *y2 = alloc16((size_t)m * n);
+        fill(x, (size_t)m * k, 1.0);
+        fill(w, (size_t)n * k, 1.0 / sqrt((double)k));
+        fill(b, n, 0.1);
+        CHECK(oracle_linear(TILE16_EXACT, m, k, n, x, w, b, 1, ref, NULL, NULL, 4) == 0, "oracle banded");
+        co_linear_hsig *chain = NULL, *sep = NULL;
+        CHECK(co_linear_hsig_create(fd, m, k, n, (const _Float16 *)w, (const _Float16 *)b, CO_CHAIN, &chain) == 0,
+              "create banded chain");
+        CHECK(co_linear_hsig_create(fd, m, k, n, (const _Float16 *)w, (const _Float16 *)b, CO_SEPARATE, &sep) == 0,
+              "create unbanded separate");
+        CHECK(co_linear_hsig_run(chain, (const _Float16 *)x, (_Float16 *)y1) == 0, "banded run");
+        CHECK(co_linear_hsig_run(sep, (const _Float16 *)x, (_Float16 *)y2) == 0, "unbanded run");
+        CHECK(memcmp(y1, ref, (size_t)m * n * 2) == 0, "banded run equals the reference arithmetic");
+        CHECK(memcmp(y2, y1, (size_t)m * n * 2) == 0, "banded equals unbanded");
+        const size_t bad[2] = {3, (size_t)(m - 1) * k + k / 2};   /* first band, last band */
+        for (int i = 0; i < 2; i++) {
+            memset(y1, 0x5a, (size_t)m * n * 2);
+            const uint16_t keep = x[bad[i]];
+            x[bad[i]] = 0x7e00u;   /* NaN */
+            CHECK(co_linear_hsig_run(chain, (const _Float16 *)x, (_Float16 *)y1) == ROCKET_E_SHAPE,
+                  "NaN in a band refused");
+            CHECK(y1[0] == 0x5a5au && y1[(size_t)m * n - 1] == 0x5a5au, "Y untouched after a refused band");
+            x[bad[i]] = keep;
+        }
+        CHECK(co_linear_hsig_run(chain, (const _Float16 *)x, (_Float16 *)y1) == 0 &&
+                  memcmp(y1, ref, (size_t)m * n * 2) == 0,
+              "banded run again after refusals");
+        co_linear_hsig_destroy(chain);
+        co_linear_hsig_destroy(sep);
+        free(x); free(w); free(b); free(ref); free(y1); free(y2);
+    }
+}
+
 static void test_create_failures(int fd) {
     const unsigned m = 32, k = 64, n = 64;
     uint16_t *w = alloc16((size_t)n * k), *b = alloc16(n);
@@ -262,6 +304,7 @@ int main(void) {
     if (fd < 0) return 1;
     test_hsig_against_reference(fd);
     test_ragged_and_fp32(fd);
+    test_banded_host_run(fd);
     test_create_failures(fd);
     test_cube_entry_and_guard(fd);
     rocket_close(fd);

@@ -80,6 +80,12 @@ int b2d_copy_2d(b2_dev *d, void *dst, size_t dpitch, const void *src, size_t spi
     for (size_t r = 0; r < rows; r++) memcpy((char *)dst + r * dpitch, (const char *)src + r * spitch, width);
     return 0;
 }
+int b2d_copy_side(b2_dev *d, void *dst, size_t dpitch, const void *src, size_t spitch, size_t width, size_t rows,
+                  int kind, unsigned ev) {
+    if (ev >= B2D_SIDE_EVENTS) return ROCKET_E_SHAPE;
+    return b2d_copy_2d(d, dst, dpitch, src, spitch, width, rows, kind);
+}
+int b2d_wait_side(b2_dev *d, unsigned ev) { return d && ev < B2D_SIDE_EVENTS ? 0 : ROCKET_E_SHAPE; }
 int b2d_memset(b2_dev *d, void *ptr, int value, size_t bytes) {
     (void)d;
     memset(ptr, value, bytes);

@@ -207,6 +207,40 @@ def test_device_entries_partial_and_epilogue(b2, gpu_fd):
     op.destroy()
 
 
+@pytest.mark.parametrize("m,k,n,acc", [(1100, 4096, 300, "tile16"), (4096, 1024, 520, "fp32")])
+def test_banded_host_run(b2, gpu_fd, m, k, n, acc):
+    """Host runs with 8 MiB or more of X and at least 1024 rows copy X in row bands on a side stream
+    and start each band's scan and GEMM as its rows land: the bytes equal the device entry's on the
+    same input (one launch over all rows), also on a caller's stream, and a NaN in the last band is
+    refused with Y untouched."""
+    torch = pytest.importorskip("torch")
+    x, w, b = uniform_case(m, n, k, 31)
+    op = b2.Linear(gpu_fd, m, k, n, w, b, post=b2.CO_LINEAR_HSIG,
+                   acc=b2.ACC_TILE16 if acc == "tile16" else b2.ACC_FP32, compat=acc == "tile16")
+    host = op.run(x)
+    xd = torch.from_numpy(x).cuda()
+    ldy = (n + 7) // 8 * 8
+    yd = torch.zeros((m, ldy), dtype=torch.float16, device="cuda")
+    torch.cuda.synchronize()
+    op.run_device(m, xd.data_ptr(), k, yd.data_ptr(), ldy)
+    b2.sync(gpu_fd)
+    assert b2.status(gpu_fd) == 0
+    assert np.array_equal(host.view(np.uint16), yd.cpu().numpy()[:, :n].view(np.uint16))
+    s = torch.cuda.Stream()
+    b2.set_stream(gpu_fd, s.cuda_stream)
+    try:
+        again = op.run(x)
+    finally:
+        b2.set_stream(gpu_fd, 0)
+    assert np.array_equal(again.view(np.uint16), host.view(np.uint16))
+    xbad = x.copy()
+    xbad[m - 1, k // 2] = np.nan
+    y = np.full((m, n), 3.0, np.float16)
+    assert op.run_rc(xbad, y) == b2.E_SHAPE
+    assert np.all(y == 3.0)
+    op.destroy()
+
+
 def test_caller_stream(b2, gpu_fd):
     torch = pytest.importorskip("torch")
     m, k, n = 256, 256, 256
