@@ -259,6 +259,22 @@ typedef struct {
 } b2k_rk_task;
 int b2d_rk_task(b2_dev *, const b2k_rk_task *task);
 
+/* A contraction chain of tasks whose intermediate results nothing else reads: MM over (x[0], w[0]),
+ * then MM_ACC over (x[i], w[i]) with the previous result as the prior for 0 < i < n, and with
+ * lut != 0 (an rk_template_id LUT value) that LUT on the last result. Only y (the last task's
+ * output) is written; every element gets the same arithmetic as the separate tasks (each chunk sum
+ * in q order in double, fp16 after every task). The n chunk sums run in parallel: `scratch` holds
+ * n * B * 256 doubles and `tickets` B words, zero on entry and left at zero, where B =
+ * ceil(y.physical_rows / 8) * ceil(y.physical_cols / 32). */
+#define B2K_RK_CHAIN_MAX 16u
+typedef struct {
+    b2k_rk_tile x[B2K_RK_CHAIN_MAX], w[B2K_RK_CHAIN_MAX], y;
+    unsigned n, lut;
+    double *scratch;
+    unsigned *tickets;
+} b2k_rk_chain;
+int b2d_rk_chain(b2_dev *, const b2k_rk_chain *chain);
+
 /* Download unpacking: the logical rows x cols of `src` into row-major device FP16 at dst with a
  * pitch of ld elements. */
 typedef struct {

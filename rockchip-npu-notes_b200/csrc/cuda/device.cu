@@ -870,6 +870,22 @@ int b2d_rk_task(b2_dev *d, const b2k_rk_task *t) {
     return rc_of(b2::rkplan::task(*t, d->stream, d->sm_count));
 }
 
+int b2d_rk_chain(b2_dev *d, const b2k_rk_chain *t) {
+    if (!set_device(d)) return ROCKET_E_DEVICE;
+    if (!t || !t->n || t->n > B2K_RK_CHAIN_MAX || (t->n < 2 && !t->lut) || !t->scratch || !t->tickets ||
+        !rk_tile_ok(t->y) || t->y.layout != B2K_RK_CUBE)
+        return ROCKET_E_SHAPE;
+    if (t->lut && !((t->lut >= 5 && t->lut <= 7) || t->lut == 10)) return ROCKET_E_SHAPE;
+    for (unsigned i = 0; i < t->n; ++i) {
+        const b2k_rk_tile &x = t->x[i], &w = t->w[i];
+        if (!rk_tile_ok(x) || x.layout != B2K_RK_CUBE || !rk_tile_ok(w) || w.layout != B2K_RK_WEIGHT ||
+            x.physical_cols > 256 || w.physical_cols != x.physical_cols || w.physical_rows < t->y.physical_cols ||
+            t->y.physical_rows > x.physical_rows)
+            return ROCKET_E_SHAPE;
+    }
+    return rc_of(b2::rkplan::chain(*t, d->stream));
+}
+
 int b2d_rk_unpack(b2_dev *d, const b2k_rk_unpack *items, unsigned count) {
     if (!set_device(d)) return ROCKET_E_DEVICE;
     if (count && !items) return ROCKET_E_SHAPE;

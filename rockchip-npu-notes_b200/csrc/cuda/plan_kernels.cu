@@ -5,7 +5,8 @@
 //   pack     every per-run upload of the schedule in one launch: the caller's FP16 windows (copied
 //            to HBM once per binding) are packed into the destination views' physical layouts,
 //            padding zeroed (research/custom-ops/src/rk_plan_runtime.c:244-339).
-//   task     one device task: the NPU program's arithmetic as the reference's host model of the NPU
+//   task     one device task (or a chain of contraction tasks whose intermediate results nothing else
+//            reads, as one launch): the NPU program's arithmetic as the reference's host model of the NPU
 //            states it (research/custom-ops/tests/mock/npu_mock.c:392-537): a matmul-shaped pass
 //            s(r, c) = sum over q of x[r][q] * w[c][q] accumulated in double in q order (every
 //            FP16 product is exact in double, so an FMA equals the separate multiply and add), the
@@ -175,6 +176,77 @@ __global__ void __launch_bounds__(CTHREADS) contract_kernel(const __grid_constan
     static_cast<unsigned short *>(t.y.ptr)[tile_index(t.y, r, c)] = round_f16(v);
 }
 
+// A chain: block (bx, by, z) stages chunk z's operands exactly as contract_kernel does and leaves its
+// 8 x 32 chunk sums in the scratch; the block that takes the last ticket of its output block folds
+// the n sums in chunk order (MM, then MM_ACC: fp16 after each), applies the LUT and stores y. The
+// partial stores, a fence and the ticket are the usual last-block hand-off; the folding block
+// reads the partials from L2 and puts the ticket back to zero for the next launch.
+__device__ __forceinline__ double lut(unsigned op, double v);
+
+__global__ void __launch_bounds__(CTHREADS) chain_kernel(const __grid_constant__ b2k_rk_chain t) {
+    extern __shared__ double sm[];
+    __shared__ unsigned ticket;
+    double *xs = sm;                  // [TR][KMAX]
+    double *ws = sm + TR * KMAX;      // [TC][WPITCH]
+    const unsigned tx = threadIdx.x % TC, ty = threadIdx.x / TC, z = blockIdx.z;
+    const unsigned r0 = blockIdx.y * TR, c0 = blockIdx.x * TC;
+    const b2k_rk_tile &X = t.x[z], &W = t.w[z];
+    const unsigned K = X.physical_cols;
+    const unsigned short *xg = static_cast<const unsigned short *>(X.ptr);
+    const unsigned short *wg = static_cast<const unsigned short *>(W.ptr);
+    constexpr int J = KMAX / 32;
+    unsigned short xv[J], wv[TC / TR][J];
+    const unsigned r = r0 + ty;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const unsigned q = tx + 32 * j;
+        xv[j] = (r < X.physical_rows && q < K) ? xg[tile_index(X, r, q)] : (unsigned short)0;
+    }
+#pragma unroll
+    for (int i = 0; i < TC / TR; ++i) {
+        const unsigned c = c0 + ty + TR * i;
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            const unsigned q = tx + 32 * j;
+            wv[i][j] = (c < W.physical_rows && q < K) ? wg[tile_index(W, c, q)] : (unsigned short)0;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) xs[ty * KMAX + tx + 32 * j] = (double)__half2float(__ushort_as_half(xv[j]));
+#pragma unroll
+    for (int i = 0; i < TC / TR; ++i)
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+            ws[(ty + TR * i) * WPITCH + tx + 32 * j] = (double)__half2float(__ushort_as_half(wv[i][j]));
+    __syncthreads();
+    const unsigned c = c0 + tx;
+    const bool live = r < t.y.physical_rows && c < t.y.physical_cols;
+    double s = 0.0;
+    if (live) {
+        const double *xr = xs + ty * KMAX, *wr = ws + tx * WPITCH;
+#pragma unroll 16
+        for (unsigned q = 0; q < K; ++q) s = __fma_rn(xr[q], wr[q], s);
+    }
+    const size_t blk = (size_t)blockIdx.y * gridDim.x + blockIdx.x;
+    const size_t stride = (size_t)gridDim.x * gridDim.y * CTHREADS;   // doubles per chunk
+    t.scratch[z * stride + blk * CTHREADS + threadIdx.x] = s;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) ticket = atomicAdd(&t.tickets[blk], 1u);
+    __syncthreads();
+    if (ticket != t.n - 1) return;
+    __threadfence();
+    if (live) {
+        const double *part = t.scratch + blk * CTHREADS + threadIdx.x;
+        unsigned short run = round_f16(__ldcg(part));
+        for (unsigned i = 1; i < t.n; ++i)
+            run = round_f16(__dadd_rn(__ldcg(part + i * stride), (double)__half2float(__ushort_as_half(run))));
+        if (t.lut) run = round_f16(lut(t.lut, (double)__half2float(__ushort_as_half(run))));
+        static_cast<unsigned short *>(t.y.ptr)[tile_index(t.y, r, c)] = run;
+    }
+    if (threadIdx.x == 0) t.tickets[blk] = 0u;
+}
+
 __device__ __forceinline__ double lut(unsigned op, double v) {
     switch (op) {
     case 5: return __ddiv_rn(1.0, __dadd_rn(1.0, exp(-v)));                          // sigmoid
@@ -212,7 +284,10 @@ static unsigned blocks_for(size_t work, int sm_count) {
 }
 
 cudaError_t prepare() {
-    return cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CONTRACT_SMEM);
+    const cudaError_t e =
+        cudaFuncSetAttribute(contract_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CONTRACT_SMEM);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CONTRACT_SMEM);
 }
 
 cudaError_t pack(const PackTable &t, size_t max_vectors, cudaStream_t s, int sm_count) {
@@ -228,6 +303,12 @@ cudaError_t task(const b2k_rk_task &t, cudaStream_t s, int sm_count) {
         const dim3 grid((t.y.physical_cols + TC - 1) / TC, (t.y.physical_rows + TR - 1) / TR);
         contract_kernel<<<grid, CTHREADS, CONTRACT_SMEM, s>>>(t);
     }
+    return cudaGetLastError();
+}
+
+cudaError_t chain(const b2k_rk_chain &t, cudaStream_t s) {
+    const dim3 grid((t.y.physical_cols + TC - 1) / TC, (t.y.physical_rows + TR - 1) / TR, t.n);
+    chain_kernel<<<grid, CTHREADS, CONTRACT_SMEM, s>>>(t);
     return cudaGetLastError();
 }
 

@@ -18,11 +18,12 @@ struct UnpackTable {
     unsigned count;
 };
 
-// The contraction kernel's shared-memory opt-in (over 48 KB) on the current device: done when a device
+// The contraction kernels' shared-memory opt-in (over 48 KB) on the current device: done when a device
 // handle opens, outside any stream capture.
 cudaError_t prepare();
 cudaError_t pack(const PackTable &t, size_t max_vectors, cudaStream_t s, int sm_count);
 cudaError_t task(const b2k_rk_task &t, cudaStream_t s, int sm_count);
+cudaError_t chain(const b2k_rk_chain &t, cudaStream_t s);
 cudaError_t unpack(const UnpackTable &t, size_t max_elements, cudaStream_t s, int sm_count);
 
 }  // namespace rkplan

@@ -964,6 +964,12 @@ struct rk_workspace {
     b2k_rk_unpack *unpacks;          /* downloads in action order */
     uint32_t nunpacks;
     struct rk_step { uint32_t kind, first, count; } *steps;   /* the run, in action order */
+    b2k_rk_chain *chains;            /* fused contraction chains (find_chains) */
+    uint32_t nchains;
+    uint32_t *chain_head;            /* [nactions]: chain index + 1 where a chain starts, else 0 */
+    unsigned char *chain_member;     /* [nactions]: a task folded into the chain before it */
+    void *chain_scratch, *chain_tickets;
+    size_t chain_scratch_bytes, chain_ticket_bytes;
     uint32_t nsteps;
     void **guard_base;               /* allocated slots for the guard check */
     size_t *guard_payload;
@@ -1062,11 +1068,118 @@ static int is_constant_upload(const rk_plan *p, const rk_action_desc *a) {
     return a->kind == RK_ACTION_UPLOAD && p->values[a->source_binding].role == RK_ROLE_CONSTANT;
 }
 
+/* ------------------------------------------------------------------------------ task chains
+ * A chain is MM, then MM_ACC tasks that each take the previous result as their prior, then
+ * optionally a LUT task on the last result: consecutive actions whose intermediate results nothing
+ * else reads. It runs as one launch that computes the chunk sums in parallel and stores only the
+ * final result (b2d_rk_chain), with the separate tasks' arithmetic. An intermediate result is
+ * "dead" after its reader when no later action reads any of its bytes before a task output or an
+ * upload (uploads rewrite their whole destination view) covers all of them; a LUT reader that writes
+ * in place ends the life of its input itself. */
+static void view_range(const rk_workspace *ws, uint32_t v, uintptr_t *lo, uintptr_t *hi) {
+    *lo = (uintptr_t)ws->tiles[v].ptr;
+    *hi = *lo + ws->plan->views[v].tensor.bytes;
+}
+
+static int views_overlap(const rk_workspace *ws, uint32_t a, uint32_t b) {
+    uintptr_t alo, ahi, blo, bhi;
+    view_range(ws, a, &alo, &ahi);
+    view_range(ws, b, &blo, &bhi);
+    return alo < bhi && blo < ahi;
+}
+
+static int same_view(const rk_workspace *ws, uint32_t a, uint32_t b) {
+    return ws->tiles[a].ptr == ws->tiles[b].ptr &&
+           same_geometry(&ws->plan->views[a].tensor, &ws->plan->views[b].tensor);
+}
+
+static int dead_after(const rk_workspace *ws, uint32_t v, uint32_t reader) {
+    const rk_plan *p = ws->plan;
+    uintptr_t lo, hi;
+    view_range(ws, v, &lo, &hi);
+    for (uint32_t j = reader; j < p->d.nactions; j++) {
+        const rk_action_desc *a = &p->actions[j];
+        for (uint32_t k = 0; k < a->ninputs && j > reader; k++)   /* the reader's own reads are checked by the caller */
+            if (views_overlap(ws, a->inputs[k], v)) return 0;
+        if ((a->kind == RK_ACTION_NPU_TASK || a->kind == RK_ACTION_UPLOAD) && a->noutputs) {
+            uintptr_t wlo, whi;
+            view_range(ws, a->outputs[0], &wlo, &whi);
+            if (wlo <= lo && hi <= whi) return 1;
+        }
+    }
+    return 1;
+}
+
+static int is_lut_template(uint32_t t) {
+    return t == RK_TEMPLATE_LUT_SIGMOID_F16 || t == RK_TEMPLATE_LUT_HARDSIGMOID_F16 ||
+           t == RK_TEMPLATE_LUT_GELU_GATE_F16 || t == RK_TEMPLATE_LUT_RSQRT_F16;
+}
+
+/* Finds the chains; returns the scratch doubles and ticket words the largest one needs. */
+static void find_chains(rk_workspace *ws, size_t *scratch_doubles, size_t *tickets) {
+    const rk_plan *p = ws->plan;
+    const uint32_t na = p->d.nactions;
+    *scratch_doubles = *tickets = 0;
+    ws->nchains = 0;
+    for (uint32_t i = 0; i < na; i++) {
+        const rk_action_desc *a = &p->actions[i];
+        if (a->kind != RK_ACTION_NPU_TASK || a->template_id != RK_TEMPLATE_MM_F16) continue;
+        b2k_rk_chain ch;
+        memset(&ch, 0, sizeof(ch));
+        ch.x[0] = ws->tiles[a->inputs[0]];
+        ch.w[0] = ws->tiles[a->inputs[1]];
+        ch.n = 1;
+        uint32_t out = a->outputs[0], end = i;
+        void *lut_dst = NULL;
+        while (end + 1 < na && !ch.lut) {
+            const uint32_t j = end + 1;
+            const rk_action_desc *b = &p->actions[j];
+            if (b->kind != RK_ACTION_NPU_TASK) break;
+            if (b->template_id == RK_TEMPLATE_MM_ACC_F16 && ch.n < B2K_RK_CHAIN_MAX) {
+                if (!same_view(ws, b->inputs[2], out) ||
+                    !same_geometry(&p->views[out].tensor, &p->views[b->outputs[0]].tensor) ||
+                    views_overlap(ws, b->inputs[0], out) || views_overlap(ws, b->inputs[1], out) ||
+                    !dead_after(ws, out, j))
+                    break;
+                ch.x[ch.n] = ws->tiles[b->inputs[0]];
+                ch.w[ch.n] = ws->tiles[b->inputs[1]];
+                ch.n++;
+            } else if (is_lut_template(b->template_id)) {
+                /* element-wise over physical elements: its input must be exactly the bytes of the
+                 * last result (in any layout of the same size) and its output as many bytes, so the
+                 * final tile is the last result's geometry at the LUT's destination */
+                if (ws->tiles[b->inputs[0]].ptr != ws->tiles[out].ptr ||
+                    p->views[b->inputs[0]].tensor.bytes != p->views[out].tensor.bytes ||
+                    p->views[b->outputs[0]].tensor.bytes != p->views[out].tensor.bytes || !dead_after(ws, out, j))
+                    break;
+                ch.lut = b->template_id;
+                lut_dst = ws->tiles[b->outputs[0]].ptr;
+                end = j;
+                break;
+            } else {
+                break;
+            }
+            out = b->outputs[0];
+            end = j;
+        }
+        if (end == i) continue;
+        ch.y = ws->tiles[out];
+        if (lut_dst) ch.y.ptr = lut_dst;
+        const size_t blocks = (size_t)((ch.y.physical_rows + 7) / 8) * ((ch.y.physical_cols + 31) / 32);
+        if (ch.n * blocks * 256 > *scratch_doubles) *scratch_doubles = ch.n * blocks * 256;
+        if (blocks > *tickets) *tickets = blocks;
+        ws->chains[ws->nchains] = ch;
+        ws->chain_head[i] = ++ws->nchains;
+        for (uint32_t j = i + 1; j <= end; j++) ws->chain_member[j] = 1;
+        i = end;
+    }
+}
+
 /* The per-run device schedule, in action order: a run of consecutive per-run uploads (neither
- * constant nor persistent) is one pack launch, each task one launch, a run of consecutive
- * downloads one unpack launch. Order matters: a plan may map buffers with disjoint live ranges to
- * one slot, so an upload or download may only run at its own position. */
-enum { STEP_PACK = 0, STEP_TASK = 1, STEP_UNPACK = 2 };
+ * constant nor persistent) is one pack launch, each task (or chain) one launch, a run of
+ * consecutive downloads one unpack launch. Order matters: a plan may map buffers with disjoint live
+ * ranges to one slot, so an upload or download may only run at its own position. */
+enum { STEP_PACK = 0, STEP_TASK = 1, STEP_UNPACK = 2, STEP_CHAIN = 3 };
 
 static void build_schedule(rk_workspace *ws) {
     const rk_plan *p = ws->plan;
@@ -1086,7 +1199,9 @@ static void build_schedule(rk_workspace *ws) {
             ws->upload_calls++;
             ws->upload_bytes += p->views[a->outputs[0]].tensor.bytes;
         } else if (a->kind == RK_ACTION_NPU_TASK) {
-            ws->steps[ws->nsteps++] = (struct rk_step){STEP_TASK, task++, 1};
+            if (ws->chain_head[i]) ws->steps[ws->nsteps++] = (struct rk_step){STEP_CHAIN, ws->chain_head[i] - 1, 1};
+            else if (!ws->chain_member[i]) ws->steps[ws->nsteps++] = (struct rk_step){STEP_TASK, task, 1};
+            task++;
         } else if (a->kind == RK_ACTION_DOWNLOAD) {
             if (!last || last->kind != STEP_UNPACK) ws->steps[ws->nsteps++] = (struct rk_step){STEP_UNPACK, unpack, 0};
             ws->steps[ws->nsteps - 1].count++;
@@ -1102,6 +1217,7 @@ static int issue_schedule(rk_workspace *ws) {
         const struct rk_step *st = &ws->steps[i];
         if (st->kind == STEP_PACK) rc = b2d_rk_pack(ws->dev, ws->packs + st->first, st->count);
         else if (st->kind == STEP_TASK) rc = b2d_rk_task(ws->dev, &ws->tasks[st->first]);
+        else if (st->kind == STEP_CHAIN) rc = b2d_rk_chain(ws->dev, &ws->chains[st->first]);
         else rc = b2d_rk_unpack(ws->dev, ws->unpacks + st->first, st->count);
     }
     for (uint32_t g = 0; g < ws->nguard && !rc; g += B2K_MAX_CUBE_TILES) {
@@ -1134,12 +1250,15 @@ static void workspace_free(rk_workspace *ws) {
     b2h_free(ws->fd, ws->in_dev, ws->in_bytes);
     b2h_free(ws->fd, ws->out_dev, ws->out_bytes);
     b2h_free(ws->fd, ws->scratch_dev, ws->scratch_bytes);
+    b2h_free(ws->fd, ws->chain_scratch, ws->chain_scratch_bytes);
+    b2h_free(ws->fd, ws->chain_tickets, ws->chain_ticket_bytes);
     b2d_host_free(ws->out_host);
     b2d_host_free(ws->in_host);
     free(ws->slots); free(ws->tiles); free(ws->in_off); free(ws->in_needed); free(ws->out_off);
     free(ws->packs); free(ws->tasks); free(ws->unpacks); free(ws->steps); free(ws->guard_base);
     free(ws->guard_payload);
     free(ws->persistent);
+    free(ws->chains); free(ws->chain_head); free(ws->chain_member);
     plan_free(ws->plan);
     free(ws);
 }
@@ -1231,8 +1350,12 @@ static int workspace_create_impl(int fd, const rk_plan *plan, const rk_binding *
     ws->guard_base = calloc(nb, sizeof(void *));
     ws->guard_payload = calloc(nb, sizeof(size_t));
     ws->persistent = calloc(na, 1);
+    ws->chains = calloc(na ? na : 1, sizeof(b2k_rk_chain));
+    ws->chain_head = calloc(na ? na : 1, sizeof(uint32_t));
+    ws->chain_member = calloc(na ? na : 1, 1);
     if (!ws->slots || !ws->tiles || !ws->in_off || !ws->in_needed || !ws->out_off || !ws->packs || !ws->tasks ||
-        !ws->unpacks || !ws->steps || !ws->guard_base || !ws->guard_payload || !ws->persistent) {
+        !ws->unpacks || !ws->steps || !ws->guard_base || !ws->guard_payload || !ws->persistent || !ws->chains ||
+        !ws->chain_head || !ws->chain_member) {
         workspace_free(ws);
         return WS_FAIL("workspace_create", RK_E_NOMEM, "out of memory");
     }
@@ -1320,6 +1443,24 @@ static int workspace_create_impl(int fd, const rk_plan *plan, const rk_binding *
         }
     }
     for (uint32_t s = 0; s < p->d.nsubmits; s++) ws->task_count += p->submits[s].ntask_ids;
+    size_t chain_doubles = 0, chain_words = 0;
+    find_chains(ws, &chain_doubles, &chain_words);
+    if (ws->nchains) {
+        ws->chain_scratch_bytes = chain_doubles * sizeof(double);
+        ws->chain_ticket_bytes = chain_words * sizeof(unsigned);
+        rc = b2h_malloc(fd, ws->chain_scratch_bytes, &ws->chain_scratch);
+        if (!rc) rc = b2h_malloc(fd, ws->chain_ticket_bytes, &ws->chain_tickets);
+        if (rc) {
+            workspace_free(ws);
+            return diag_set(diag, rc == ROCKET_E_NOMEM ? RK_E_NOMEM : RK_E_DEVICE, "workspace_create",
+                            "chain scratch allocation failed", UINT32_MAX, NULL, rc);
+        }
+        ws->device_bytes += ws->chain_scratch_bytes + ws->chain_ticket_bytes;
+        for (uint32_t c = 0; c < ws->nchains; c++) {
+            ws->chains[c].scratch = ws->chain_scratch;
+            ws->chains[c].tickets = ws->chain_tickets;
+        }
+    }
     build_schedule(ws);
     rc = upload_constants(ws, constants, nconstants, diag);
     if (rc) {

@@ -494,6 +494,36 @@ int b2d_rk_task(b2_dev *d, const b2k_rk_task *t) {
     return 0;
 }
 
+/* The chain as its separate tasks into host temporaries: only y is written (the intermediate
+ * views are left as they were, as on the device). */
+int b2d_rk_chain(b2_dev *d, const b2k_rk_chain *t) {
+    if (!d || !t || !t->n || t->n > B2K_RK_CHAIN_MAX || (t->n < 2 && !t->lut)) return ROCKET_E_SHAPE;
+    const size_t elems = (size_t)t->y.physical_rows * t->y.physical_cols;
+    uint16_t *tmp[2] = {calloc(elems, 2), calloc(elems, 2)};
+    int rc = tmp[0] && tmp[1] ? 0 : ROCKET_E_NOMEM;
+    rk_oracle_tile y = mock_tile(&t->y), prev = y;
+    for (unsigned i = 0; !rc && i <= t->n; i++) {
+        if (i == t->n && !t->lut) break;
+        const int last = t->lut ? i == t->n : i == t->n - 1;
+        rk_oracle_tile out = y;
+        if (!last) out.p = tmp[i & 1];
+        if (i == t->n) {
+            rc = rk_oracle_task((int)t->lut, &prev, &prev, &prev, &out);
+        } else {
+            rk_oracle_tile x = mock_tile(&t->x[i]), w = mock_tile(&t->w[i]);
+            rc = rk_oracle_task(i ? 2 : 1, &x, &w, &prev, &out);
+        }
+        prev = out;
+        mock_rk_tasks++;
+    }
+    free(tmp[0]);
+    free(tmp[1]);
+    if (rc) return ROCKET_E_SHAPE;
+    if (mock_rk_inject == 1) y.p[0] = 0x7e00;
+    if (mock_rk_inject == 2) ((unsigned char *)y.p)[(size_t)y.prows * y.pcols * 2] ^= 0x5a;
+    return 0;
+}
+
 int b2d_rk_unpack(b2_dev *d, const b2k_rk_unpack *items, unsigned count) {
     if (!d || (count && !items)) return ROCKET_E_SHAPE;
     for (unsigned i = 0; i < count; i++) {
