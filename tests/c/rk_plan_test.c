@@ -543,6 +543,71 @@ static void kacc_case(int fd) {
     rk_plan_destroy(plan);
 }
 
+/* The same K accumulation with the MM partial also downloaded after the MM_ACC: the partial is
+ * read after its chain reader, so the two tasks must run separately and both outputs hold their
+ * own results (a chain would leave the partial unwritten; the CPU seam writes only a chain's final
+ * tile, like the device). */
+static void kacc_observed_case(int fd) {
+    enum { M = 40, K = 300, N = 48 };
+    static pb b;
+    memset(&b, 0, sizeof(b));
+    const uint32_t X = pb_value(&b, RK_ROLE_INPUT, 2, M, K, "X");
+    const uint32_t W = pb_value(&b, RK_ROLE_CONSTANT, 2, N, K, "W");
+    const uint32_t Y = pb_value(&b, RK_ROLE_OUTPUT, 2, M, N, "Y");
+    const uint32_t P = pb_value(&b, RK_ROLE_OUTPUT, 2, M, N, "P");
+    const uint32_t x0 = pb_view(&b, RK_LAYOUT_CUBE_F16, M, 256, RK_ROLE_INPUT_SLICE);
+    const uint32_t x1 = pb_view(&b, RK_LAYOUT_CUBE_F16, M, K - 256, RK_ROLE_INPUT_SLICE);
+    const uint32_t w0 = pb_view(&b, RK_LAYOUT_WEIGHT_F16, N, 256, RK_ROLE_WEIGHT);
+    const uint32_t w1 = pb_view(&b, RK_LAYOUT_WEIGHT_F16, N, K - 256, RK_ROLE_WEIGHT);
+    const uint32_t ya = pb_view(&b, RK_LAYOUT_CUBE_F16, M, N, RK_ROLE_ACCUMULATOR);
+    const uint32_t yb = pb_view(&b, RK_LAYOUT_CUBE_F16, M, N, RK_ROLE_OUTPUT);
+    const uint32_t ux0 = pb_upload(&b, X, x0, 0, 0, 0), ux1 = pb_upload(&b, X, x1, 0, 256, 0);
+    const uint32_t uw0 = pb_upload(&b, W, w0, 0, 0, RK_ACTION_FLAG_CACHE_CONSTANT);
+    const uint32_t uw1 = pb_upload(&b, W, w1, 0, 256, RK_ACTION_FLAG_CACHE_CONSTANT);
+    const uint32_t t0 = pb_task(&b, RK_TEMPLATE_MM_F16, (uint32_t[]){x0, w0}, 2, ya, (uint32_t[]){ux0, uw0}, 2);
+    const uint32_t t1 = pb_task(&b, RK_TEMPLATE_MM_ACC_F16, (uint32_t[]){x1, w1, ya}, 3, yb,
+                                (uint32_t[]){ux1, uw1, t0}, 3);
+    b.actions[t0].source_k_count = b.actions[t1].source_k_count = 2;
+    b.actions[t1].source_k_index = 1;
+    pb_download(&b, Y, yb, t1, 0, 0);
+    pb_download(&b, P, ya, t1, 0, 0);
+    pb_submit(&b, t0, 2);
+    rk_plan_desc desc = pb_desc(&b);
+    rk_diag diag;
+    rk_plan *plan = NULL;
+    EXPECT(rk_plan_create(&desc, &plan, &diag) == 0);
+    if (!plan) {
+        fprintf(stderr, "  kacc observed create: %s\n", diag.message);
+        return;
+    }
+    static _Float16 x[M * K], w[N * K], y[M * N], part[M * N], ref[M * N], pref[M * N];
+    for (int i = 0; i < M * K; i++) x[i] = (_Float16)((double)pattern((unsigned)i, 5) * 4.0);
+    for (int i = 0; i < N * K; i++) w[i] = pattern((unsigned)i, 13);
+    for (int r = 0; r < M; r++)
+        for (int c = 0; c < N; c++) {
+            double s0 = 0, s1 = 0;
+            for (int q = 0; q < 256; q++) s0 += (double)x[r * K + q] * (double)w[c * K + q];
+            for (int q = 256; q < K; q++) s1 += (double)x[r * K + q] * (double)w[c * K + q];
+            pref[r * N + c] = (_Float16)s0;
+            ref[r * N + c] = (_Float16)(s1 + (double)(_Float16)s0);
+        }
+    rk_binding constants[] = {binding(&b.values[W], w)};
+    rk_workspace *ws = NULL;
+    EXPECT(rk_workspace_create(fd, plan, constants, 1, &ws, &diag) == 0);
+    if (ws) {
+        rk_binding in[] = {binding(&b.values[X], x)};
+        rk_binding out[] = {binding(&b.values[Y], y), binding(&b.values[P], part)};
+        rk_run_report report;
+        memset(y, 0x23, sizeof(y));
+        memset(part, 0x23, sizeof(part));
+        EXPECT(rk_workspace_run(ws, in, 1, out, 2, &report, &diag) == 0);
+        EXPECT(!memcmp(y, ref, sizeof(y)));
+        EXPECT(!memcmp(part, pref, sizeof(part)));
+        EXPECT(rk_workspace_destroy(ws, &diag) == 0);
+    }
+    rk_plan_destroy(plan);
+}
+
 /* ------------------------------------------------------------------------------ EW, LUT, broadcast */
 enum { EM = 20, EN = 72, EP = 96, ETILES = 10 };
 
@@ -901,6 +966,7 @@ int main(void) {
     EXPECT(rk_target_check(&diag) == 0);
     multitile_case(fd);
     kacc_case(fd);
+    kacc_observed_case(fd);
     ew_case(fd);
     many_uploads_case(fd);
     rocket_close(fd);
