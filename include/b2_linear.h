@@ -134,10 +134,12 @@ int b2_linear_group_run_device(b2_linear *const *ops, unsigned count, unsigned m
 typedef struct {
     unsigned m, k, n;
     unsigned kernel;             /* 0 = tcgen05 GEMM, 1 = GEMV (small M) */
-    unsigned tile_m, tile_n, tile_k;
+    unsigned tile_m, tile_n, tile_k;   /* GEMM tile_n: 256, or 128 / 64 for 1-SM launches whose 256-wide
+                                           tiles would fill at most half / a quarter of the SMs */
     unsigned stages;             /* GEMM: TMA ring depth; streamed GEMV: copy slots (6, 11 or 12); else 0 */
     unsigned grid;               /* CTAs of the main kernel for the create-time m */
-    unsigned launches_per_run;   /* CUDA launches of one co_linear_run */
+    unsigned launches_per_run;   /* CUDA launches of one co_linear_run (scan + GEMM per row band when a
+                                    large input is copied in bands) */
     enum b2_accumulate acc;
     size_t device_bytes;         /* HBM held by the operator */
 } b2_linear_info;

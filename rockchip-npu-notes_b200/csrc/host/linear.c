@@ -589,7 +589,7 @@ int b2_linear_get_info(const b2_linear *c, b2_linear_info *info) {
     if (rc) return rc;
     *info = (b2_linear_info){c->plan.m, c->plan.k, c->plan.n, cfg.kernel, cfg.tile_m, cfg.tile_n,
                              cfg.tile_k, cfg.stages, cfg.grid,
-                             1u + (c->mode == CO_CHAIN ? 1u : 2u), c->acc,
+                             host_bands(c) * (1u + (c->mode == CO_CHAIN ? 1u : 2u)), c->acc,
                              c->bytes + c->ws_bytes};
     return 0;
 }
