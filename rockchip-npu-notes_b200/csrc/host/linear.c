@@ -210,12 +210,18 @@ int co_linear_hsig_run(co_linear_hsig *c, const _Float16 *x, _Float16 *y) {
         /* band i: rows [m * i / bands, m * (i + 1) / bands) rounded down to multiples of 128 */
         unsigned r[B2D_SIDE_EVENTS + 1];
         for (unsigned i = 0; i <= bands; i++) r[i] = i == bands ? m : (unsigned)((size_t)m * i / bands) & ~127u;
-        for (unsigned i = 0; !rc && i < bands; i++)
+        unsigned issued = 0;
+        for (unsigned i = 0; !rc && i < bands; i++) {
             rc = b2d_copy_side(d, (_Float16 *)c->x + (size_t)r[i] * c->ldx, c->ldx * 2, x + (size_t)r[i] * k, (size_t)k * 2,
                                (size_t)k * 2, r[i + 1] - r[i], B2D_H2D, i);
-        for (unsigned i = 0; !rc && i < bands; i++) {
+            if (!rc) issued = i + 1;
+        }
+        /* the handle's stream waits for every band that was issued, also after an error, so that the
+         * sync below covers the copies still reading the caller's X */
+        for (unsigned i = 0; i < issued; i++) {
             const _Float16 *xb = (const _Float16 *)c->x + (size_t)r[i] * c->ldx;
-            rc = b2d_wait_side(d, i);
+            const int wrc = b2d_wait_side(d, i);
+            if (!rc) rc = wrc;
             if (!rc) {
                 rc = b2d_scan_nonfinite(d, xb, r[i + 1] - r[i], k, c->ldx, B2_STATUS_NONFINITE_INPUT);
                 launches += !rc;

@@ -217,7 +217,9 @@ def test_banded_host_run(b2, gpu_fd, m, k, n, acc):
     x, w, b = uniform_case(m, n, k, 31)
     op = b2.Linear(gpu_fd, m, k, n, w, b, post=b2.CO_LINEAR_HSIG,
                    acc=b2.ACC_TILE16 if acc == "tile16" else b2.ACC_FP32, compat=acc == "tile16")
+    before = b2.counters()["launches"]
     host = op.run(x)
+    assert b2.counters()["launches"] - before == op.info().launches_per_run == 2 * (m // 512 if m // 512 < 8 else 8)
     xd = torch.from_numpy(x).cuda()
     ldy = (n + 7) // 8 * 8
     yd = torch.zeros((m, ldy), dtype=torch.float16, device="cuda")
