@@ -33,6 +33,7 @@ struct co_linear_hsig {
     void *x; size_t ldx;            /* FP16 staging [m, ldx] */
     void *y; size_t ldy;            /* FP16 staging [m, ldy] */
     float *ws; size_t ws_bytes;     /* FP32 workspace, separate mode with FP32 accumulation */
+    void *y_stage;                  /* pinned host copy of Y for small outputs (host runs), or NULL */
     size_t bytes;                   /* HBM held, excluding the lazily sized workspace */
 };
 
@@ -59,9 +60,15 @@ void co_linear_hsig_destroy(co_linear_hsig *c) {
     b2h_free(c->fd, c->x, (size_t)c->plan.m * c->ldx * 2);
     b2h_free(c->fd, c->y, (size_t)c->plan.m * c->ldy * 2);
     b2h_free(c->fd, c->ws, c->ws_bytes);
+    b2d_host_free(c->y_stage);
     free(c);
 }
 void co_linear_destroy(co_linear *c) { co_linear_hsig_destroy(c); }
+
+/* Host runs whose Y is at most this many bytes copy it into pinned staging right behind the
+ * kernels, sync once, check the status and then copy it to the caller's Y on the host: one
+ * stream synchronisation fewer than copying into Y after the check. */
+#define Y_STAGE_MAX ((size_t)64 << 10)
 
 static int upload_weights(co_linear_hsig *c, const _Float16 *w, const _Float16 *b) {
     b2_dev *d = b2h_dev(c->fd);
@@ -105,6 +112,7 @@ static int create_impl(int fd, unsigned m, unsigned k, unsigned n, const _Float1
         return rc;
     }
     c->bytes = plan.device_bytes;
+    if ((size_t)m * n * 2 <= Y_STAGE_MAX) c->y_stage = b2d_host_alloc((size_t)m * n * 2);   /* NULL: direct copy */
     *out = c;
     return 0;
 }
@@ -232,13 +240,16 @@ int co_linear_hsig_run(co_linear_hsig *c, const _Float16 *x, _Float16 *y) {
             }
         }
     }
+    if (!rc && c->y_stage) rc = b2d_copy_2d(d, c->y_stage, (size_t)n * 2, c->y, c->ldy * 2, (size_t)n * 2, m, B2D_D2H);
     int sync_rc = b2d_sync(d);
     if (!rc) rc = sync_rc;
     uint32_t st = b2d_status(d, 1);
     b2d_status_merge(d, prior);
     if (!rc && b2h_fault(B2_FAULT_NAN_OUTPUT)) st |= B2_STATUS_NONFINITE_OUTPUT;
     if (!rc) rc = status_rc(st, 1);
-    if (!rc) {
+    if (!rc && c->y_stage) {
+        memcpy(y, c->y_stage, (size_t)m * n * 2);
+    } else if (!rc) {
         rc = b2d_copy_2d(d, y, (size_t)n * 2, c->y, c->ldy * 2, (size_t)n * 2, m, B2D_D2H);
         if (!rc) rc = b2d_sync(d);
     }
