@@ -184,17 +184,20 @@ constexpr int SWZ_BOX_K = 64;                        // K width of one 128-byte 
 // ring, hiding the launch's ramp-up and tail.
 // Wide sliced launches (WX: x rows beyond 32 KB, e.g. M = 8 at K = 4096) use 8 slots, a 64 KB x
 // table and buffers for M x tiles <= 128, so the batch streams W once.
+// WX is the wide configuration of either kind: for sliced launches the 64 KB x table, for whole-row
+// launches the 24 KB slots of long octet rows; both have 8 slots.
 template <bool SL, bool HF = false, bool WX = false>
 struct SCfg {
     static_assert(!(SL && HF), "half-SM launches are whole-row launches");
-    static_assert(!WX || SL, "the wide x table is for sliced launches");
-    static constexpr int STAGES = HF ? 6 : (SL ? (WX ? 8 : 11) : 12);
+    static_assert(!(WX && HF), "the wide configurations are full-SM launches");
+    static constexpr int STAGES = HF ? 6 : (WX ? 8 : (SL ? 11 : 12));
     static constexpr int THREADS = 32 * (1 + STAGES);
     static constexpr int MIN_BLOCKS = HF ? 2 : 1;
-    static constexpr uint32_t STAGE_BYTES = STREAM_ROW_BYTES;
+    static constexpr uint32_t STAGE_BYTES = (!SL && WX) ? STREAM_WIDE_ROW_BYTES : STREAM_ROW_BYTES;
     static constexpr int PROBS = SL ? 1 : GROUP_MAX;
-    static constexpr uint32_t X_BYTES = HF ? STREAM_X_HALF_BYTES : (WX ? STREAM_X_WIDE_BYTES : STREAM_X_BYTES);
-    static constexpr int BUF_FL = 16 * (WX ? STREAM_MAX_XTILES_WIDE : STREAM_MAX_XTILES);   // floats per buffer
+    static constexpr uint32_t X_BYTES =
+        HF ? STREAM_X_HALF_BYTES : ((SL && WX) ? STREAM_X_WIDE_BYTES : STREAM_X_BYTES);
+    static constexpr int BUF_FL = 16 * ((SL && WX) ? STREAM_MAX_XTILES_WIDE : STREAM_MAX_XTILES);   // floats per buffer
     static constexpr uint32_t X_OFFSET = STAGES * STAGE_BYTES;
     static constexpr uint32_t META_OFFSET = X_OFFSET + X_BYTES;
     static constexpr uint32_t BAR_OFFSET = META_OFFSET + STAGES * sizeof(Meta);
@@ -208,6 +211,10 @@ struct SCfg {
 static_assert(SCfg<false>::SMEM_BYTES <= 232448 && SCfg<true>::SMEM_BYTES <= 232448 &&
               SCfg<true, false, true>::SMEM_BYTES <= 232448, "shared memory");
 static_assert(SCfg<true, false, true>::BAR_OFFSET % 8 == 0, "barrier alignment");
+static_assert(SCfg<false, false, true>::SMEM_BYTES <= 232448 && SCfg<false, false, true>::BAR_OFFSET % 8 == 0 &&
+                  SCfg<false, false, true>::PROB_OFFSET % 8 == 0 && STREAM_WIDE_ROW_BYTES % 16 == 0 &&
+                  STREAM_OCTET_WIDE_MAX_K * 2 <= STREAM_WIDE_ROW_BYTES && STREAM_OCTET_WIDE_MAX_K * 2 <= STREAM_X_BYTES,
+              "wide-slot whole-row configuration");
 // two half-SM CTAs (each with the 1 KB the hardware reserves per CTA) in the SM's 228 KB
 static_assert(2 * (SCfg<false, true>::SMEM_BYTES + 1024) <= 233472, "two half-SM CTAs per SM");
 static_assert(SCfg<false>::STAGES <= 32 && SCfg<true>::STAGES <= 32, "one producer lane per slot");
@@ -376,10 +383,10 @@ __device__ __forceinline__ void produce_sliced(const Group &g, const Problem *pr
 // together with a non-blocking test, so no lane's wait holds up another lane's copy. A unit is one
 // bulk copy of its rows. After an abort or a wait that ran out, each lane waits (bounded) for its
 // own copy in flight. (Sliced launches use produce_sliced.)
-template <bool HF>
+template <bool HF, bool WX>
 __device__ __forceinline__ void produce(const Group &g, const Problem *prob, uint8_t *smem, Meta *meta, uint32_t full0,
                                         uint32_t empty0, volatile int *abort_flag, int lane) {
-    using C = SCfg<false, HF>;
+    using C = SCfg<false, HF, WX>;
     const int count = g.count, units = g.units;
     const bool mine = lane < C::STAGES;
     const int slot = mine ? lane : 0;
@@ -921,7 +928,7 @@ __global__ void __launch_bounds__(SCfg<SL, HF, WX>::THREADS, SCfg<SL, HF, WX>::M
         __syncwarp();
         asm volatile("bar.arrive 2, %0;" ::"r"(C::THREADS) : "memory");
         if constexpr (SL) produce_sliced<HF, WX>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
-        else produce<HF>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
+        else produce<HF, WX>(g, prob, smem, meta, full0, empty0, abort_flag, lane);
         return;
     }
     asm volatile("bar.sync 2, %0;" ::"r"(C::THREADS) : "memory");   // barriers and problem table ready
@@ -1016,6 +1023,9 @@ cudaError_t stream_attr() {
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(gemv_stream_kernel<false, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)SCfg<false, true>::SMEM_BYTES);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemv_stream_kernel<false, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)SCfg<false, false, true>::SMEM_BYTES);
     if (e == cudaSuccess && dev >= 0 && dev < 64) done[dev] = true;
     return e;
 }
@@ -1049,12 +1059,18 @@ unsigned direct_grid(int M, int N, int sm_count) {
 }
 
 // Long-K whole-row (octet) units: 2048 < K <= 8192 with the row in one slot, M <= 4, and the M x rows
-// within the 32 KB x table.
+// within the 32 KB x table; or, at M = 1, rows up to K = 12288 in the wide slots.
 bool octet(int M, int K, long long ldw) {
     const long long k8 = ((long long)K + 7) & ~7ll;
-    return k8 > STREAM_WHOLE_K && k8 <= STREAM_OCTET_MAX_K && ldw * 2 <= (long long)STREAM_ROW_BYTES && M >= 1 &&
-           M <= STREAM_OCTET_MAX_M && (long long)M * k8 * 2 <= STREAM_X_BYTES;
+    if (k8 <= STREAM_WHOLE_K) return false;
+    if (k8 <= STREAM_OCTET_MAX_K && ldw * 2 <= (long long)STREAM_ROW_BYTES && M >= 1 && M <= STREAM_OCTET_MAX_M &&
+        (long long)M * k8 * 2 <= STREAM_X_BYTES)
+        return true;
+    return M == 1 && k8 <= STREAM_OCTET_WIDE_MAX_K && ldw * 2 <= (long long)STREAM_WIDE_ROW_BYTES;
 }
+
+// Rows longer than a 16 KB slot (octet units of the wide-slot configuration).
+bool wide_rows(long long ldw) { return ldw * 2 > (long long)STREAM_ROW_BYTES; }
 
 // Whole-row problems: rows per unit spread the group's weight bytes over about two units per SM, one
 // slot at most. Octet problems: one or two whole rows per unit. Other long-K problems (or rows wider
@@ -1202,6 +1218,7 @@ static long long rows_that_fit(int M, int N, int K, long long ldw) {
 int stream_stages(int M, int N, int K, long long ldw) {
     if (!stream_launches(M, N, K, ldw)) return 0;
     if (sliced(M, K, ldw)) return wide_x(M, K) ? SCfg<true, false, true>::STAGES : SCfg<true>::STAGES;
+    if (wide_rows(ldw)) return SCfg<false, false, true>::STAGES;
     const long long xelems = (long long)M * (((long long)K + 7) & ~7ll);
     return half_sm(false, xelems) ? SCfg<false, true>::STAGES : SCfg<false>::STAGES;
 }
@@ -1278,7 +1295,9 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
         }
         long long wbytes = 0;
         for (int i = 0; i < g.count; ++i) wbytes += (long long)g.prob[i].N * g.prob[i].ldw * 2;
-        const bool hf = half_sm(sl, xused);
+        bool wr = false;                         // octet rows longer than a 16 KB slot: wide slots
+        for (int i = 0; i < g.count; ++i) wr = wr || (!sl && wide_rows(g.prob[i].ldw));
+        const bool hf = half_sm(sl, xused) && !wr;
         const unsigned grid = stream_grid(hf, wbytes, g.units, sm_count);
         // Two half-SM CTAs per SM keep ~28 MB of weights in flight across the GPU, and loads queue
         // behind them: the x rows the consumers need first would wait ~2-4 us. In those launches
@@ -1290,10 +1309,12 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(grid);
         const bool wx = sl && wide_x(g.M, g.prob[0].K);
-        cfg.blockDim = dim3(sl ? (wx ? SCfg<true, false, true>::THREADS : SCfg<true>::THREADS)
-                               : (hf ? SCfg<false, true>::THREADS : SCfg<false>::THREADS));
-        cfg.dynamicSmemBytes = sl ? (wx ? SCfg<true, false, true>::SMEM_BYTES : SCfg<true>::SMEM_BYTES)
-                                  : (hf ? SCfg<false, true>::SMEM_BYTES : SCfg<false>::SMEM_BYTES);
+        cfg.blockDim = dim3(sl   ? (wx ? SCfg<true, false, true>::THREADS : SCfg<true>::THREADS)
+                            : wr ? SCfg<false, false, true>::THREADS
+                                 : (hf ? SCfg<false, true>::THREADS : SCfg<false>::THREADS));
+        cfg.dynamicSmemBytes = sl   ? (wx ? SCfg<true, false, true>::SMEM_BYTES : SCfg<true>::SMEM_BYTES)
+                               : wr ? SCfg<false, false, true>::SMEM_BYTES
+                                    : (hf ? SCfg<false, true>::SMEM_BYTES : SCfg<false>::SMEM_BYTES);
         cfg.stream = stream;
         // Early start of the next kernel: always for half-SM launches (half_sm); full-SM launches
         // (whose next CTAs cannot become resident before this launch's exit) allow it where the fixed
@@ -1306,6 +1327,7 @@ cudaError_t launch_group(Group &all, cudaStream_t stream, int sm_count, unsigned
         cfg.numAttrs = 1;
         const cudaError_t le0 = sl   ? (wx ? cudaLaunchKernelEx(&cfg, gemv_stream_kernel<true, false, true>, g)
                                            : cudaLaunchKernelEx(&cfg, gemv_stream_kernel<true, false, false>, g))
+                                : wr ? cudaLaunchKernelEx(&cfg, gemv_stream_kernel<false, false, true>, g)
                                 : hf ? cudaLaunchKernelEx(&cfg, gemv_stream_kernel<false, true, false>, g)
                                      : cudaLaunchKernelEx(&cfg, gemv_stream_kernel<false, false, false>, g);
         if (le0 != cudaSuccess) return le0;

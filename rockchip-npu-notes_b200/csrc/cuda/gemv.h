@@ -52,6 +52,11 @@ constexpr int STREAM_ROW_BYTES = 16384; // one copy slot
 constexpr int STREAM_WHOLE_K = 2048;
 constexpr int STREAM_OCTET_MAX_K = 8192;
 constexpr int STREAM_OCTET_MAX_M = 4;
+// Octet units of one row up to K = STREAM_OCTET_WIDE_MAX_K at M = 1 run in the wide-slot
+// configuration (8 slots of STREAM_WIDE_ROW_BYTES, one CTA per SM), so rows longer than a 16 KB
+// slot still stream whole instead of as K slices.
+constexpr int STREAM_WIDE_ROW_BYTES = 24576;
+constexpr int STREAM_OCTET_WIDE_MAX_K = 12288;
 constexpr int STREAM_SLICE = 512;       // 16 rows x 512 FP16 = one slot; a multiple of the 256-K tile
 constexpr int STREAM_MAX_XTILES = 64;   // sliced launches: M x (256-K tiles) per block buffer
 // Wide sliced launches (x rows beyond 32 KB, e.g. M = 8 at K = 4096): 8 ring slots, a 64 KB x table

@@ -213,11 +213,12 @@ def test_long_k_blocks_against_oracle(b2, gpu_fd, n, k):
     finishes most of its blocks itself and reuses its shared tile-sum buffers -- 16384 x 2560 gives
     about seven blocks per CTA, more than the four buffers -- and completes the blocks at the ends of
     its range across CTAs), while M = 4 (two passes) and M = 1 stream whole rows as octet units; all
-    give the same bits for the same x row. K > 8192 is sliced at every M. Tile-16 and FP32 results
-    within tolerance of the oracle / FP64, repeated launches identical (the block counters return
-    to zero)."""
+    give the same bits for the same x row. Up to K = 12288, M = 1 streams whole rows longer than a
+    16 KB slot as octet units in the 8-slot wide configuration (24 KB slots) and M = 4 is sliced,
+    again with the same bits; above, every M is sliced. Tile-16 and FP32 results within tolerance
+    of the oracle / FP64, repeated launches identical (the block counters return to zero)."""
     rng = np.random.default_rng(n + k)
-    ms = (8, 4, 1) if k <= 4096 else (1,)
+    ms = (8, 4, 1) if k <= 4096 else ((4, 1) if k <= 12288 else (1,))
     m = ms[0]
     x = rng.uniform(-1, 1, (m, k)).astype(np.float16)
     w = rng.uniform(-1 / np.sqrt(k), 1 / np.sqrt(k), (n, k)).astype(np.float16)
@@ -226,7 +227,8 @@ def test_long_k_blocks_against_oracle(b2, gpu_fd, n, k):
     for acc in (b2.ACC_TILE16, b2.ACC_FP32):
         op = b2.Linear(gpu_fd, 1, k, n, w, b, post=b2.CO_LINEAR_NONE, acc=acc, compat=False)
         info = op.info()
-        assert info.kernel == 1 and info.stages == (6 if k <= 4096 else 11)   # M=1: octet (half-SM) / sliced
+        # M=1: octet (half-SM) / octet in wide slots / sliced
+        assert info.kernel == 1 and info.stages == (6 if k <= 4096 else (8 if k <= 12288 else 11))
         ldy = r8(n)
         ys = [torch.zeros((m, ldy), dtype=torch.float16, device="cuda") for _ in range(3)]
         others = {mm: torch.zeros((mm, ldy), dtype=torch.float16, device="cuda") for mm in ms[1:]}
