@@ -47,13 +47,14 @@ def bits(t, cols):
     return t[:, :cols].cpu().numpy().view(np.uint16)
 
 
-@pytest.mark.parametrize("k", [1, 17, 576, 1000, 1536, 2048, 2056, 3000, 4096, 6000, 8192])
+@pytest.mark.parametrize("k", [1, 17, 576, 1000, 1536, 2048, 2056, 3000, 4096, 6000, 8192, 8200, 12288])
 def test_small_m_rows_are_batch_independent_and_within_tolerance(b2, gpu_fd, k):
     """Rows of M=1, 2, 3, 4 and 8 runs agree bit for bit (each x row's result does not depend on the
     rest of the batch, nor on the unit kind that serves it: above K = 2048, M <= 4 runs long-K
     whole-row (octet) units when the x rows fit 32 KB -- two W rows per unit up to K = 4096, one
     above -- and the other batches 16-row K slices; M=8 at K=4096 is one wide sliced launch with a
-    64 KB x table, at K=8192 two launches of 4 rows), in both accumulation modes, with and without
+    64 KB x table, at K=8192 two launches of 4 rows; above K = 8192, M = 1 runs one-row octet units
+    in 24 KB slots and the other batches slices), in both accumulation modes, with and without
     bias and HardSigmoid; all rows within tolerance. N is odd, so a two-row unit ends with one row."""
     n = 301
     x, w, b = uniform_case(8, n, k, 7000 + k)
@@ -65,8 +66,8 @@ def test_small_m_rows_are_batch_independent_and_within_tolerance(b2, gpu_fd, k):
                 op = b2.Linear(gpu_fd, 1, k, n, w, bias, post=post, mode=b2.CO_CHAIN, acc=acc, compat=False)
                 info = op.info()
                 # M=1: half-SM ring while the x row fits its 12 KB table (whole-row and long-K octet
-                # units alike); K = 8192 (16 KB) runs full-SM CTAs with 12 slots
-                assert info.kernel == 1 and info.stages == (12 if k > 6144 else 6)
+                # units alike); K = 8192 (16 KB) runs full-SM CTAs with 12 slots; longer rows 8 wide slots
+                assert info.kernel == 1 and info.stages == (6 if k <= 6144 else (12 if k <= 8192 else 8))
                 ys = {m: torch.zeros((m, ldy), dtype=torch.float16, device="cuda") for m in (1, 2, 3, 4, 8)}
                 torch.cuda.synchronize()
                 for m, y in ys.items():
